@@ -25,3 +25,11 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def cuda_ctx():
+    from tysor_b200.runtime import CudaContext
+    ctx = CudaContext(0)
+    yield ctx
+    ctx.close()

@@ -1,0 +1,144 @@
+"""tcgen05 matmul through the C ABI against the oracle's sequential f32
+matmul (runtime/tensor.rs:163-194).
+
+Tolerances (Frobenius-relative): strict 3xTF32 1e-5, fast 1xTF32 2e-3;
+the CUDA-core path (exact mode, and shapes that break TMA alignment) must be
+bit-identical to the oracle."""
+import numpy as np
+import pytest
+
+import local as L
+
+pytestmark = pytest.mark.gpu
+
+
+def frob(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def oracle_mm(a, b):
+    m, k = a.shape
+    n = b.shape[1]
+    t = L.matmul(L.Tensor([m, k], np.ascontiguousarray(a, np.float32).reshape(-1)),
+                 L.Tensor([k, n], np.ascontiguousarray(b, np.float32).reshape(-1)))
+    return t.data.reshape(m, n)
+
+
+def run_ex(ctx, a_stored, ta, b_stored, tb, m, n, k, batch=1, bias=None, alpha=1.0, acc=None, relu=False):
+    from tysor_b200 import native
+    from tysor_b200.runtime import DeviceBuffer
+    lib = native.lib()
+    A = DeviceBuffer.from_array(ctx, a_stored)
+    B = DeviceBuffer.from_array(ctx, b_stored)
+    C = DeviceBuffer.from_array(ctx, acc) if acc is not None else DeviceBuffer.zeros(ctx, batch * m * n)
+    Bi = DeviceBuffer.from_array(ctx, bias) if bias is not None else None
+    lda = a_stored.shape[-1]
+    ldb = b_stored.shape[-1]
+    sa = a_stored.shape[-2] * lda if batch > 1 else 0
+    sb = b_stored.shape[-2] * ldb if batch > 1 else 0
+    ok = lib.tysor_cuda_dispatch_matmul_ex(ctx.handle, batch, m, n, k, A.handle, ta, lda, sa, B.handle, tb, ldb, sb,
+                                           C.handle, n, m * n if batch > 1 else 0,
+                                           Bi.handle if Bi else None, alpha, acc is not None, relu)
+    native.check(ok, "matmul_ex")
+    out = C.read().reshape(batch, m, n) if batch > 1 else C.read().reshape(m, n)
+    for buf in (A, B, C, Bi):
+        if buf:
+            buf.free()
+    return out
+
+
+SHAPES = [(128, 256, 64), (300, 200, 72), (257, 130, 36), (64, 48, 16), (1000, 1000, 1000)]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+def test_strict_matmul_layouts(cuda_ctx, m, n, k, ta, tb):
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    want = oracle_mm(a, b)
+    got = run_ex(cuda_ctx, np.ascontiguousarray(a.T) if ta else a, ta,
+                 np.ascontiguousarray(b.T) if tb else b, tb, m, n, k)
+    assert frob(got, want) < 1e-5
+
+
+def test_matmul_relu_2048_strict(cuda_ctx):
+    """The matmul+relu program at x, w fp32 [2048, 2048], U[-1, 1]."""
+    from tysor_b200.runtime import DeviceBuffer
+    from tysor_b200 import native
+    rng0, rng1 = np.random.default_rng(0), np.random.default_rng(1)
+    x = rng0.uniform(-1, 1, (2048, 2048)).astype(np.float32)
+    w = rng1.uniform(-1, 1, (2048, 2048)).astype(np.float32)
+    L.set_threads(8)
+    want = np.maximum(oracle_mm(x, w), 0)
+    got = run_ex(cuda_ctx, x, False, w, False, 2048, 2048, 2048, relu=True)
+    assert frob(got, want) < 1e-5
+
+
+def test_fast_mode_tolerance(cuda_ctx):
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (512, 1024)).astype(np.float32)
+    b = rng.uniform(-1, 1, (1024, 384)).astype(np.float32)
+    want = oracle_mm(a, b)
+    cuda_ctx.set_matmul_mode("fast")
+    try:
+        got = run_ex(cuda_ctx, a, False, b, False, 512, 384, 1024)
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    err = frob(got, want)
+    assert 1e-7 < err < 2e-3
+
+
+def test_exact_mode_is_bit_exact(cuda_ctx):
+    rng = np.random.default_rng(6)
+    a = rng.uniform(-1, 1, (70, 50)).astype(np.float32)
+    b = rng.uniform(-1, 1, (50, 33)).astype(np.float32)
+    cuda_ctx.set_matmul_mode("exact")
+    try:
+        got = run_ex(cuda_ctx, a, False, b, False, 70, 33, 50)
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    np.testing.assert_array_equal(got, oracle_mm(a, b))
+
+
+def test_unaligned_shapes_use_exact_path(cuda_ctx):
+    rng = np.random.default_rng(7)
+    a = rng.uniform(-1, 1, (5, 3)).astype(np.float32)
+    b = rng.uniform(-1, 1, (3, 7)).astype(np.float32)
+    got = run_ex(cuda_ctx, a, False, b, False, 5, 7, 3)
+    np.testing.assert_array_equal(got, oracle_mm(a, b))
+
+
+def test_batched_and_epilogue(cuda_ctx):
+    rng = np.random.default_rng(8)
+    bt, m, n, k = 3, 130, 96, 64
+    a = rng.uniform(-1, 1, (bt, m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (bt, k, n)).astype(np.float32)
+    c0 = rng.uniform(-1, 1, (bt, m, n)).astype(np.float32)
+    got = run_ex(cuda_ctx, a, False, b, False, m, n, k, batch=bt, alpha=0.5, acc=c0)
+    for i in range(bt):
+        prod = oracle_mm(a[i], b[i])
+        want = c0[i] + prod * np.float32(0.5)
+        assert frob(got[i], want) < 1e-5
+
+
+def test_bias_epilogue(cuda_ctx):
+    rng = np.random.default_rng(9)
+    a = rng.uniform(-1, 1, (200, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (96, 300)).astype(np.float32)
+    bias = rng.uniform(-1, 1, 300).astype(np.float32)
+    got = run_ex(cuda_ctx, a, False, b, False, 200, 300, 96, bias=bias)
+    assert frob(got, oracle_mm(a, b) + bias) < 1e-5
+
+
+def test_dispatch_matmul_metal_signature(cuda_ctx):
+    """tysor_cuda_dispatch_matmul has the Metal bridge's argument order."""
+    from tysor_b200 import native
+    from tysor_b200.runtime import DeviceBuffer
+    x = L.synthetic([2, 3]).data.reshape(2, 3)
+    w = L.synthetic([3, 4]).data.reshape(3, 4)
+    X, W, O = DeviceBuffer.from_array(cuda_ctx, x), DeviceBuffer.from_array(cuda_ctx, w), DeviceBuffer.zeros(cuda_ctx, 8)
+    native.check(native.lib().tysor_cuda_dispatch_matmul(cuda_ctx.handle, X.handle, W.handle, O.handle, 2, 4, 3))
+    np.testing.assert_array_equal(O.read().reshape(2, 4), oracle_mm(x, w))

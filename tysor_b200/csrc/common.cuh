@@ -1,0 +1,100 @@
+// Shared definitions for the tysor CUDA backend (sm_100a).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <stdexcept>
+#include <string>
+
+namespace tysor {
+
+// Kernel launches enqueued by this library (every launcher adds to it).
+extern std::atomic<int64_t> g_launches;
+
+// Error codes written by kernels into the context's device error word.  A
+// kernel never traps: it records the first problem it sees and returns, and
+// the host turns the word into an error message at the next check.
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrIndexRange = 1,      // embedding / label index outside [0, n)
+  kErrBarrierTimeout = 2,  // an mbarrier wait ran past its time limit
+  kErrTmemAlloc = 3,
+};
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define TYSOR_CUDA(call) ::tysor::check_cuda((call), #call)
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Grid size for a grid-stride elementwise loop: a few waves of the 148 SMs.
+inline int elementwise_blocks(int64_t n, int threads) {
+  int64_t want = ceil_div(n, threads);
+  int64_t cap = 148 * 16;
+  if (want > cap) want = cap;
+  return (int)(want < 1 ? 1 : want);
+}
+
+// ---------------------------------------------------------------------------
+// GEMM interface (gemm.cu).
+// C[b] = alpha * op(A[b]) . op(B[b])  (+ bias) (relu) (+ C_old when accumulate)
+// op(A) is [M, K]: A stored [M, K] row-major (trans_a = false) or [K, M]
+// (trans_a = true).  op(B) is [K, N]: B stored [K, N] (trans_b = false) or
+// [N, K] (trans_b = true).  All fp32.
+// ---------------------------------------------------------------------------
+struct GemmOperand {
+  const float* ptr;
+  bool trans;
+  int64_t ld;            // row pitch of the stored matrix, in elements
+  int64_t batch_stride;  // elements between batch items (0 for one item)
+};
+
+struct GemmOutput {
+  float* ptr;
+  int64_t ld;
+  int64_t batch_stride;
+};
+
+struct GemmEpilogue {
+  const float* bias;  // [N] or null
+  float alpha;        // multiplies the product (1.0f for plain matmul)
+  int accumulate;     // 1: C = C_old + result
+  int relu;           // 1: result = max(result, 0)
+};
+
+enum GemmMode : int {
+  kGemmStrict = 0,  // 3xTF32 split: fp32-level accuracy
+  kGemmFast = 1,    // 1xTF32
+  kGemmExact = 2,   // CUDA-core fp32, products and sums in k order (bit-exact)
+};
+
+// Scratch the strict-mode GEMM needs: one "lo" copy of each operand.
+struct GemmScratch {
+  float* a_lo;
+  float* b_lo;
+  int64_t a_elems;
+  int64_t b_elems;
+};
+
+// Returns the number of elements of scratch each operand needs in strict
+// mode (0 when the call runs on the CUDA-core path).
+void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
+                       const GemmOperand& B, int mode, int64_t* a_elems, int64_t* b_elems);
+
+// Launches the GEMM on `stream`.  Throws CudaError on a launch problem.
+// Picks the tcgen05 path when every TMA alignment rule holds, else the
+// CUDA-core path.  Returns 1 if the tensor-core path ran, 0 otherwise.
+int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
+                const GemmOperand& B, const GemmOutput& C, const GemmEpilogue& ep, int mode,
+                const GemmScratch& scratch, int* d_err, cudaStream_t stream);
+
+}  // namespace tysor

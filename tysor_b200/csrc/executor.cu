@@ -1,0 +1,1483 @@
+// Device-resident graph executor (tysor_cuda_graph_* in include/tysor_cuda.h).
+//
+// One executor object holds one lowered graph.  Planning walks the graph
+// once on the host, exactly in the order of the reference interpreters
+// (runtime/graph_executor.rs:249-356 for --run, training/backward.rs:145-380
+// for --backward, training/executor.rs:252-816 for --train): it evaluates
+// constants and layer constructors, infers every tensor shape, reports the
+// reference's errors, and records a list of device steps.  All tensors live
+// in one device arena laid out after planning; reshape and flatten_heads are
+// views.  Executing a plan only enqueues kernels on the context stream; a
+// train step (forward, backward, optional gradient all-reduce, SGD) is
+// captured once as a CUDA graph and replayed.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <deque>
+#include <functional>
+#include <map>
+#include <memory>
+#include <set>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "../../include/tysor_cuda.h"
+#include "context.cuh"
+#include "ops.cuh"
+
+namespace tysor {
+namespace {
+
+enum VKind { kVTensor, kVInt, kVFloat, kVBool, kVCallable };
+enum NKind { kNConst, kNBinary, kNPrimitive, kNCall, kNCtor, kNApply };
+enum Mode { kModeRun = 0, kModeBackward = 1, kModeTrain = 2 };
+
+struct GValue {
+  int id = 0;
+  VKind kind = kVTensor;
+  bool is_param = false;
+  std::string name;
+};
+
+struct GNode {
+  NKind kind = kNConst;
+  int output = 0;
+  std::string op;
+  char binop = '+';
+  int ckind = 0;  // const: 0 int, 1 float, 2 bool
+  int64_t ival = 0;
+  double fval = 0;
+  std::vector<int> inputs;
+};
+
+// A region of the device arena.  Views point into their base.
+struct Slot {
+  size_t n = 0;
+  Slot* base = nullptr;
+  size_t offset = 0;
+  float* p = nullptr;
+};
+
+struct HVal {
+  enum T { None, Int, Float, Bool, Tensor, Linear, Embedding, Act, RmsNorm } t = None;
+  int64_t i = 0;
+  double f = 0;
+  bool b = false;
+  std::vector<int64_t> shape;
+  Slot* slot = nullptr;
+  // closures
+  int64_t in_features = -1, out_features = 0;
+  bool with_bias = true;
+  int64_t num = 0, dim = 0, hidden = 0;
+  std::string act;
+  double prob = 0, eps = 1e-5;
+  int ctor_id = -1;
+};
+
+struct Param {
+  std::vector<int64_t> shape;
+  Slot* value = nullptr;
+  Slot* grad = nullptr;
+  bool grad_written = false;
+  // initialiser: 0 linear weight, 1 linear bias, 2 embedding weight, 3 ones
+  int init = 0;
+};
+
+using StepFn = std::function<void(cudaStream_t)>;
+
+int64_t numel(const std::vector<int64_t>& s) {
+  int64_t n = 1;
+  for (auto d : s) n *= d;
+  return n;
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::ostringstream o;
+  o << "[";
+  for (size_t i = 0; i < s.size(); ++i) o << (i ? ", " : "") << s[i];
+  o << "]";
+  return o.str();
+}
+
+[[noreturn]] void fail(const std::string& m) { throw CudaError(m); }
+
+struct Executor {
+  Context* ctx = nullptr;
+  std::vector<GValue> values;
+  std::vector<GNode> nodes;
+  std::vector<int> outputs;
+  int objective = -1;
+  std::map<std::string, std::vector<int64_t>> shapes;
+  std::map<std::string, std::vector<float>> inputs;
+  std::map<std::string, std::vector<float>> param_init;
+
+  // plan
+  int mode = -1;
+  bool dirty = true;
+  std::deque<Slot> slots;
+  std::vector<HVal> hv;
+  std::vector<StepFn> setup;      // once per plan: constant weights, parameter init
+  std::vector<std::pair<std::string, StepFn>> upload;  // once per call: graph inputs
+  std::set<std::string> device_inputs;  // inputs last written by upload_input
+  std::vector<StepFn> forward;    // every step
+  std::vector<StepFn> backward;   // every step
+  std::vector<StepFn> update;     // every train step
+  std::map<int, Slot*> vgrad;
+  std::map<std::string, Param> params;
+  std::vector<std::string> param_order;
+  Slot* loss = nullptr;           // one float per step
+  Slot* grad_block = nullptr;     // all parameter gradients + loss, contiguous
+  size_t scratch_floats = 0;
+  Slot* scratch = nullptr;
+  void* arena = nullptr;
+  bool setup_done = false;
+  bool capture = true;
+  bool allreduce = false;
+  cudaGraphExec_t exec = nullptr;
+  int64_t last_launches = 0;
+
+  void run_uploads() {
+    for (auto& [name, fn] : upload)
+      if (!device_inputs.count(name)) fn(ctx->stream);
+  }
+
+  ~Executor() { release(); }
+
+  void release() {
+    if (exec) cudaGraphExecDestroy(exec);
+    exec = nullptr;
+    if (arena) cudaFree(arena);
+    arena = nullptr;
+    slots.clear();
+    hv.clear();
+    setup.clear();
+    upload.clear();
+    forward.clear();
+    backward.clear();
+    update.clear();
+    vgrad.clear();
+    params.clear();
+    param_order.clear();
+    loss = grad_block = scratch = nullptr;
+    scratch_floats = 0;
+    setup_done = false;
+  }
+
+  Slot* alloc(size_t n) {
+    slots.push_back(Slot{n, nullptr, 0, nullptr});
+    return &slots.back();
+  }
+  Slot* view(Slot* base, size_t offset, size_t n) {
+    while (base->base) {
+      offset += base->offset;
+      base = base->base;
+    }
+    slots.push_back(Slot{n, base, offset, nullptr});
+    return &slots.back();
+  }
+  void need_scratch(size_t floats) {
+    if (floats > scratch_floats) scratch_floats = floats;
+  }
+
+  // ---- parsing ------------------------------------------------------------
+  void parse(const char* text) {
+    std::istringstream in(text);
+    std::string line;
+    while (std::getline(in, line)) {
+      std::istringstream ls(line);
+      std::string tag;
+      if (!(ls >> tag)) continue;
+      if (tag == "graph") continue;
+      if (tag == "end") break;
+      if (tag == "value") {
+        GValue v;
+        std::string kind, name;
+        int param;
+        ls >> v.id >> kind >> param >> name;
+        if (kind == "tensor") v.kind = kVTensor;
+        else if (kind == "int") v.kind = kVInt;
+        else if (kind == "float") v.kind = kVFloat;
+        else if (kind == "bool") v.kind = kVBool;
+        else v.kind = kVCallable;
+        v.is_param = param != 0;
+        v.name = name == "-" ? "" : name;
+        if (v.id != (int)values.size()) fail("graph text: value ids must be dense and ordered");
+        values.push_back(v);
+      } else if (tag == "node") {
+        GNode n;
+        std::string kind;
+        ls >> kind >> n.output;
+        if (kind == "const") {
+          std::string ck;
+          ls >> ck;
+          if (ck == "int") {
+            n.ckind = 0;
+            ls >> n.ival;
+          } else if (ck == "float") {
+            n.ckind = 1;
+            std::string s;
+            ls >> s;
+            n.fval = strtod(s.c_str(), nullptr);
+          } else {
+            n.ckind = 2;
+            ls >> n.ival;
+          }
+          n.kind = kNConst;
+        } else if (kind == "binary") {
+          std::string op;
+          ls >> op;
+          n.binop = op[0];
+          n.kind = kNBinary;
+        } else if (kind == "apply") {
+          n.kind = kNApply;
+        } else {
+          ls >> n.op;
+          n.kind = kind == "primitive" ? kNPrimitive : kind == "call" ? kNCall : kNCtor;
+        }
+        int x;
+        while (ls >> x) n.inputs.push_back(x);
+        for (int i : n.inputs)
+          if (i < 0 || i >= (int)values.size()) fail("graph text: input id out of range");
+        if (n.output < 0 || n.output >= (int)values.size()) fail("graph text: output id out of range");
+        nodes.push_back(n);
+      } else if (tag == "output") {
+        int o;
+        ls >> o;
+        outputs.push_back(o);
+      } else if (tag == "objective") {
+        ls >> objective;
+      }
+    }
+    if (values.empty()) fail("graph text: no values");
+  }
+
+  // ---- helpers over planning values ----------------------------------------
+  const HVal& val(int id) const { return hv.at(id); }
+  const HVal& tensor(int id, const char* /*what*/) const {
+    const HVal& h = hv.at(id);
+    if (h.t != HVal::Tensor) fail("Graph executor expected tensor value");
+    return h;
+  }
+  static double number(const HVal& h) {
+    switch (h.t) {
+      case HVal::Int: return (double)h.i;
+      case HVal::Float: return h.f;
+      case HVal::Bool: return h.b ? 1.0 : 0.0;
+      default: fail("Graph executor expected scalar value");
+    }
+  }
+  static int64_t integer(const HVal& h) {
+    if (h.t != HVal::Int) fail("Graph executor expected integer value");
+    return h.i;
+  }
+  static bool boolean(const HVal& h) {
+    if (h.t != HVal::Bool) fail("Graph executor expected bool value");
+    return h.b;
+  }
+
+  HVal new_tensor(std::vector<int64_t> shape) {
+    HVal h;
+    h.t = HVal::Tensor;
+    h.shape = std::move(shape);
+    h.slot = alloc((size_t)numel(h.shape));
+    return h;
+  }
+
+  // ---- parameters ---------------------------------------------------------------
+  Param& ensure_param(const std::string& name, std::vector<int64_t> shape, int init) {
+    auto it = params.find(name);
+    if (it != params.end()) return it->second;
+    Param p;
+    p.shape = shape;
+    p.value = alloc((size_t)numel(shape));
+    p.init = init;
+    params[name] = p;
+    param_order.push_back(name);
+    Param& ref = params[name];
+    Slot* s = ref.value;
+    const int64_t n = numel(shape);
+    auto explicit_it = param_init.find(name);
+    if (explicit_it != param_init.end()) {
+      if ((int64_t)explicit_it->second.size() != n)
+        fail("initial value of '" + name + "' has " + std::to_string(explicit_it->second.size()) +
+             " values, expected " + std::to_string(n));
+      const std::vector<float>* host = &explicit_it->second;
+      setup.push_back([s, host, n](cudaStream_t st) {
+        TYSOR_CUDA(cudaMemcpyAsync(s->p, host->data(), sizeof(float) * n, cudaMemcpyHostToDevice, st));
+      });
+    } else {
+      setup.push_back([s, n, init](cudaStream_t st) { fill_pattern(s->p, n, init, st); });
+    }
+    return ref;
+  }
+
+  static void fill_pattern(float* p, int64_t n, int init, cudaStream_t st) {
+    switch (init) {
+      case 0: launch_pattern(p, n, 13, 1.0f, 16.0f, st); break;   // layers.rs:39-51
+      case 1: launch_pattern(p, n, 7, 1.0f, 32.0f, st); break;    // layers.rs:53-63
+      case 2: launch_pattern(p, n, 17, 1.0f, 8.0f, st); break;    // layers.rs:65-75
+      case 3: launch_fill(p, n, 1.0f, st); break;                 // RMSNorm gain
+      case 4: launch_pattern(p, n, 11, -5.0f, 16.0f, st); break;  // backward.rs:225-235
+      default: launch_pattern(p, n, 17, 1.0f, 8.0f, st); break;   // tensor.rs:24-34
+    }
+  }
+
+  // A constant (non-trainable) pattern tensor for --run / --backward.
+  Slot* const_pattern(std::vector<int64_t> shape, int init) {
+    Slot* s = alloc((size_t)numel(shape));
+    const int64_t n = numel(shape);
+    setup.push_back([s, n, init](cudaStream_t st) { fill_pattern(s->p, n, init, st); });
+    return s;
+  }
+
+  // ---- GEMM step --------------------------------------------------------------
+  void gemm_step(std::vector<StepFn>& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
+                 bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
+                 Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu) {
+    // Scratch for the split operands (strict mode): bound by the operand spans.
+    const int64_t span_a = (batch - 1) * sa + (ta ? (K - 1) * lda + M : (M - 1) * lda + K);
+    const int64_t span_b = (batch - 1) * sb + (tb ? (N - 1) * ldb + K : (K - 1) * ldb + N);
+    need_scratch((size_t)(span_a + span_b + 128));
+    Context* cx = ctx;
+    Slot** scr = &scratch;
+    out.push_back([=](cudaStream_t st) {
+      GemmOperand A{a->p, ta, lda, sa};
+      GemmOperand B{b->p, tb, ldb, sb};
+      GemmOutput O{c->p, ldc, sc};
+      GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0};
+      GemmScratch s{nullptr, nullptr, 0, 0};
+      int64_t na = 0, nb = 0;
+      gemm_scratch_need(batch, M, N, K, A, B, cx->matmul_mode, &na, &nb);
+      if (na + nb > 0) {
+        const int64_t pad = (na + 63) & ~(int64_t)63;
+        s.a_lo = (*scr)->p;
+        s.b_lo = (*scr)->p + pad;
+        s.a_elems = na;
+        s.b_elems = nb;
+      }
+      gemm_launch(batch, M, N, K, A, B, O, ep, cx->matmul_mode, s, cx->d_err, st);
+    });
+  }
+
+  // C = lhs . rhs for rank 2, or batched over equal leading dims.
+  HVal plan_matmul(const HVal& l, const HVal& r, std::vector<StepFn>& out) {
+    if (l.shape.size() < 2 || r.shape.size() < 2) fail("matmul currently requires rank-2 tensors");
+    if (l.shape.size() != r.shape.size()) fail("matmul currently requires rank-2 tensors");
+    for (size_t i = 0; i + 2 < l.shape.size(); ++i)
+      if (l.shape[i] != r.shape[i]) fail("matmul currently requires rank-2 tensors");
+    const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back();
+    const int64_t k2 = r.shape[r.shape.size() - 2], n = r.shape.back();
+    if (k != k2)
+      fail("matmul inner dimension mismatch: lhs=" + shape_str(l.shape) + " rhs=" + shape_str(r.shape));
+    std::vector<int64_t> os(l.shape.begin(), l.shape.end() - 2);
+    const int batch = (int)numel(os);
+    os.push_back(m);
+    os.push_back(n);
+    HVal o = new_tensor(os);
+    gemm_step(out, batch, m, n, k, l.slot, false, k, m * k, r.slot, false, n, k * n, o.slot, n, m * n,
+              nullptr, 1.0f, false, false);
+    return o;
+  }
+
+  // ---- forward planning --------------------------------------------------------
+  void plan_forward() {
+    hv.assign(values.size(), HVal());
+    for (const GValue& v : values) {
+      if (!v.is_param) continue;
+      if (v.kind != kVTensor) fail("Graph executor currently supports tensor parameters only");
+      auto it = shapes.find(v.name);
+      std::vector<int64_t> shape;
+      auto in_it = inputs.find(v.name);
+      if (it != shapes.end()) {
+        shape = it->second;
+      } else if (in_it != inputs.end()) {
+        shape = {(int64_t)in_it->second.size()};
+      } else {
+        fail("Missing --shape for tensor parameter '" + v.name + "'");
+      }
+      HVal h = new_tensor(shape);
+      Slot* s = h.slot;
+      const int64_t n = numel(shape);
+      if (in_it != inputs.end()) {
+        if ((int64_t)in_it->second.size() != n)
+          fail("input '" + v.name + "' has " + std::to_string(in_it->second.size()) +
+               " values, shape " + shape_str(shape) + " needs " + std::to_string(n));
+        const std::vector<float>* host = &in_it->second;
+        upload.push_back({v.name, [s, host, n](cudaStream_t st) {
+                            TYSOR_CUDA(cudaMemcpyAsync(s->p, host->data(), sizeof(float) * n,
+                                                       cudaMemcpyHostToDevice, st));
+                          }});
+      } else {
+        setup.push_back([s, n](cudaStream_t st) { fill_pattern(s->p, n, 5, st); });
+      }
+      hv[v.id] = h;
+    }
+    for (const GNode& node : nodes) hv[node.output] = plan_node(node);
+  }
+
+  HVal plan_node(const GNode& node) {
+    switch (node.kind) {
+      case kNConst: {
+        HVal h;
+        if (node.ckind == 0) {
+          h.t = HVal::Int;
+          h.i = node.ival;
+        } else if (node.ckind == 1) {
+          h.t = HVal::Float;
+          h.f = node.fval;
+        } else {
+          h.t = HVal::Bool;
+          h.b = node.ival != 0;
+        }
+        return h;
+      }
+      case kNBinary: return plan_binary(node);
+      case kNPrimitive: return plan_primitive(node);
+      case kNCall: return plan_call(node);
+      case kNCtor: return plan_ctor(node);
+      case kNApply: return plan_apply(node);
+    }
+    fail("unknown node kind");
+  }
+
+  static int binop_code(char c) {
+    switch (c) {
+      case '+': return kAdd;
+      case '-': return kSub;
+      case '*': return kMul;
+      case '/': return kDiv;
+    }
+    fail("unsupported tensor binary op");
+  }
+
+  HVal plan_binary(const GNode& node) {
+    const HVal& l = val(node.inputs[0]);
+    const HVal& r = val(node.inputs[1]);
+    const int op = binop_code(node.binop);
+    if (l.t == HVal::Tensor && r.t == HVal::Tensor) {
+      if (l.shape != r.shape) fail("tensor shape mismatch");
+      HVal o = new_tensor(l.shape);
+      Slot *a = l.slot, *b = r.slot, *c = o.slot;
+      const int64_t n = numel(l.shape);
+      forward.push_back([=](cudaStream_t st) { launch_binary_tt(op, a->p, b->p, c->p, n, st); });
+      return o;
+    }
+    if (l.t == HVal::Tensor) {
+      const float s = (float)number(r);
+      HVal o = new_tensor(l.shape);
+      Slot *a = l.slot, *c = o.slot;
+      const int64_t n = numel(l.shape);
+      forward.push_back([=](cudaStream_t st) { launch_binary_ts(op, a->p, s, c->p, n, st); });
+      return o;
+    }
+    if (r.t == HVal::Tensor) {
+      const float s = (float)number(l);
+      HVal o = new_tensor(r.shape);
+      Slot *b = r.slot, *c = o.slot;
+      const int64_t n = numel(r.shape);
+      forward.push_back([=](cudaStream_t st) { launch_binary_st(op, s, b->p, c->p, n, st); });
+      return o;
+    }
+    // scalar-scalar in f64 (graph_executor.rs:299-305)
+    const double a = number(l), b = number(r);
+    HVal h;
+    h.t = HVal::Float;
+    h.f = node.binop == '+' ? a + b : node.binop == '-' ? a - b : node.binop == '*' ? a * b : a / b;
+    return h;
+  }
+
+  HVal plan_primitive(const GNode& node) {
+    if (node.op == "matmul") {
+      const HVal& l = val(node.inputs.at(0));
+      const HVal& r = val(node.inputs.at(1));
+      if (l.t != HVal::Tensor || r.t != HVal::Tensor) fail("Graph executor expected tensor value");
+      return plan_matmul(l, r, forward);
+    }
+    if (node.op == "relu") {
+      const HVal& x = tensor(node.inputs.at(0), "relu");
+      HVal o = new_tensor(x.shape);
+      Slot *a = x.slot, *c = o.slot;
+      const int64_t n = numel(x.shape);
+      forward.push_back([=](cudaStream_t st) { launch_unary(kUnaryRelu, a->p, c->p, n, 0.0f, st); });
+      return o;
+    }
+    if (node.op == "scale") {
+      const HVal& x = tensor(node.inputs.at(0), "scale");
+      const float s = (float)number(val(node.inputs.at(1)));
+      HVal o = new_tensor(x.shape);
+      Slot *a = x.slot, *c = o.slot;
+      const int64_t n = numel(x.shape);
+      forward.push_back([=](cudaStream_t st) { launch_binary_ts(kMul, a->p, s, c->p, n, st); });
+      return o;
+    }
+    fail("Unsupported primitive graph op '" + node.op + "'");
+  }
+
+  static void rope_dims(const std::vector<int64_t>& s, int64_t hd, int64_t* outer, int64_t* seq) {
+    if (s.empty() || s.back() != hd) fail("rope head_dim mismatch");
+    if (hd % 2 != 0) fail("rope requires an even head_dim");
+    *seq = s.size() >= 2 ? s[s.size() - 2] : s[0];
+    *outer = numel(s) / (*seq * hd);
+  }
+
+  HVal plan_call(const GNode& node) {
+    const std::string& op = node.op;
+    if (op == "rms_norm") {
+      const HVal& x = tensor(node.inputs.at(0), "rms_norm");
+      const int64_t h = integer(val(node.inputs.at(1)));
+      if (x.shape.empty() || x.shape.back() != h)
+        fail("rms_norm hidden size mismatch: expected " + std::to_string(h) + ", got " + shape_str(x.shape));
+      HVal o = new_tensor(x.shape);
+      Slot *a = x.slot, *c = o.slot;
+      const int64_t rows = numel(x.shape) / h;
+      forward.push_back([=](cudaStream_t st) { launch_rms_norm(a->p, c->p, rows, h, st); });
+      return o;
+    }
+    if (op == "cross_entropy") {
+      const HVal& lg = tensor(node.inputs.at(0), "logits");
+      const HVal& tg = tensor(node.inputs.at(1), "target");
+      const int64_t w = lg.shape.empty() ? 1 : lg.shape.back();
+      const int64_t rows = numel(lg.shape) / (w > 0 ? w : 1);
+      HVal o = new_tensor({rows, 1});
+      Slot *a = lg.slot, *t = tg.slot, *c = o.slot;
+      if (lg.shape != tg.shape && numel(tg.shape) == rows) {
+        Context* cx = ctx;
+        forward.push_back([=](cudaStream_t st) {
+          launch_cross_entropy_labels(a->p, t->p, c->p, rows, w, cx->d_err, st);
+        });
+        return o;
+      }
+      if (lg.shape != tg.shape) fail("cross_entropy requires logits and target to have identical shapes");
+      forward.push_back([=](cudaStream_t st) { launch_cross_entropy(a->p, t->p, c->p, rows, w, st); });
+      return o;
+    }
+    if (op == "reshape") {
+      const HVal& x = tensor(node.inputs.at(0), "reshape");
+      std::vector<int64_t> s;
+      for (size_t i = 1; i < node.inputs.size(); ++i) s.push_back(integer(val(node.inputs[i])));
+      int64_t n = 1;
+      for (auto d : s) n *= d;
+      if (n != numel(x.shape) || s.empty()) fail("reshape requires matching element counts");
+      HVal o;
+      o.t = HVal::Tensor;
+      o.shape = s;
+      o.slot = view(x.slot, 0, (size_t)n);
+      return o;
+    }
+    if (op == "flatten_heads") {
+      const HVal& x = tensor(node.inputs.at(0), "flatten_heads");
+      HVal o;
+      o.t = HVal::Tensor;
+      o.shape = x.shape;
+      if (x.shape.size() >= 3) {
+        o.shape.assign(x.shape.begin(), x.shape.end() - 2);
+        o.shape.push_back(x.shape[x.shape.size() - 2] * x.shape.back());
+      }
+      o.slot = view(x.slot, 0, (size_t)numel(x.shape));
+      return o;
+    }
+    if (op == "repeat_kv") {
+      const HVal& x = tensor(node.inputs.at(0), "repeat_kv");
+      const int64_t rep = integer(val(node.inputs.at(1)));
+      if (rep <= 0) fail("repeat_kv repeats must be positive");
+      if (x.shape.size() < 2) fail("repeat_kv expects rank >= 2");
+      std::vector<int64_t> s = x.shape;
+      s[1] *= rep;
+      HVal o = new_tensor(s);
+      int64_t inner = 1;
+      for (size_t i = 2; i < x.shape.size(); ++i) inner *= x.shape[i];
+      const int64_t outer = x.shape[0], heads = x.shape[1];
+      Slot *a = x.slot, *c = o.slot;
+      forward.push_back([=](cudaStream_t st) { launch_repeat_kv(a->p, c->p, outer, heads, inner, rep, st); });
+      return o;
+    }
+    if (op == "causal_mask") {
+      const HVal& x = tensor(node.inputs.at(0), "causal_mask");
+      if (x.shape.size() < 2) fail("causal_mask expects rank >= 2");
+      const int64_t q = x.shape[x.shape.size() - 2], k = x.shape.back();
+      const int64_t outer = numel(x.shape) / (q * k > 0 ? q * k : 1);
+      HVal o = new_tensor(x.shape);
+      Slot *a = x.slot, *c = o.slot;
+      forward.push_back([=](cudaStream_t st) { launch_causal_mask(a->p, c->p, outer, q, k, st); });
+      return o;
+    }
+    if (op == "rope") {
+      const HVal& x = tensor(node.inputs.at(0), "rope");
+      const int64_t hd = integer(val(node.inputs.at(1)));
+      const double theta = number(val(node.inputs.at(2)));
+      int64_t outer, seq;
+      rope_dims(x.shape, hd, &outer, &seq);
+      HVal o = new_tensor(x.shape);
+      const float2* tab = ctx->rope_table(seq, hd / 2, theta);
+      Slot *a = x.slot, *c = o.slot;
+      forward.push_back([=](cudaStream_t st) { launch_rope(a->p, c->p, tab, outer, seq, hd / 2, st); });
+      return o;
+    }
+    if (op == "transpose") {
+      const HVal& x = tensor(node.inputs.at(0), "transpose");
+      int64_t a = integer(val(node.inputs.at(1))), b = integer(val(node.inputs.at(2)));
+      const int64_t rank = (int64_t)x.shape.size();
+      if (a < 0) a += rank;
+      if (b < 0) b += rank;
+      if (a < 0 || b < 0 || a >= rank || b >= rank || rank > 8) fail("transpose axis out of range");
+      if (a > b) std::swap(a, b);
+      std::vector<int64_t> s = x.shape;
+      std::swap(s[a], s[b]);
+      HVal o = new_tensor(s);
+      std::vector<int64_t> dims = x.shape;
+      Slot *src = x.slot, *dst = o.slot;
+      const int ia = (int)a, ib = (int)b;
+      forward.push_back([=](cudaStream_t st) {
+        launch_transpose(src->p, dst->p, dims.data(), (int)dims.size(), ia, ib, 0, st);
+      });
+      return o;
+    }
+    fail("Unsupported library graph call '" + op + "'");
+  }
+
+  HVal plan_ctor(const GNode& node) {
+    HVal h;
+    h.ctor_id = node.output;
+    const auto& in = node.inputs;
+    if (node.op == "linear") {
+      h.t = HVal::Linear;
+      if (in.size() == 1) {
+        h.out_features = integer(val(in[0]));
+      } else if (in.size() == 2 && val(in[1]).t == HVal::Bool) {
+        h.out_features = integer(val(in[0]));
+        h.with_bias = boolean(val(in[1]));
+      } else {
+        h.in_features = integer(val(in.at(0)));
+        h.out_features = integer(val(in.at(1)));
+        if (in.size() == 3) h.with_bias = boolean(val(in[2]));
+      }
+      return h;
+    }
+    if (node.op == "SiLU" || node.op == "Softmax") {
+      h.t = HVal::Act;
+      h.act = node.op;
+      return h;
+    }
+    if (node.op == "Embedding") {
+      h.t = HVal::Embedding;
+      h.num = integer(val(in.at(0)));
+      h.dim = integer(val(in.at(1)));
+      return h;
+    }
+    if (node.op == "Dropout") {
+      h.t = HVal::Act;
+      h.act = "Dropout";
+      h.prob = number(val(in.at(0)));
+      return h;
+    }
+    if (node.op == "RMSNorm") {
+      h.t = HVal::RmsNorm;
+      h.hidden = integer(val(in.at(0)));
+      h.eps = in.size() > 1 ? number(val(in[1])) : 1e-5;
+      return h;
+    }
+    fail("Unsupported library constructor '" + node.op + "'");
+  }
+
+  std::string linear_weight_name(int id) { return "linear_" + std::to_string(id) + "_weight"; }
+  std::string linear_bias_name(int id) { return "linear_" + std::to_string(id) + "_bias"; }
+  std::string embedding_weight_name(int id) { return "embedding_" + std::to_string(id) + "_weight"; }
+  std::string gain_name(int id) { return "rmsnorm_" + std::to_string(id) + "_gain"; }
+
+  // Weight of a linear apply: named parameter (train) or constant pattern.
+  Slot* linear_weight_slot(const HVal& cl, int64_t in_f) {
+    if (mode == kModeTrain)
+      return ensure_param(linear_weight_name(cl.ctor_id), {in_f, cl.out_features}, 0).value;
+    return const_pattern({in_f, cl.out_features}, 0);
+  }
+
+  HVal plan_apply(const GNode& node) {
+    const HVal& cl = val(node.inputs.at(0));
+    const HVal& x = val(node.inputs.at(1));
+    if (x.t != HVal::Tensor) fail("Graph executor expected tensor value");
+    switch (cl.t) {
+      case HVal::Linear: {
+        if (x.shape.size() != 2) {
+          if (mode != kModeTrain) fail("linear currently requires rank-2 input tensors");
+          fail("matmul currently requires rank-2 tensors");
+        }
+        const int64_t in_f = cl.in_features >= 0 ? cl.in_features : x.shape[1];
+        if (mode != kModeTrain && x.shape[1] != in_f)
+          fail("linear expected input feature size " + std::to_string(in_f) + ", got " + std::to_string(x.shape[1]));
+        if (x.shape[1] != in_f)
+          fail("matmul inner dimension mismatch: lhs=" + shape_str(x.shape) + " rhs=" +
+               shape_str({in_f, cl.out_features}));
+        Slot* w = linear_weight_slot(cl, in_f);
+        Slot* b = nullptr;
+        if (cl.with_bias) {
+          if (mode == kModeTrain) b = ensure_param(linear_bias_name(cl.ctor_id), {cl.out_features}, 1).value;
+          else b = const_pattern({cl.out_features}, 1);
+        }
+        const int64_t m = x.shape[0], n = cl.out_features;
+        HVal o = new_tensor({m, n});
+        gemm_step(forward, 1, m, n, in_f, x.slot, false, in_f, 0, w, false, n, 0, o.slot, n, 0, b, 1.0f,
+                  false, false);
+        return o;
+      }
+      case HVal::Embedding: {
+        Slot* w;
+        if (mode == kModeTrain) w = ensure_param(embedding_weight_name(cl.ctor_id), {cl.num, cl.dim}, 2).value;
+        else w = const_pattern({cl.num, cl.dim}, 2);
+        std::vector<int64_t> s = x.shape;
+        s.push_back(cl.dim);
+        HVal o = new_tensor(s);
+        Slot *ix = x.slot, *c = o.slot;
+        const int64_t count = numel(x.shape), num = cl.num, dim = cl.dim;
+        Context* cx = ctx;
+        forward.push_back([=](cudaStream_t st) { launch_embedding(ix->p, w->p, c->p, count, num, dim, cx->d_err, st); });
+        return o;
+      }
+      case HVal::RmsNorm: {
+        if (x.shape.empty() || x.shape.back() != cl.hidden)
+          fail("rms_norm hidden size mismatch: expected " + std::to_string(cl.hidden) + ", got " + shape_str(x.shape));
+        Slot* g;
+        if (mode == kModeTrain) g = ensure_param(gain_name(cl.ctor_id), {cl.hidden}, 3).value;
+        else g = const_pattern({cl.hidden}, 3);
+        HVal o = new_tensor(x.shape);
+        Slot *a = x.slot, *c = o.slot;
+        const int64_t h = cl.hidden, rows = numel(x.shape) / h;
+        const float eps = (float)cl.eps;
+        forward.push_back([=](cudaStream_t st) { launch_rms_norm_gain(a->p, g->p, c->p, rows, h, eps, st); });
+        return o;
+      }
+      case HVal::Act: {
+        HVal o = new_tensor(x.shape);
+        Slot *a = x.slot, *c = o.slot;
+        const int64_t n = numel(x.shape);
+        if (cl.act == "SiLU") {
+          forward.push_back([=](cudaStream_t st) { launch_unary(kUnarySilu, a->p, c->p, n, 0.0f, st); });
+        } else if (cl.act == "Softmax") {
+          if (x.shape.empty()) fail("softmax requires a tensor with at least one dimension");
+          const int64_t w = x.shape.back();
+          if (w == 0 || n % w != 0) fail("softmax requires the last dimension to divide the data length");
+          forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
+        } else {
+          if (!(cl.prob >= 0.0 && cl.prob < 1.0)) fail("dropout probability must be in [0, 1)");
+          const float keep = (float)(1.0 - cl.prob);
+          forward.push_back([=](cudaStream_t st) { launch_binary_ts(kMul, a->p, keep, c->p, n, st); });
+        }
+        return o;
+      }
+      default: fail("Unsupported graph apply operation");
+    }
+  }
+
+  // ---- backward planning ---------------------------------------------------------
+  // Returns the gradient slot of `vid` and whether this contribution must be
+  // accumulated into an existing value (accumulate_value, executor.rs:545-552).
+  std::pair<Slot*, bool> contrib(int vid) {
+    auto it = vgrad.find(vid);
+    if (it != vgrad.end()) return {it->second, true};
+    const HVal& h = val(vid);
+    Slot* s = alloc((size_t)numel(h.shape));
+    vgrad[vid] = s;
+    return {s, false};
+  }
+
+  std::pair<Slot*, bool> param_contrib(const std::string& name) {
+    Param& p = params.at(name);
+    if (!p.grad) p.grad = alloc((size_t)numel(p.shape));
+    bool acc = p.grad_written;
+    p.grad_written = true;
+    return {p.grad, acc};
+  }
+
+  void emit_copy(Slot* g, int vid, int64_t n) {
+    auto [d, acc] = contrib(vid);
+    backward.push_back([=](cudaStream_t st) {
+      if (acc) launch_add_inplace(d->p, g->p, n, st);
+      else launch_unary(kUnaryCopy, g->p, d->p, n, 0.0f, st);
+    });
+  }
+  void emit_neg(Slot* g, int vid, int64_t n) {
+    auto [d, acc] = contrib(vid);
+    backward.push_back([=](cudaStream_t st) {
+      if (acc) launch_binary_tt(kSub, d->p, g->p, d->p, n, st);
+      else launch_unary(kUnaryNeg, g->p, d->p, n, 0.0f, st);
+    });
+  }
+  void emit_tt(int op, Slot* g, Slot* other, int vid, int64_t n) {
+    auto [d, acc] = contrib(vid);
+    backward.push_back([=](cudaStream_t st) {
+      if (acc) launch_binary_tt_acc(op, g->p, other->p, d->p, n, st);
+      else launch_binary_tt(op, g->p, other->p, d->p, n, st);
+    });
+  }
+  void emit_ts(int op, Slot* g, float s, int vid, int64_t n) {
+    auto [d, acc] = contrib(vid);
+    backward.push_back([=](cudaStream_t st) {
+      if (acc) launch_binary_ts_acc(op, g->p, s, d->p, n, 0, st);
+      else launch_binary_ts(op, g->p, s, d->p, n, st);
+    });
+  }
+  // d(lhs) of lhs.rhs: g . rhs^T ; d(rhs): lhs^T . g  (layers.rs:521-527)
+  void emit_matmul_grads(Slot* g, const HVal& l, const HVal& r, int lid, int rid, bool want_l,
+                         bool want_r) {
+    const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
+    std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
+    const int batch = (int)numel(lead);
+    if (want_l) {
+      auto [d, acc] = contrib(lid);
+      gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr,
+                1.0f, acc, false);
+    }
+    if (want_r) {
+      auto [d, acc] = contrib(rid);
+      gemm_step(backward, batch, k, n, m, l.slot, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr,
+                1.0f, acc, false);
+    }
+  }
+
+  void plan_backward() {
+    const int oid = objective;
+    if (oid < 0) fail("Graph does not have a return value");
+    const HVal& obj = val(oid);
+    if (obj.t != HVal::Tensor) fail("Train executor expected tensor value");
+    {
+      Slot* s = alloc((size_t)numel(obj.shape));
+      vgrad[oid] = s;
+      const int64_t n = numel(obj.shape);
+      backward.push_back([=](cudaStream_t st) { launch_fill(s->p, n, 1.0f, st); });
+    }
+    const bool train = mode == kModeTrain;
+    for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
+      const GNode& node = *it;
+      auto gi = vgrad.find(node.output);
+      if (gi == vgrad.end()) continue;
+      Slot* g = gi->second;
+      const HVal& out = val(node.output);
+      const int64_t n = out.t == HVal::Tensor ? numel(out.shape) : 0;
+      switch (node.kind) {
+        case kNConst:
+        case kNCtor: break;
+        case kNBinary: {
+          const HVal& l = val(node.inputs[0]);
+          const HVal& r = val(node.inputs[1]);
+          const int li = node.inputs[0], ri = node.inputs[1];
+          if (l.t == HVal::Tensor && r.t == HVal::Tensor) {
+            switch (node.binop) {
+              case '+': emit_copy(g, li, n); emit_copy(g, ri, n); break;
+              case '-': emit_copy(g, li, n); emit_neg(g, ri, n); break;
+              case '*': emit_tt(kMul, g, r.slot, li, n); emit_tt(kMul, g, l.slot, ri, n); break;
+              case '/': {
+                emit_tt(kDiv, g, r.slot, li, n);
+                if (!train) {
+                  auto [d, acc] = contrib(ri);
+                  Slot *ls = l.slot, *rs = r.slot;
+                  backward.push_back([=](cudaStream_t st) { launch_div_rhs_grad(g->p, ls->p, rs->p, d->p, n, acc, st); });
+                }
+                break;
+              }
+              default: fail("Unsupported binary op in train backward");
+            }
+          } else if (l.t == HVal::Tensor) {
+            if (node.binop == '+' || node.binop == '-') emit_copy(g, li, n);
+            else emit_ts(binop_code(node.binop), g, (float)number(r), li, n);
+          } else if (r.t == HVal::Tensor) {
+            switch (node.binop) {
+              case '+': emit_copy(g, ri, n); break;
+              case '-': emit_neg(g, ri, n); break;
+              case '*': emit_ts(kMul, g, (float)number(l), ri, n); break;
+              default:
+                if (!train) fail("Backward for scalar/tensor division is not implemented yet");
+            }
+          }
+          break;
+        }
+        case kNPrimitive: {
+          if (node.op == "matmul") {
+            const HVal& l = val(node.inputs[0]);
+            const HVal& r = val(node.inputs[1]);
+            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true);
+          } else if (node.op == "relu") {
+            auto [d, acc] = contrib(node.inputs[0]);
+            Slot* y = out.slot;
+            backward.push_back([=](cudaStream_t st) { launch_relu_backward(y->p, g->p, d->p, n, acc, st); });
+          } else if (node.op == "scale") {
+            emit_ts(kMul, g, (float)number(val(node.inputs[1])), node.inputs[0], n);
+          } else {
+            fail(train ? "Unsupported primitive op in train backward"
+                       : "Unsupported primitive op '" + node.op + "' in graph backward");
+          }
+          break;
+        }
+        case kNCall: plan_call_backward(node, g, out, n, train); break;
+        case kNApply: plan_apply_backward(node, g, out, n, train); break;
+      }
+    }
+  }
+
+  void plan_call_backward(const GNode& node, Slot* g, const HVal& out, int64_t n, bool train) {
+    const std::string& op = node.op;
+    const int xi = node.inputs.at(0);
+    const HVal& x = val(xi);
+    if (op == "rms_norm") {
+      if (x.shape != out.shape) fail("backward_rms_norm_input shape mismatch");
+      emit_copy(g, xi, n);
+      return;
+    }
+    if (op == "cross_entropy") {
+      const HVal& t = val(node.inputs.at(1));
+      const int64_t w = x.shape.back(), rows = numel(x.shape) / w;
+      const bool labels = x.shape != t.shape;
+      {
+        auto [d, acc] = contrib(xi);
+        Slot *lg = x.slot, *tg = t.slot;
+        Context* cx = ctx;
+        backward.push_back([=](cudaStream_t st) {
+          if (labels) launch_cross_entropy_labels_backward(lg->p, tg->p, d->p, rows, w, acc, cx->d_err, st);
+          else launch_cross_entropy_backward(lg->p, tg->p, d->p, rows, w, acc, st);
+        });
+      }
+      if (!train) {
+        auto [d, acc] = contrib(node.inputs.at(1));
+        const int64_t tn = numel(t.shape);
+        if (!acc) backward.push_back([=](cudaStream_t st) { launch_fill(d->p, tn, 0.0f, st); });
+      }
+      return;
+    }
+    if (op == "transpose") {
+      int64_t a = integer(val(node.inputs[1])), b = integer(val(node.inputs[2]));
+      const int64_t rank = (int64_t)x.shape.size();
+      if (a < 0) a += rank;
+      if (b < 0) b += rank;
+      if (a > b) std::swap(a, b);
+      auto [d, acc] = contrib(xi);
+      std::vector<int64_t> dims = out.shape;
+      const int ia = (int)a, ib = (int)b;
+      backward.push_back([=](cudaStream_t st) {
+        launch_transpose(g->p, d->p, dims.data(), (int)dims.size(), ia, ib, acc, st);
+      });
+      return;
+    }
+    if (!train) fail("Unsupported library op '" + op + "' in graph backward");
+    if (op == "reshape" || op == "flatten_heads") {
+      if (numel(x.shape) != n) fail("reshape backward requires matching element counts");
+      emit_copy(g, xi, n);
+    } else if (op == "repeat_kv") {
+      const int64_t rep = integer(val(node.inputs.at(1)));
+      int64_t inner = 1;
+      for (size_t i = 2; i < x.shape.size(); ++i) inner *= x.shape[i];
+      const int64_t outer = x.shape[0], heads = x.shape[1];
+      auto [d, acc] = contrib(xi);
+      backward.push_back([=](cudaStream_t st) {
+        launch_repeat_kv_backward(g->p, d->p, outer, heads, inner, rep, acc, st);
+      });
+    } else if (op == "causal_mask") {
+      const int64_t q = out.shape[out.shape.size() - 2], k = out.shape.back();
+      const int64_t outer = n / (q * k > 0 ? q * k : 1);
+      auto [d, acc] = contrib(xi);
+      backward.push_back([=](cudaStream_t st) { launch_causal_mask_backward(g->p, d->p, outer, q, k, acc, st); });
+    } else if (op == "rope") {
+      const int64_t hd = integer(val(node.inputs.at(1)));
+      const double theta = number(val(node.inputs.at(2)));
+      int64_t outer, seq;
+      rope_dims(out.shape, hd, &outer, &seq);
+      const float2* tab = ctx->rope_table(seq, hd / 2, theta);
+      auto [d, acc] = contrib(xi);
+      backward.push_back([=](cudaStream_t st) { launch_rope_backward(g->p, d->p, tab, outer, seq, hd / 2, acc, st); });
+    }
+    // Other library calls contribute nothing in train mode (executor.rs:661-687).
+  }
+
+  void plan_apply_backward(const GNode& node, Slot* g, const HVal& out, int64_t n, bool train) {
+    const HVal& cl = val(node.inputs.at(0));
+    const int xi = node.inputs.at(1);
+    const HVal& x = val(xi);
+    switch (cl.t) {
+      case HVal::Linear: {
+        const int64_t in_f = cl.in_features >= 0 ? cl.in_features : (x.shape.size() > 1 ? x.shape[1] : 0);
+        const int64_t m = x.shape[0], nf = cl.out_features;
+        Slot* w;
+        if (train) {
+          auto pit = params.find(linear_weight_name(cl.ctor_id));
+          w = pit != params.end() ? pit->second.value : const_pattern({in_f, nf}, 0);
+        } else {
+          w = const_pattern({in_f, nf}, 4);  // backward.rs:225-235 fake weight
+        }
+        {
+          auto [d, acc] = contrib(xi);
+          gemm_step(backward, 1, m, in_f, nf, g, false, nf, 0, w, true, nf, 0, d, in_f, 0, nullptr, 1.0f, acc, false);
+        }
+        if (train) {
+          auto [dw, accw] = param_contrib(linear_weight_name(cl.ctor_id));
+          gemm_step(backward, 1, in_f, nf, m, x.slot, true, in_f, 0, g, false, nf, 0, dw, nf, 0, nullptr, 1.0f,
+                    accw, false);
+          if (cl.with_bias) {
+            auto [db, accb] = param_contrib(linear_bias_name(cl.ctor_id));
+            need_scratch((size_t)colsum_partial_elems(m, nf));
+            Slot** scr = &scratch;
+            backward.push_back([=](cudaStream_t st) { launch_colsum(g->p, db->p, (*scr)->p, m, nf, accb, st); });
+          }
+        }
+        return;
+      }
+      case HVal::Embedding: {
+        if (!train) fail("Graph backward does not support this library apply yet");
+        auto [dw, accw] = param_contrib(embedding_weight_name(cl.ctor_id));
+        const int64_t count = numel(x.shape), num = cl.num, dim = cl.dim;
+        need_scratch(embedding_backward_work_bytes(count, num) / sizeof(float) + 1);
+        Slot** scr = &scratch;
+        Slot* ix = x.slot;
+        backward.push_back([=](cudaStream_t st) {
+          launch_embedding_backward(g->p, ix->p, dw->p, count, num, dim, (*scr)->p, accw, st);
+        });
+        return;
+      }
+      case HVal::RmsNorm: {
+        const int64_t h = cl.hidden, rows = numel(x.shape) / h;
+        const float eps = (float)cl.eps;
+        Slot* gain;
+        Slot* dg = nullptr;
+        bool accg = false;
+        if (train) {
+          gain = params.at(gain_name(cl.ctor_id)).value;
+          auto pc = param_contrib(gain_name(cl.ctor_id));
+          dg = pc.first;
+          accg = pc.second;
+        } else {
+          gain = const_pattern({h}, 3);
+          dg = alloc((size_t)h);  // discarded in --backward
+        }
+        auto [d, acc] = contrib(xi);
+        need_scratch((size_t)rms_gain_partial_elems(rows, h));
+        Slot** scr = &scratch;
+        Slot* xs = x.slot;
+        backward.push_back([=](cudaStream_t st) {
+          launch_rms_norm_gain_backward(xs->p, gain->p, g->p, d->p, dg->p, (*scr)->p, rows, h, eps, acc, accg, st);
+        });
+        return;
+      }
+      case HVal::Act: {
+        auto [d, acc] = contrib(xi);
+        Slot* xs = x.slot;
+        Slot* ys = out.slot;
+        if (cl.act == "SiLU") {
+          backward.push_back([=](cudaStream_t st) { launch_silu_backward(xs->p, g->p, d->p, n, acc, st); });
+        } else if (cl.act == "Softmax") {
+          backward.push_back([=](cudaStream_t st) { launch_softmax_backward(ys->p, g->p, d->p, n, acc, st); });
+        } else {
+          const float keep = (float)(1.0 - cl.prob);
+          backward.push_back([=](cudaStream_t st) {
+            if (acc) launch_binary_ts_acc(kMul, g->p, keep, d->p, n, 0, st);
+            else launch_binary_ts(kMul, g->p, keep, d->p, n, st);
+          });
+        }
+        return;
+      }
+      default: fail(train ? "Unsupported apply in train backward" : "Graph backward does not support this library apply yet");
+    }
+  }
+
+  // ---- update planning (train) ------------------------------------------------------
+  void plan_update() {
+    // The loss (sum of the objective) is computed before the update, from
+    // the forward values of this step (executor.rs:803-811).
+    const HVal& obj = val(objective);
+    const int64_t n = numel(obj.shape);
+    Slot* o = obj.slot;
+    Slot** ls = &loss;
+    need_scratch(1024);
+    Slot** scr = &scratch;
+    update.push_back([=](cudaStream_t st) { launch_reduce_sum(o->p, (*ls)->p, (*scr)->p, n, st); });
+    Context* cx = ctx;
+    Slot** gb = &grad_block;
+    update.push_back([=, this](cudaStream_t st) {
+      (void)st;
+      if (allreduce && (*gb)->n > 0) comm_allreduce(cx, (*gb)->p, (*gb)->n);
+    });
+    std::vector<std::string> names(param_order);
+    std::sort(names.begin(), names.end());  // BTreeMap order (executor.rs:750)
+    for (const std::string& name : names) {
+      Param& p = params.at(name);
+      if (!p.grad) continue;
+      Slot *pv = p.value, *pg = p.grad;
+      const int64_t pn = numel(p.shape);
+      float* lr_ptr = &lr_f;
+      update.push_back([=](cudaStream_t st) { launch_sgd(pv->p, pg->p, *lr_ptr, pn, st); });
+    }
+  }
+  float lr_f = 0.01f;
+
+  // ---- arena layout --------------------------------------------------------------------
+  void layout() {
+    // Parameter gradients and the loss share one contiguous block so that a
+    // data-parallel step all-reduces them with one collective.
+    size_t gtotal = 0;
+    std::vector<Slot*> gslots;
+    for (const std::string& name : param_order) {
+      Param& p = params.at(name);
+      if (p.grad) {
+        gslots.push_back(p.grad);
+        gtotal += (p.grad->n + 63) & ~(size_t)63;
+      }
+    }
+    if (mode == kModeTrain) {
+      loss = alloc(1);
+      gslots.push_back(loss);
+      gtotal += 64;
+    }
+    scratch = alloc(scratch_floats + 64);
+    size_t total = 0;
+    std::map<Slot*, size_t> off;
+    // grad block first
+    size_t gb_start = 0;
+    for (Slot* s : gslots) {
+      off[s] = total;
+      total += (s->n + 63) & ~(size_t)63;
+    }
+    const size_t gb_end = total;
+    for (Slot& s : slots) {
+      if (s.base || off.count(&s)) continue;
+      off[&s] = total;
+      total += (s.n + 63) & ~(size_t)63;
+    }
+    if (arena) cudaFree(arena);
+    TYSOR_CUDA(cudaMalloc(&arena, sizeof(float) * (total + 64)));
+    // Zeroed once so the padding inside the gradient block is defined.
+    TYSOR_CUDA(cudaMemsetAsync(arena, 0, sizeof(float) * (total + 64), ctx->stream));
+    float* basep = (float*)arena;
+    for (Slot& s : slots)
+      if (!s.base) s.p = basep + off[&s];
+    for (Slot& s : slots)
+      if (s.base) s.p = s.base->p + s.offset;
+    if (mode == kModeTrain) {
+      slots.push_back(Slot{gb_end - gb_start, nullptr, 0, basep + gb_start});
+      grad_block = &slots.back();
+    }
+  }
+
+  void plan(int m) {
+    if (!dirty && mode == m) return;
+    release();
+    mode = m;
+    plan_forward();
+    if (mode != kModeRun) plan_backward();
+    if (mode == kModeTrain) plan_update();
+    layout();
+    dirty = false;
+  }
+
+  void run_list(const std::vector<StepFn>& list) {
+    for (const StepFn& f : list) f(ctx->stream);
+  }
+
+  void ensure_setup() {
+    if (setup_done) return;
+    run_list(setup);
+    setup_done = true;
+  }
+};
+
+Executor* E(void* g) {
+  if (!g) throw CudaError("null graph");
+  Executor* e = static_cast<Executor*>(g);
+  TYSOR_CUDA(cudaSetDevice(e->ctx->device));
+  return e;
+}
+
+template <typename F>
+bool guarded_g(F&& f) {
+  try {
+    f();
+    return true;
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return false;
+  }
+}
+
+Slot* value_slot(Executor* e, int id, std::vector<int64_t>* shape) {
+  if (id < 0 || id >= (int)e->hv.size()) throw CudaError("value id out of range");
+  const HVal& h = e->hv[id];
+  if (h.t != HVal::Tensor || !h.slot) throw CudaError("value " + std::to_string(id) + " is not a tensor");
+  if (shape) *shape = h.shape;
+  return h.slot;
+}
+
+}  // namespace
+}  // namespace tysor
+
+using namespace tysor;
+
+extern "C" {
+
+void* tysor_cuda_graph_new(void* context, const char* graph_text) {
+  Executor* out = nullptr;
+  guarded_g([&] {
+    if (!context) throw CudaError("null context");
+    if (!graph_text) throw CudaError("null graph text");
+    auto e = std::make_unique<Executor>();
+    e->ctx = static_cast<Context*>(context);
+    e->parse(graph_text);
+    out = e.release();
+  });
+  return out;
+}
+
+void tysor_cuda_graph_free(void* graph) {
+  if (!graph) return;
+  Executor* e = static_cast<Executor*>(graph);
+  cudaSetDevice(e->ctx->device);
+  cudaStreamSynchronize(e->ctx->stream);
+  delete e;
+}
+
+bool tysor_cuda_graph_set_shape(void* graph, const char* name, const int64_t* dims, int rank) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (rank < 1) throw CudaError("shape must contain at least one dimension");
+    std::vector<int64_t> s(dims, dims + rank);
+    for (auto d : s)
+      if (d <= 0) throw CudaError("invalid dimension in shape");
+    e->shapes[name] = s;
+    e->dirty = true;
+  });
+}
+
+bool tysor_cuda_graph_set_input(void* graph, const char* name, const float* data, size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    auto it = e->inputs.find(name);
+    const bool same_size = it != e->inputs.end() && it->second.size() == count;
+    e->inputs[name].assign(data, data + count);
+    e->device_inputs.erase(name);
+    if (!same_size) e->dirty = true;  // the plan reads the stored vector at each call
+  });
+}
+
+bool tysor_cuda_graph_upload_input(void* graph, const char* name, const float* data,
+                                   size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (e->mode < 0 || e->dirty) throw CudaError("graph buffers are not planned yet: run it once first");
+    for (const GValue& v : e->values) {
+      if (!v.is_param || v.name != name) continue;
+      Slot* s = e->hv.at(v.id).slot;
+      if (!s || count != s->n)
+        throw CudaError("input '" + std::string(name) + "' holds " + std::to_string(s ? s->n : 0) +
+                        " values, " + std::to_string(count) + " given");
+      TYSOR_CUDA(cudaMemcpyAsync(s->p, data, sizeof(float) * count, cudaMemcpyHostToDevice, e->ctx->stream));
+      // Later calls must not overwrite it with a stored input.
+      e->device_inputs.insert(v.name);
+      return;
+    }
+    throw CudaError(std::string("no graph input named '") + name + "'");
+  });
+}
+
+bool tysor_cuda_graph_set_parameter(void* graph, const char* name, const float* data,
+                                    size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    e->param_init[name].assign(data, data + count);
+    e->dirty = true;
+  });
+}
+
+bool tysor_cuda_graph_run(void* graph) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    const int64_t l0 = g_launches.load();
+    e->plan(kModeRun);
+    e->ensure_setup();
+    e->run_uploads();
+    e->run_list(e->forward);
+    e->last_launches = g_launches.load() - l0;
+    e->ctx->sync_and_check();
+  });
+}
+
+bool tysor_cuda_graph_backward(void* graph) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    const int64_t l0 = g_launches.load();
+    e->plan(kModeBackward);
+    e->ensure_setup();
+    e->run_uploads();
+    e->run_list(e->forward);
+    e->run_list(e->backward);
+    e->last_launches = g_launches.load() - l0;
+    e->ctx->sync_and_check();
+  });
+}
+
+bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losses) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (iterations < 0) throw CudaError("iterations must be >= 0");
+    e->plan(kModeTrain);
+    e->lr_f = (float)lr;
+    e->ensure_setup();
+    e->run_uploads();
+    cudaStream_t st = e->ctx->stream;
+    float* d_losses = nullptr;
+    if (iterations > 0) TYSOR_CUDA(cudaMallocAsync(&d_losses, sizeof(float) * iterations, st));
+    auto step = [&]() {
+      e->run_list(e->forward);
+      e->run_list(e->backward);
+      e->run_list(e->update);
+    };
+    for (int it = 0; it < iterations; ++it) {
+      const int64_t l0 = g_launches.load();
+      if (e->capture && it > 0) {
+        if (!e->exec) {
+          cudaGraph_t g = nullptr;
+          TYSOR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+          try {
+            step();
+          } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+          }
+          TYSOR_CUDA(cudaStreamEndCapture(st, &g));
+          TYSOR_CUDA(cudaGraphInstantiate(&e->exec, g, 0));
+          cudaGraphDestroy(g);
+          e->last_launches = g_launches.load() - l0;
+        }
+        TYSOR_CUDA(cudaGraphLaunch(e->exec, st));
+      } else {
+        step();
+        e->last_launches = g_launches.load() - l0;
+      }
+      TYSOR_CUDA(cudaMemcpyAsync(d_losses + it, e->loss->p, sizeof(float), cudaMemcpyDeviceToDevice, st));
+    }
+    std::vector<float> host(iterations > 0 ? iterations : 1);
+    if (iterations > 0) {
+      TYSOR_CUDA(cudaMemcpyAsync(host.data(), d_losses, sizeof(float) * iterations, cudaMemcpyDeviceToHost, st));
+      TYSOR_CUDA(cudaFreeAsync(d_losses, st));
+    }
+    e->ctx->sync_and_check();
+    if (losses)
+      for (int i = 0; i < iterations; ++i) losses[i] = host[i];
+  });
+}
+
+int tysor_cuda_graph_value_rank(void* graph, int value_id) {
+  int rank = -1;
+  guarded_g([&] {
+    std::vector<int64_t> s;
+    value_slot(E(graph), value_id, &s);
+    rank = (int)s.size();
+  });
+  return rank;
+}
+
+bool tysor_cuda_graph_value_shape(void* graph, int value_id, int64_t* dims) {
+  return guarded_g([&] {
+    std::vector<int64_t> s;
+    value_slot(E(graph), value_id, &s);
+    for (size_t i = 0; i < s.size(); ++i) dims[i] = s[i];
+  });
+}
+
+bool tysor_cuda_graph_read_value(void* graph, int value_id, float* out, size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    std::vector<int64_t> s;
+    Slot* sl = value_slot(e, value_id, &s);
+    if (count > sl->n) throw CudaError("read past the end of the value");
+    e->ctx->sync_and_check();
+    TYSOR_CUDA(cudaMemcpy(out, sl->p, sizeof(float) * count, cudaMemcpyDeviceToHost));
+  });
+}
+
+bool tysor_cuda_graph_read_value_grad(void* graph, int value_id, float* out, size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    auto it = e->vgrad.find(value_id);
+    if (it == e->vgrad.end()) throw CudaError("value has no gradient");
+    if (count > it->second->n) throw CudaError("read past the end of the gradient");
+    e->ctx->sync_and_check();
+    TYSOR_CUDA(cudaMemcpy(out, it->second->p, sizeof(float) * count, cudaMemcpyDeviceToHost));
+  });
+}
+
+int tysor_cuda_graph_num_parameters(void* graph) {
+  int n = -1;
+  guarded_g([&] { n = (int)E(graph)->param_order.size(); });
+  return n;
+}
+
+const char* tysor_cuda_graph_parameter_name(void* graph, int index) {
+  const char* out = nullptr;
+  guarded_g([&] {
+    Executor* e = E(graph);
+    if (index < 0 || index >= (int)e->param_order.size()) throw CudaError("parameter index out of range");
+    out = e->param_order[index].c_str();
+  });
+  return out;
+}
+
+size_t tysor_cuda_graph_parameter_count(void* graph, const char* name) {
+  size_t n = 0;
+  guarded_g([&] {
+    Executor* e = E(graph);
+    n = (size_t)numel(e->params.at(name).shape);
+  });
+  return n;
+}
+
+bool tysor_cuda_graph_read_parameter(void* graph, const char* name, float* out, size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    auto it = e->params.find(name);
+    if (it == e->params.end()) throw CudaError(std::string("no parameter '") + name + "'");
+    if (count > it->second.value->n) throw CudaError("read past the end of the parameter");
+    e->ensure_setup();
+    e->ctx->sync_and_check();
+    TYSOR_CUDA(cudaMemcpy(out, it->second.value->p, sizeof(float) * count, cudaMemcpyDeviceToHost));
+  });
+}
+
+bool tysor_cuda_graph_read_parameter_grad(void* graph, const char* name, float* out, size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    auto it = e->params.find(name);
+    if (it == e->params.end() || !it->second.grad) throw CudaError(std::string("no gradient for '") + name + "'");
+    if (count > it->second.grad->n) throw CudaError("read past the end of the gradient");
+    e->ctx->sync_and_check();
+    TYSOR_CUDA(cudaMemcpy(out, it->second.grad->p, sizeof(float) * count, cudaMemcpyDeviceToHost));
+  });
+}
+
+int64_t tysor_cuda_graph_launch_count(void* graph) {
+  int64_t n = -1;
+  guarded_g([&] { n = E(graph)->last_launches; });
+  return n;
+}
+
+bool tysor_cuda_graph_set_capture(void* graph, bool enable) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    e->capture = enable;
+    if (!enable && e->exec) {
+      cudaGraphExecDestroy(e->exec);
+      e->exec = nullptr;
+    }
+  });
+}
+
+bool tysor_cuda_graph_enable_allreduce(void* graph, bool enable) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (enable && !e->ctx->comm) throw CudaError("no communicator: call tysor_cuda_comm_init first");
+    if (e->allreduce != enable) {
+      e->allreduce = enable;
+      if (e->exec) {
+        cudaGraphExecDestroy(e->exec);
+        e->exec = nullptr;
+      }
+    }
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,614 @@
+// fp32 matmul for sm_100a.
+//
+// Tensor-core path: a tcgen05 kernel.  TMA (cp.async.bulk.tensor) stages
+// 128 x 16 (A) and BN x 16 (B) fp32 tiles in shared memory through a 4-stage
+// mbarrier ring; one elected thread issues tcgen05.mma.kind::tf32 with the
+// accumulator in tensor memory (128 lanes x BN fp32 columns); four warps read
+// the accumulator back with tcgen05.ld and apply the epilogue (alpha, bias,
+// relu, accumulate-into-C).
+//
+// Strict mode (the default) is 3xTF32: each operand x is used as-is (the
+// tensor core reads its top 19 bits, i.e. the tf32 truncation hi(x)) and as
+// lo(x) = x - hi(x), prepared in scratch memory by split_lo_kernel; the
+// products hi*hi + hi*lo + lo*hi recover fp32-level accuracy.  Fast mode
+// issues only hi*hi.
+//
+// Both operand layouts are supported without copies: a K-contiguous operand
+// is staged with 64-byte swizzle (K-major UMMA descriptor), an
+// M/N-contiguous one with 128-byte swizzle (MN-major descriptor), so the
+// transposed products of backward (dY.W^T, X^T.dY) read the stored tensors
+// directly.
+//
+// CUDA-core path: products and sums rounded separately in increasing k
+// order (bit-identical to a sequential fp32 loop).  It serves shapes whose
+// strides break TMA's 16-byte rules and the opt-in exact mode.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tysor {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 16;  // fp32 elements of K per stage (64 bytes)
+constexpr int kThreads = 128;
+constexpr int kStages = 4;
+constexpr long long kWaitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the given phase parity; gives up after kWaitCycles, recording
+// kErrBarrierTimeout, so a lost arrival can never hang the GPU.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, (int)kErrBarrierTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+// Layout types of the descriptor (bits 61-63).
+constexpr uint32_t kLayoutSW128Base32B = 1;  // 128-byte rows, 32-byte chunks swizzled
+constexpr uint32_t kLayoutSW64 = 4;
+
+// Descriptor of the k-th (8-deep) MMA slice of a staged operand tile.
+// K-major tiles: rows of 64 bytes, 8-row swizzle atoms of 512 bytes; the
+// slice offset is 32 bytes inside the atom.  MN-major tiles (32-bit
+// elements admit only the "128B, 32-byte atom" swizzle): blocks of 32 M/N
+// elements x 16 k-rows of 128 bytes (2 KiB per block, LBO), 4-row swizzle
+// atoms (512 bytes, SBO); the slice offset is 8 k-rows (1 KiB).
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, bool mn_major, int kslice) {
+  if (mn_major) return smem_desc(tile + 1024u * kslice, 2048u, 512u, kLayoutSW128Base32B);
+  return smem_desc(tile + 32u * kslice, 16u, 512u, kLayoutSW64);
+}
+
+template <int BN>
+struct TileCfg {
+  static constexpr int kABytes = BM * BK * 4;
+  static constexpr int kBBytes = BN * BK * 4;
+};
+
+template <int BN, bool kStrict>
+struct PipeCfg {
+  static constexpr int kA = TileCfg<BN>::kABytes;
+  static constexpr int kB = TileCfg<BN>::kBBytes;
+  static constexpr int kStageBytes = kStrict ? 2 * (kA + kB) : (kA + kB);
+  static constexpr int kStagesRaw = (192 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+// The tensor core adds each MMA's products into the accumulator with
+// round-toward-zero, so a long K run in one accumulator drifts by up to
+// (number of MMAs) x 2^-24 relative.  The kernel therefore accumulates K in
+// chunks of kChunkKb k-blocks (128 elements) into one of two tensor-memory
+// buffers, and eight "accumulator" warps add each finished chunk into fp32
+// registers with round-to-nearest while the tensor core fills the other
+// buffer.  The error stays at the chunk level (about 1.4e-6 relative in
+// strict mode) whatever K is.
+constexpr int kChunkKb = 8;
+constexpr int kAccWarps = 8;
+constexpr int kThreadsTC = 64 + 32 * kAccWarps;
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+template <int BN, bool kStrict, bool kAmn, bool kBmn>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_alo,
+                     const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_blo, GemmOutput out,
+                     GemmEpilogue ep, int M, int N, int K, int* err) {
+  using Cfg = PipeCfg<BN, kStrict>;
+  constexpr int kA = Cfg::kA;
+  constexpr int kB = Cfg::kB;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kStageBytes = Cfg::kStageBytes;
+  constexpr uint32_t kTxBytes = kStageBytes;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr int kHalf = BN / 2;  // columns per accumulator warp
+  constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kAmn ? 1u : 0u) << 15) |
+                              ((kBmn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(BM >> 4) << 24);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1 KiB alignment for the swizzle atoms.
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + kStages * kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* tfull_bar = bars + 2 * kStages;       // [2] chunk accumulated
+  uint64_t* tempty_bar = bars + 2 * kStages + 2;  // [2] chunk read back
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kStages + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int bz = blockIdx.z;
+  const int num_kb = (K + BK - 1) / BK;
+  const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull_bar[b]), 1);
+      mbar_init(smem_u32(&tempty_bar[b]), kAccWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int s = kb % kStages;
+      if (kb >= kStages) ok = mbar_wait(smem_u32(&empty_bar[s]), ((kb / kStages) - 1) & 1, err);
+      if (!ok) break;
+      const uint32_t fb = smem_u32(&full_bar[s]);
+      mbar_expect_tx(fb, kTxBytes);
+      const uint32_t base = smem_u32(smem + s * kStageBytes);
+      const int k0 = kb * BK;
+      const int nmaps = kStrict ? 2 : 1;
+      for (int h = 0; h < nmaps; ++h) {
+        const CUtensorMap* ma = h ? &map_alo : &map_a;
+        const CUtensorMap* mb = h ? &map_blo : &map_b;
+        const uint32_t ta = base + h * kA;
+        const uint32_t tb = base + nmaps * kA + h * kB;
+        if (kAmn) {
+#pragma unroll
+          for (int i = 0; i < BM / 32; ++i) tma_load_3d(ta + i * 2048, ma, fb, m0 + 32 * i, k0, bz);
+        } else {
+          tma_load_3d(ta, ma, fb, k0, m0, bz);
+        }
+        if (kBmn) {
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) tma_load_3d(tb + i * 2048, mb, fb, n0 + 32 * i, k0, bz);
+        } else {
+          tma_load_3d(tb, mb, fb, k0, n0, bz);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: chunk c accumulates into tensor-memory buffer c & 1.
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int s = kb % kStages;
+      const int chunk = kb / kChunkKb;
+      const int buf = chunk & 1;
+      const bool first = (kb % kChunkKb) == 0;
+      const bool last = (kb % kChunkKb) == kChunkKb - 1 || kb == num_kb - 1;
+      if (first && chunk >= 2) {
+        ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((chunk >> 1) - 1) & 1, err);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      ok = mbar_wait(smem_u32(&full_bar[s]), (kb / kStages) & 1, err);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(buf * BN);
+      const uint32_t base = smem_u32(smem + s * kStageBytes);
+      const int nmaps = kStrict ? 2 : 1;
+      const uint32_t ta = base, talo = base + kA;
+      const uint32_t tb = base + nmaps * kA, tblo = tb + kB;
+#pragma unroll
+      for (int j = 0; j < BK / 8; ++j) {
+        const uint64_t da = operand_desc(ta, kAmn, j);
+        const uint64_t db = operand_desc(tb, kBmn, j);
+        const uint32_t acc = (first && j == 0) ? 0u : 1u;
+        if (kStrict) {
+          // Small terms first, then the leading hi*hi product.
+          umma_tf32(d, operand_desc(talo, kAmn, j), db, kIdesc, acc);
+          umma_tf32(d, da, operand_desc(tblo, kBmn, j), kIdesc, 1u);
+          umma_tf32(d, da, db, kIdesc, 1u);
+        } else {
+          umma_tf32(d, da, db, kIdesc, acc);
+        }
+      }
+      umma_commit(smem_u32(&empty_bar[s]));
+      if (last) umma_commit(smem_u32(&tfull_bar[buf]));
+    }
+  }
+  __syncwarp();
+
+  if (warp >= 2) {
+    // Accumulator warps: TMEM lane quadrant = warp % 4 (hardware rule),
+    // column half = (warp - 2) / 4.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    float acc[kHalf];
+#pragma unroll
+    for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
+    bool have = true;
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+      const int buf = chunk & 1;
+      have = mbar_wait(smem_u32(&tfull_bar[buf]), (chunk >> 1) & 1, err);
+      if (!have) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
+#pragma unroll
+      for (int c = 0; c < kHalf; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c + i] = acc[c + i] + __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[buf]));
+    }
+
+    // Epilogue: alpha, bias, relu, accumulate-into-C, store.
+    const int row = m0 + quad * 32 + lane;
+    const int col0 = n0 + half * kHalf;
+    if (have && row < M && col0 < N) {
+      float* crow = out.ptr + (int64_t)bz * out.batch_stride + (int64_t)row * out.ld + col0;
+      const bool vec_ok = ((out.ld & 3) == 0) && ((((uintptr_t)out.ptr) & 15) == 0) &&
+                          ((out.batch_stride & 3) == 0) && (col0 + kHalf <= N);
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
+        float r = acc[i] * ep.alpha;
+        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
+        if (ep.relu) r = fmaxf(r, 0.0f);
+        acc[i] = r;
+      }
+      if (vec_ok) {
+        float4* dst = (float4*)crow;
+#pragma unroll
+        for (int q = 0; q < kHalf / 4; ++q) {
+          float4 w = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+          if (ep.accumulate) {
+            const float4 o = dst[q];
+            w.x = o.x + w.x;
+            w.y = o.y + w.y;
+            w.z = o.z + w.z;
+            w.w = o.w + w.w;
+          }
+          dst[q] = w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i)
+          if (col0 + i < N) crow[i] = ep.accumulate ? crow[i] + acc[i] : acc[i];
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// lo(x) = x - tf32_trunc(x), elementwise over a contiguous span.
+__global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
+  const int64_t n4 = n >> 2;
+  const float4* x4 = (const float4*)x;
+  float4* lo4 = (float4*)lo;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = x4[i];
+    float4 r;
+    r.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    r.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    r.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    r.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    lo4[i] = r;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float v = x[i];
+    lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  }
+}
+
+// CUDA-core GEMM: one output per thread, 16x16 tiles staged in shared
+// memory, k walked in increasing order with separately rounded products
+// and sums.
+__global__ void gemm_simt_kernel(GemmOperand A, GemmOperand B, GemmOutput C, GemmEpilogue ep,
+                                 int M, int N, int K) {
+  __shared__ float sa[16][17];
+  __shared__ float sb[16][17];
+  const int bz = blockIdx.z;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int row = blockIdx.y * 16 + ty;
+  const int col = blockIdx.x * 16 + tx;
+  const float* a = A.ptr + (int64_t)bz * A.batch_stride;
+  const float* b = B.ptr + (int64_t)bz * B.batch_stride;
+  float acc = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    {
+      const int r = blockIdx.y * 16 + ty, k = k0 + tx;
+      float v = 0.0f;
+      if (r < M && k < K) v = A.trans ? a[(int64_t)k * A.ld + r] : a[(int64_t)r * A.ld + k];
+      sa[ty][tx] = v;
+    }
+    {
+      const int k = k0 + ty, c = blockIdx.x * 16 + tx;
+      float v = 0.0f;
+      if (k < K && c < N) v = B.trans ? b[(int64_t)c * B.ld + k] : b[(int64_t)k * B.ld + c];
+      sb[ty][tx] = v;
+    }
+    __syncthreads();
+    const int kmax = (K - k0) < 16 ? (K - k0) : 16;
+    for (int kk = 0; kk < kmax; ++kk) acc = __fadd_rn(acc, __fmul_rn(sa[ty][kk], sb[kk][tx]));
+    __syncthreads();
+  }
+  if (row < M && col < N) {
+    float r = __fmul_rn(acc, ep.alpha);
+    if (ep.alpha == 1.0f) r = acc;
+    if (ep.bias != nullptr) r = __fadd_rn(r, ep.bias[col]);
+    if (ep.relu) r = fmaxf(r, 0.0f);
+    float* dst = C.ptr + (int64_t)bz * C.batch_stride + (int64_t)row * C.ld + col;
+    *dst = ep.accumulate ? __fadd_rn(*dst, r) : r;
+  }
+}
+
+// ---- host side ------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  if (!fn) throw CudaError("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// Rank-3 fp32 tensor map {inner, outer, batch}.
+CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, uint64_t batch,
+                     uint64_t ld, uint64_t bstride, uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swz) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  uint64_t bs = bstride ? bstride : ld * outer;
+  bs = (bs + 3) & ~(uint64_t)3;
+  cuuint64_t strides[2] = {ld * 4, bs * 4};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return m;
+}
+
+bool tma_ok(const GemmOperand& X, int batch) {
+  if (((uintptr_t)X.ptr & 15) != 0) return false;
+  if ((X.ld & 3) != 0) return false;
+  if (batch > 1 && (X.batch_stride & 3) != 0) return false;
+  return true;
+}
+
+// Number of elements from the operand's first to its last stored element.
+int64_t operand_span(const GemmOperand& X, int batch, int64_t rows, int64_t cols) {
+  return (int64_t)(batch - 1) * X.batch_stride + (rows - 1) * X.ld + cols;
+}
+
+template <int BN, bool S, bool AMN, bool BMN>
+void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
+               const CUtensorMap& mblo, const GemmOutput& C, const GemmEpilogue& ep, int batch,
+               int M, int N, int K, int* d_err, cudaStream_t st) {
+  constexpr int smem = PipeCfg<BN, S>::kSmem;
+  auto kern = gemm_tf32_kernel<BN, S, AMN, BMN>;
+  static bool configured = false;
+  if (!configured) {
+    TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((unsigned)ceil_div(N, BN), (unsigned)ceil_div(M, BM), (unsigned)batch);
+  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, C, ep, M, N, K, d_err);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <int BN, bool S>
+void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
+                     const CUtensorMap& mb, const CUtensorMap& mblo, const GemmOutput& C,
+                     const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
+                     cudaStream_t st) {
+  if (amn) {
+    if (bmn) launch_tc<BN, S, true, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc<BN, S, true, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  } else {
+    if (bmn) launch_tc<BN, S, false, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc<BN, S, false, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  }
+}
+
+}  // namespace
+
+void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
+                       const GemmOperand& B, int mode, int64_t* a_elems, int64_t* b_elems) {
+  *a_elems = 0;
+  *b_elems = 0;
+  if (mode != kGemmStrict || !tma_ok(A, batch) || !tma_ok(B, batch) || M == 0 || N == 0 ||
+      K == 0)
+    return;
+  *a_elems = A.trans ? operand_span(A, batch, K, M) : operand_span(A, batch, M, K);
+  *b_elems = B.trans ? operand_span(B, batch, N, K) : operand_span(B, batch, K, N);
+}
+
+int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
+                const GemmOperand& B, const GemmOutput& C, const GemmEpilogue& ep, int mode,
+                const GemmScratch& scratch, int* d_err, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || batch <= 0) return 0;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
+    throw CudaError("matmul dimension too large");
+  const bool tc = mode != kGemmExact && K > 0 && tma_ok(A, batch) && tma_ok(B, batch);
+  if (!tc) {
+    // (K == 0 lands here too: the loop adds nothing and the epilogue writes
+    // the empty product.)
+    dim3 grid((unsigned)ceil_div(N, 16), (unsigned)ceil_div(M, 16), (unsigned)batch);
+    gemm_simt_kernel<<<grid, dim3(16, 16), 0, st>>>(A, B, C, ep, (int)M, (int)N, (int)K);
+    TYSOR_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return 0;
+  }
+  const bool strict = mode == kGemmStrict;
+  const float* alo = A.ptr;
+  const float* blo = B.ptr;
+  if (strict) {
+    int64_t na, nb;
+    gemm_scratch_need(batch, M, N, K, A, B, mode, &na, &nb);
+    if (scratch.a_lo == nullptr || scratch.b_lo == nullptr || scratch.a_elems < na ||
+        scratch.b_elems < nb)
+      throw CudaError("strict matmul needs scratch for the split operands");
+    split_lo_kernel<<<elementwise_blocks(na / 4 + 1, 256), 256, 0, st>>>(A.ptr, scratch.a_lo, na);
+    split_lo_kernel<<<elementwise_blocks(nb / 4 + 1, 256), 256, 0, st>>>(B.ptr, scratch.b_lo, nb);
+    TYSOR_CUDA(cudaGetLastError());
+    g_launches.fetch_add(2, std::memory_order_relaxed);
+    alo = scratch.a_lo;
+    blo = scratch.b_lo;
+  }
+  const int BN = N <= 128 ? 128 : 256;
+  const bool amn = A.trans, bmn = !B.trans;
+  // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
+  const uint64_t a_in = amn ? M : K, a_out = amn ? K : M;
+  const uint64_t b_in = bmn ? N : K, b_out = bmn ? K : N;
+  const uint32_t a_box_in = amn ? 32 : BK, a_box_out = amn ? BK : BM;
+  const uint32_t b_box_in = bmn ? 32 : BK, b_box_out = bmn ? BK : (uint32_t)BN;
+  const CUtensorMapSwizzle a_sw = amn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle b_sw = bmn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap ma = make_map(A.ptr, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
+  CUtensorMap mb = make_map(B.ptr, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
+  CUtensorMap malo = ma, mblo = mb;
+  if (strict) {
+    malo = make_map(alo, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
+    mblo = make_map(blo, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
+  }
+  if (BN == 128) {
+    if (strict) dispatch_layout<128, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else dispatch_layout<128, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  } else {
+    if (strict) dispatch_layout<256, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else dispatch_layout<256, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  }
+  return 1;
+}
+
+}  // namespace tysor

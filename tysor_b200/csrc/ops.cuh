@@ -1,0 +1,112 @@
+// Bandwidth-bound kernels of the tysor CUDA backend: elementwise, row
+// reductions, gathers, masks, rotations, updates.  All fp32.  Each launcher
+// enqueues on `st` and returns immediately; kernels that can meet an invalid
+// index record it in the device error word `err` instead of trapping.
+#pragma once
+
+#include "common.cuh"
+
+namespace tysor {
+
+enum UnaryOp : int {
+  kUnaryCopy = 0,
+  kUnaryRelu = 1,
+  kUnarySilu = 2,
+  kUnaryScale = 3,  // x * param
+  kUnaryNeg = 4,
+};
+
+enum BinaryOp : int { kAdd = 0, kSub = 1, kMul = 2, kDiv = 3 };
+
+// Pattern fills of the reference initialisers: out[i] = ((i % mod) + add) / div.
+void launch_pattern(float* out, int64_t n, int mod, float add, float div, cudaStream_t st);
+void launch_fill(float* out, int64_t n, float value, cudaStream_t st);
+
+void launch_unary(int op, const float* x, float* out, int64_t n, float param, cudaStream_t st);
+void launch_binary_tt(int op, const float* a, const float* b, float* out, int64_t n,
+                      cudaStream_t st);
+void launch_binary_ts(int op, const float* a, float s, float* out, int64_t n, cudaStream_t st);
+void launch_binary_st(int op, float s, const float* b, float* out, int64_t n, cudaStream_t st);
+// dst = dst + src (gradient accumulation, tensor.rs:94-103 order).
+void launch_add_inplace(float* dst, const float* src, int64_t n, cudaStream_t st);
+// dst = dst + op(a, b)  /  dst = dst + op(a, s) (or op(s, a) when scalar_first):
+// the product is rounded first, then added, as the reference computes a
+// gradient term and then accumulates it.
+void launch_binary_tt_acc(int op, const float* a, const float* b, float* dst, int64_t n,
+                          cudaStream_t st);
+void launch_binary_ts_acc(int op, const float* a, float s, float* dst, int64_t n,
+                          int scalar_first, cudaStream_t st);
+// Gradient of the divisor of a tensor/tensor division (backward.rs:285-294):
+// v = -((g * lhs) / (rhs * rhs)); dst = accumulate ? dst + v : v.
+void launch_div_rhs_grad(const float* g, const float* lhs, const float* rhs, float* dst, int64_t n,
+                         int accumulate, cudaStream_t st);
+
+// Backward helpers.  `accumulate` adds the result into dx instead of storing.
+void launch_relu_backward(const float* out_act, const float* grad, float* dx, int64_t n,
+                          int accumulate, cudaStream_t st);
+void launch_silu_backward(const float* x, const float* grad, float* dx, int64_t n, int accumulate,
+                          cudaStream_t st);
+void launch_softmax_backward(const float* y, const float* grad, float* dx, int64_t n,
+                             int accumulate, cudaStream_t st);
+
+void launch_rms_norm(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st);
+void launch_rms_norm_gain(const float* x, const float* g, float* out, int64_t rows, int64_t width,
+                          float eps, cudaStream_t st);
+// dx (+)= dy * g;  dg = column sums of dy * x * rsqrt(mean(x^2)+eps).
+// `partial` needs rms_gain_partial_elems(rows, width) floats of scratch.
+int64_t rms_gain_partial_elems(int64_t rows, int64_t width);
+void launch_rms_norm_gain_backward(const float* x, const float* g, const float* dy, float* dx,
+                                   float* dg, float* partial, int64_t rows, int64_t width,
+                                   float eps, int accumulate_dx, int accumulate_dg,
+                                   cudaStream_t st);
+
+void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st);
+void launch_cross_entropy(const float* logits, const float* target, float* loss, int64_t rows,
+                          int64_t width, cudaStream_t st);
+void launch_cross_entropy_backward(const float* logits, const float* target, float* grad,
+                                   int64_t rows, int64_t width, int accumulate, cudaStream_t st);
+void launch_cross_entropy_labels(const float* logits, const float* labels, float* loss,
+                                 int64_t rows, int64_t width, int* err, cudaStream_t st);
+void launch_cross_entropy_labels_backward(const float* logits, const float* labels, float* grad,
+                                          int64_t rows, int64_t width, int accumulate, int* err,
+                                          cudaStream_t st);
+
+void launch_embedding(const float* idx, const float* weight, float* out, int64_t count,
+                      int64_t num, int64_t dim, int* err, cudaStream_t st);
+// Deterministic scatter-add: every weight row sums its tokens' gradient rows
+// in increasing token order (layers.rs:497-519), skipping out-of-range ids.
+// `work` needs embedding_backward_work_bytes(count, num) bytes.
+size_t embedding_backward_work_bytes(int64_t count, int64_t num);
+void launch_embedding_backward(const float* grad, const float* idx, float* wgrad, int64_t count,
+                               int64_t num, int64_t dim, void* work, int accumulate,
+                               cudaStream_t st);
+
+void launch_repeat_kv(const float* x, float* out, int64_t outer, int64_t heads, int64_t inner,
+                      int64_t repeats, cudaStream_t st);
+void launch_repeat_kv_backward(const float* grad, float* dx, int64_t outer, int64_t heads,
+                               int64_t inner, int64_t repeats, int accumulate, cudaStream_t st);
+void launch_causal_mask(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
+                        cudaStream_t st);
+void launch_causal_mask_backward(const float* grad, float* dx, int64_t outer, int64_t q, int64_t k,
+                                 int accumulate, cudaStream_t st);
+// `table` holds seq x half (cos, sin) pairs computed on the host.
+void launch_rope(const float* x, float* out, const float2* table, int64_t outer, int64_t seq,
+                 int64_t half, cudaStream_t st);
+void launch_rope_backward(const float* grad, float* dx, const float2* table, int64_t outer,
+                          int64_t seq, int64_t half, int accumulate, cudaStream_t st);
+// Exchange axes a < b of a row-major tensor of rank <= 8.
+void launch_transpose(const float* x, float* out, const int64_t* dims, int rank, int a, int b,
+                      int accumulate, cudaStream_t st);
+
+// Column sums of a [rows, width] gradient (bias gradient); `partial` needs
+// colsum_partial_elems(rows, width) floats.
+int64_t colsum_partial_elems(int64_t rows, int64_t width);
+void launch_colsum(const float* grad, float* out, float* partial, int64_t rows, int64_t width,
+                   int accumulate, cudaStream_t st);
+// Sum of all elements into out[0]; `partial` needs 1024 floats.
+void launch_reduce_sum(const float* x, float* out, float* partial, int64_t n, cudaStream_t st);
+
+// p = p - (lr * g), each product and difference rounded separately.
+void launch_sgd(float* p, const float* g, float lr, int64_t n, cudaStream_t st);
+
+}  // namespace tysor

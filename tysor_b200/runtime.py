@@ -1,0 +1,282 @@
+"""Host-side runtime of the CUDA backend: the Python mirror of the
+reference's backend entry points, driving libtysor_cuda.so.
+
+  run_cuda_module      <- run_metal_module / run_local_forward_module
+                          (src/backend/metal/runtime.rs:434-451,
+                           src/runtime/interpreter.rs:24-54)
+  backward_cuda_module <- run_backward_module (src/training/backward.rs:382-399)
+  train_cuda_module    <- run_train_module (src/training/executor.rs:764-816)
+
+Each returns the values and also formats them exactly as the reference
+prints them (tensor.rs:36-69, backward.rs:385-397, executor.rs:794-814), so
+a harness can diff the text.  There is no fallback path: every tensor
+operation runs in libtysor_cuda on an sm_100 device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import native
+from .graph import Graph
+from .native import check, fptr
+
+MATMUL_MODES = {"strict": 0, "fast": 1, "exact": 2}
+
+
+class CudaContext:
+    """A device, its stream and scratch (tysor_cuda_context_new)."""
+
+    def __init__(self, device: int = 0, matmul: str = "strict"):
+        self._lib = native.lib()
+        self.handle = self._lib.tysor_cuda_context_new(int(device))
+        check(self.handle, "tysor_cuda_context_new")
+        self.device = device
+        self.set_matmul_mode(matmul)
+
+    def set_matmul_mode(self, mode: str) -> None:
+        check(self._lib.tysor_cuda_set_matmul_mode(self.handle, MATMUL_MODES[mode]), "set_matmul_mode")
+
+    def synchronize(self) -> None:
+        check(self._lib.tysor_cuda_synchronize(self.handle), "synchronize")
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.tysor_cuda_context_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class DeviceBuffer:
+    """An fp32 device buffer (tysor_cuda_buffer_*)."""
+
+    def __init__(self, ctx: CudaContext, handle, count: int):
+        self.ctx = ctx
+        self.handle = handle
+        self.count = count
+
+    @classmethod
+    def from_array(cls, ctx: CudaContext, arr) -> "DeviceBuffer":
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        h = native.lib().tysor_cuda_buffer_new_with_data(ctx.handle, fptr(a), a.size)
+        check(h, "buffer_new_with_data")
+        return cls(ctx, h, a.size)
+
+    @classmethod
+    def zeros(cls, ctx: CudaContext, count: int) -> "DeviceBuffer":
+        h = native.lib().tysor_cuda_buffer_new_zeroed(ctx.handle, int(count))
+        check(h, "buffer_new_zeroed")
+        return cls(ctx, h, int(count))
+
+    def read(self, count: Optional[int] = None) -> np.ndarray:
+        n = self.count if count is None else count
+        out = np.empty(n, dtype=np.float32)
+        check(native.lib().tysor_cuda_buffer_read(self.handle, fptr(out), n), "buffer_read")
+        return out
+
+    def write(self, arr) -> None:
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        check(native.lib().tysor_cuda_buffer_write(self.handle, fptr(a), a.size), "buffer_write")
+
+    def free(self) -> None:
+        if self.handle:
+            native.lib().tysor_cuda_buffer_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+@dataclass
+class HostTensor:
+    shape: List[int]
+    data: np.ndarray
+    dtype: str = "float32"
+
+
+def format_tensor(t: HostTensor) -> str:
+    """tensor.rs:48-69 print_tensor_body."""
+    vals = ", ".join(f"{float(v):.4f}" for v in t.data)
+    return f"shape=[{', '.join(str(d) for d in t.shape)}] dtype={t.dtype}\nvalues=[{vals}]"
+
+
+class CudaGraphExecutor:
+    """The device-resident executor for one lowered graph."""
+
+    def __init__(self, ctx: CudaContext, graph: Graph, shapes: Dict[str, Sequence[int]],
+                 inputs: Optional[Dict[str, np.ndarray]] = None,
+                 parameters: Optional[Dict[str, np.ndarray]] = None):
+        self.ctx = ctx
+        self.graph = graph
+        self._lib = native.lib()
+        self.handle = self._lib.tysor_cuda_graph_new(ctx.handle, graph.to_text().encode())
+        check(self.handle, "graph_new")
+        for name, dims in shapes.items():
+            self.set_shape(name, dims)
+        for name, arr in (inputs or {}).items():
+            self.set_input(name, arr)
+        for name, arr in (parameters or {}).items():
+            self.set_parameter(name, arr)
+
+    def set_shape(self, name: str, dims: Sequence[int]) -> None:
+        d = (ctypes.c_int64 * len(dims))(*[int(x) for x in dims])
+        check(self._lib.tysor_cuda_graph_set_shape(self.handle, name.encode(), d, len(dims)), "set_shape")
+
+    def set_input(self, name: str, arr) -> None:
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        check(self._lib.tysor_cuda_graph_set_input(self.handle, name.encode(), fptr(a), a.size), "set_input")
+
+    def set_parameter(self, name: str, arr) -> None:
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        check(self._lib.tysor_cuda_graph_set_parameter(self.handle, name.encode(), fptr(a), a.size),
+              "set_parameter")
+
+    def set_capture(self, enable: bool) -> None:
+        check(self._lib.tysor_cuda_graph_set_capture(self.handle, bool(enable)), "set_capture")
+
+    def enable_allreduce(self, enable: bool = True) -> None:
+        check(self._lib.tysor_cuda_graph_enable_allreduce(self.handle, bool(enable)), "enable_allreduce")
+
+    # --- execution -----------------------------------------------------------
+    def run(self) -> HostTensor:
+        check(self._lib.tysor_cuda_graph_run(self.handle), "run")
+        if not self.graph.outputs:
+            raise native.NativeError("Entry function did not return a value")
+        if len(self.graph.outputs) != 1:
+            raise native.NativeError("Runtime interpreter currently supports a single return value")
+        return self.value(self.graph.outputs[0])
+
+    def backward(self) -> List[Tuple[str, HostTensor]]:
+        """backward.rs:382-399: gradient of every graph parameter (zeros if none)."""
+        check(self._lib.tysor_cuda_graph_backward(self.handle), "backward")
+        out = []
+        for v in self.graph.parameters():
+            g = self.value_grad(v.id)
+            if g is None:
+                t = self.value(v.id)
+                g = HostTensor(t.shape, np.zeros_like(t.data), t.dtype)
+            out.append((f"{v.name}_grad", g))
+        return out
+
+    def train(self, iterations: Optional[int] = None, lr: Optional[float] = None) -> List[float]:
+        it = self.graph.iterations if iterations is None else int(iterations)
+        rate = self.graph.lr if lr is None else float(lr)
+        if self.graph.optimizer != "sgd":
+            raise native.NativeError("Train executor currently supports only optimizer='sgd'")
+        losses = np.zeros(max(it, 1), dtype=np.float32)
+        check(self._lib.tysor_cuda_graph_train(self.handle, it, rate, fptr(losses)), "train")
+        return [float(x) for x in losses[:it]]
+
+    # --- results -------------------------------------------------------------
+    def shape(self, value_id: int) -> List[int]:
+        r = self._lib.tysor_cuda_graph_value_rank(self.handle, int(value_id))
+        check(r >= 0, "value_rank")
+        d = (ctypes.c_int64 * max(r, 1))()
+        check(self._lib.tysor_cuda_graph_value_shape(self.handle, int(value_id), d), "value_shape")
+        return [int(d[i]) for i in range(r)]
+
+    def value(self, value_id: int) -> HostTensor:
+        s = self.shape(value_id)
+        out = np.empty(int(np.prod(s, dtype=np.int64)), dtype=np.float32)
+        check(self._lib.tysor_cuda_graph_read_value(self.handle, int(value_id), fptr(out), out.size), "read_value")
+        return HostTensor(s, out)
+
+    def value_grad(self, value_id: int) -> Optional[HostTensor]:
+        s = self.shape(value_id)
+        out = np.empty(int(np.prod(s, dtype=np.int64)), dtype=np.float32)
+        if not self._lib.tysor_cuda_graph_read_value_grad(self.handle, int(value_id), fptr(out), out.size):
+            return None
+        return HostTensor(s, out)
+
+    def parameter_names(self) -> List[str]:
+        n = self._lib.tysor_cuda_graph_num_parameters(self.handle)
+        check(n >= 0, "num_parameters")
+        return [self._lib.tysor_cuda_graph_parameter_name(self.handle, i).decode() for i in range(n)]
+
+    def parameter(self, name: str) -> np.ndarray:
+        n = self._lib.tysor_cuda_graph_parameter_count(self.handle, name.encode())
+        out = np.empty(n, dtype=np.float32)
+        check(self._lib.tysor_cuda_graph_read_parameter(self.handle, name.encode(), fptr(out), n), "read_parameter")
+        return out
+
+    def parameter_grad(self, name: str) -> np.ndarray:
+        n = self._lib.tysor_cuda_graph_parameter_count(self.handle, name.encode())
+        out = np.empty(n, dtype=np.float32)
+        check(self._lib.tysor_cuda_graph_read_parameter_grad(self.handle, name.encode(), fptr(out), n),
+              "read_parameter_grad")
+        return out
+
+    def parameters(self) -> Dict[str, np.ndarray]:
+        return {n: self.parameter(n) for n in self.parameter_names()}
+
+    def launch_count(self) -> int:
+        return int(self._lib.tysor_cuda_graph_launch_count(self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            self._lib.tysor_cuda_graph_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---- reference-shaped entry points --------------------------------------------------
+
+def run_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, echo: bool = True) -> HostTensor:
+    ex = CudaGraphExecutor(ctx, graph, shapes, inputs)
+    try:
+        out = ex.run()
+    finally:
+        ex.close()
+    if echo:
+        print("\n--- Execution Output ---")
+        print(format_tensor(out))
+        print("------------------------")
+    return out
+
+
+def backward_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, echo: bool = True):
+    ex = CudaGraphExecutor(ctx, graph, shapes, inputs)
+    try:
+        grads = ex.backward()
+    finally:
+        ex.close()
+    if echo:
+        print("\n--- Gradient Output ---")
+        for name, t in grads:
+            print(f"{name}:")
+            print(format_tensor(t))
+        print("-----------------------")
+    return grads
+
+
+def train_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, parameters=None,
+                      echo: bool = True):
+    ex = CudaGraphExecutor(ctx, graph, shapes, inputs, parameters)
+    try:
+        losses = ex.train()
+        params = ex.parameters()
+    finally:
+        ex.close()
+    if echo:
+        print("\n--- Training Output ---")
+        print("backend=cuda")
+        for i, loss in enumerate(losses):
+            print(f"step={i + 1} loss={loss:.6f} params={len(params)}")
+        print("-----------------------")
+    return losses, params
