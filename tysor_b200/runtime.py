@@ -15,6 +15,7 @@ operation runs in libtysor_cuda on an sm_100 device.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -28,14 +29,21 @@ MATMUL_MODES = {"strict": 0, "fast": 1, "exact": 2}
 
 
 class CudaContext:
-    """A device, its stream and scratch (tysor_cuda_context_new)."""
+    """A device, its stream and scratch (tysor_cuda_context_new).
+
+    Buffers and graph executors made on a context must be released before
+    it; `close()` releases any that are still open."""
 
     def __init__(self, device: int = 0, matmul: str = "strict"):
         self._lib = native.lib()
         self.handle = self._lib.tysor_cuda_context_new(int(device))
         check(self.handle, "tysor_cuda_context_new")
         self.device = device
+        self._children = weakref.WeakSet()
         self.set_matmul_mode(matmul)
+
+    def _adopt(self, child) -> None:
+        self._children.add(child)
 
     def set_matmul_mode(self, mode: str) -> None:
         check(self._lib.tysor_cuda_set_matmul_mode(self.handle, MATMUL_MODES[mode]), "set_matmul_mode")
@@ -45,6 +53,8 @@ class CudaContext:
 
     def close(self) -> None:
         if self.handle:
+            for child in list(self._children):
+                child.close()
             self._lib.tysor_cuda_context_free(self.handle)
             self.handle = None
 
@@ -62,6 +72,7 @@ class DeviceBuffer:
         self.ctx = ctx
         self.handle = handle
         self.count = count
+        ctx._adopt(self)
 
     @classmethod
     def from_array(cls, ctx: CudaContext, arr) -> "DeviceBuffer":
@@ -87,9 +98,11 @@ class DeviceBuffer:
         check(native.lib().tysor_cuda_buffer_write(self.handle, fptr(a), a.size), "buffer_write")
 
     def free(self) -> None:
-        if self.handle:
+        if self.handle and self.ctx.handle:
             native.lib().tysor_cuda_buffer_free(self.handle)
-            self.handle = None
+        self.handle = None
+
+    close = free
 
     def __del__(self):
         try:
@@ -122,6 +135,7 @@ class CudaGraphExecutor:
         self._lib = native.lib()
         self.handle = self._lib.tysor_cuda_graph_new(ctx.handle, graph.to_text().encode())
         check(self.handle, "graph_new")
+        ctx._adopt(self)
         for name, dims in shapes.items():
             self.set_shape(name, dims)
         for name, arr in (inputs or {}).items():
@@ -224,9 +238,15 @@ class CudaGraphExecutor:
         return int(self._lib.tysor_cuda_graph_launch_count(self.handle))
 
     def close(self) -> None:
-        if self.handle:
+        if self.handle and self.ctx.handle:
             self._lib.tysor_cuda_graph_free(self.handle)
-            self.handle = None
+        self.handle = None
+
+    def upload_input(self, name: str, arr) -> None:
+        """Host -> device copy of a graph input, enqueued on the stream (pinned
+        host memory makes it asynchronous); the graph must have run once."""
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        check(self._lib.tysor_cuda_graph_upload_input(self.handle, name.encode(), fptr(a), a.size), "upload_input")
 
     def __del__(self):
         try:
