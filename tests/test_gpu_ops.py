@@ -26,6 +26,17 @@ def close(got, want, rtol=1e-5):
     assert float(err.max(initial=0.0)) <= rtol, float(err.max())
 
 
+def close_sums(got, want, l1, rtol=1e-5):
+    """Sums that cancel are judged against the size of their terms: the
+    device (tree order) and the oracle (row order) both round within
+    n * 2^-24 * sum|terms|; the bar is rtol * sum|terms| per output."""
+    got = np.asarray(got, np.float64).reshape(-1)
+    want = np.asarray(want, np.float64).reshape(-1)
+    l1 = np.asarray(l1, np.float64).reshape(-1)
+    err = np.abs(got - want) / np.maximum(l1, 1e-30)
+    assert float(err.max(initial=0.0)) <= rtol, float(err.max())
+
+
 @pytest.fixture
 def dev(cuda_ctx):
     from tysor_b200 import native
@@ -164,9 +175,9 @@ def test_bias_grad_and_reduce_sum(dev):
     g = rnd((3001, 77), 15)
     Gb, DB, S = dev.buf(g), dev.zeros(77), dev.zeros(1)
     dev.ok(dev.lib.tysor_cuda_dispatch_bias_grad(dev.h, Gb.handle, DB.handle, 3001, 77, False))
-    close(DB.read(), L.bias_grad(T(g.shape, g)).data, 1e-5)
+    close_sums(DB.read(), L.bias_grad(T(g.shape, g)).data, np.abs(g).sum(axis=0))
     dev.ok(dev.lib.tysor_cuda_dispatch_reduce_sum(dev.h, Gb.handle, S.handle, g.size))
-    close(S.read(), [L.tensor_sum(T([g.size], g))], 1e-4)
+    close_sums(S.read(), [L.tensor_sum(T([g.size], g))], [np.abs(g).sum()])
 
 
 def test_activation_backwards(dev):
@@ -210,7 +221,8 @@ def test_rms_norm_softmax_silu_sweep(dev, rows, width):
                                                               DG.handle, rows, width, 1e-6, False))
     wdx, wdg = L.rms_norm_gain_backward(xt, T([width], gain), T(dy.shape, dy), 1e-6)
     np.testing.assert_array_equal(DX.read(), wdx.data)
-    close(DG.read(), wdg.data, 1e-4 if rows > 1000 else 1e-5)
+    scale = 1.0 / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-6)
+    close_sums(DG.read(), wdg.data, np.abs(dy * x * scale).sum(axis=0))
 
 
 @pytest.mark.parametrize("rows,width", [(2, 3), (17, 1000), (8192, 32000)])

@@ -1,0 +1,71 @@
+"""Summaries of ncu output for profiles/.
+
+    python -m tysor_b200.profiling launches gpurun_out/launches.csv
+        per-kernel launches, total device time and share of a
+        `ncu --metrics gpu__time_duration.sum --csv` launch list
+    python -m tysor_b200.profiling report prof.ncu-rep
+        the headline metrics of an `ncu --set full` capture
+"""
+from __future__ import annotations
+
+import collections
+import csv
+import io
+import subprocess
+import sys
+
+UNIT_NS = {"ns": 1.0, "nsecond": 1.0, "us": 1e3, "usecond": 1e3, "ms": 1e6, "msecond": 1e6}
+
+
+def launches(path: str) -> str:
+    text = open(path).read().splitlines()
+    start = next(i for i, line in enumerate(text) if line.startswith('"ID"'))
+    rows = list(csv.reader(text[start:]))
+    hdr = rows[0]
+    ki, mi, ui, vi = (hdr.index(k) for k in ("Kernel Name", "Metric Name", "Metric Unit", "Metric Value"))
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for r in rows[1:]:
+        if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
+            continue
+        name = r[ki].split("(")[0].replace("(anonymous namespace)::", "")
+        agg[name][0] += 1
+        agg[name][1] += float(r[vi].replace(",", "")) * UNIT_NS.get(r[ui], 1.0)
+    total = sum(v[1] for v in agg.values())
+    out = [f"{sum(v[0] for v in agg.values())} launches, {total / 1e6:.2f} ms total (cold-cache, serialised)",
+           "", "| kernel | launches | total ms | share |", "|---|---:|---:|---:|"]
+    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        out.append(f"| `{name}` | {n} | {t / 1e6:.3f} | {100 * t / total:.1f}% |")
+    return "\n".join(out)
+
+
+REPORT_KEYS = [
+    "gpu__time_duration.sum", "sm__cycles_elapsed.avg.per_second",
+    "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active",
+    "dram__bytes_read.sum", "dram__bytes_write.sum",
+    "dram__throughput.avg.pct_of_peak_sustained_elapsed",
+    "lts__t_sector_hit_rate.pct", "l1tex__throughput.avg.pct_of_peak_sustained_active",
+    "launch__registers_per_thread", "launch__occupancy_limit_shared_mem",
+    "smsp__average_warps_issue_stalled_long_scoreboard_per_issue_active.ratio",
+    "sm__warps_active.avg.pct_of_peak_sustained_active",
+]
+
+
+def report(path: str) -> str:
+    raw = subprocess.run(["ncu", "-i", path, "--page", "raw", "--csv"], capture_output=True, text=True,
+                         check=True).stdout
+    rows = list(csv.reader(io.StringIO(raw)))
+    hdr, units = rows[0], rows[1]
+    out = []
+    for vals in rows[2:]:
+        name = vals[hdr.index("Kernel Name")] if "Kernel Name" in hdr else "kernel"
+        out.append(f"kernel: `{name.split('(')[0]}`")
+        for k in REPORT_KEYS:
+            if k in hdr:
+                i = hdr.index(k)
+                out.append(f"- {k}: {vals[i]} {units[i]}")
+    return "\n".join(out)
+
+
+if __name__ == "__main__":
+    kind, path = sys.argv[1], sys.argv[2]
+    print(launches(path) if kind == "launches" else report(path))
