@@ -243,6 +243,21 @@ int64_t tysor_cuda_graph_launch_count(void* graph);
  * (default on for train). */
 bool tysor_cuda_graph_set_capture(void* graph, bool enable);
 
+/* ---- matmul without allocation ---------------------------------------------
+ * No counterpart in the reference.  For callers that must not allocate
+ * device memory (code running inside another framework's reserved memory
+ * pool, or a hot path where cudaMalloc's implicit synchronisation is not
+ * allowed): C[m,n] = A[m,k] . B[k,n], row-major fp32 device pointers, strict
+ * 3xTF32, enqueued on `stream` (a cudaStream_t; NULL = default stream).  It
+ * needs no context and allocates nothing: the split operands live in a fixed
+ * 32 MiB device array inside the library, so A and B together may span at
+ * most 8,388,608 elements (larger calls fail with an error).  The first call
+ * on each device looks up that array's address; make it before any stream
+ * capture.  All calls on a device share the array, so calls that overlap on
+ * the GPU race; order them on one stream. */
+bool tysor_cuda_matmul_noalloc(void* stream, uint32_t m, uint32_t n, uint32_t k, const float* a,
+                               const float* b, float* c);
+
 /* ---- data-parallel gradient all-reduce (NCCL over NVLink) ----------------
  * No reference counterpart: the reference has no multi-device code. */
 bool tysor_cuda_nccl_get_unique_id(uint8_t out_id[128]);

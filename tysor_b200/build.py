@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libtysor_cuda.so")
 
-SOURCES = ["gemm.cu", "ops.cu", "bridge.cu", "executor.cu", "comm.cu"]
+SOURCES = ["gemm.cu", "ops.cu", "bridge.cu", "executor.cu", "comm.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++20", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off",
           "--expt-relaxed-constexpr", "-I" + os.path.join(os.path.dirname(HERE), "include")]
