@@ -902,8 +902,9 @@ def backward_report(graph, shapes, inputs=None) -> List[Tuple[str, Tensor]]:
 
 # ---- --train ------------------------------------------------------------------
 
-def compute_parameter_gradients(graph, values, oid, parameters) -> Dict[str, Tensor]:
-    """training/executor.rs:563-743."""
+def compute_parameter_gradients(graph, values, oid, parameters, value_grads=None) -> Dict[str, Tensor]:
+    """training/executor.rs:563-743.  If `value_grads` is a dict it receives
+    the per-value gradients of the walk as well."""
     obj = _tensor(values.get(oid))
     vgrads: Dict[int, Tensor] = {oid: Tensor(list(obj.shape), np.ones(obj.data.size, np.float32), obj.dtype)}
     pgrads: Dict[str, Tensor] = {}
@@ -1013,6 +1014,8 @@ def compute_parameter_gradients(graph, values, oid, parameters) -> Dict[str, Ten
                     raise OracleError("Unsupported activation in train backward")
             else:
                 raise OracleError("Unsupported apply in train backward")
+    if value_grads is not None:
+        value_grads.update(vgrads)
     return pgrads
 
 
@@ -1045,13 +1048,14 @@ def train(graph, shapes, inputs=None, parameters: Optional[Dict[str, Tensor]] = 
     return losses, params
 
 
-def train_step_grads(graph, shapes, inputs=None, parameters=None):
+def train_step_grads(graph, shapes, inputs=None, parameters=None, value_grads=None):
     """One forward + parameter-gradient pass without the update (used to
-    check the device backward in isolation).  Returns (values, grads, params)."""
+    check the device backward in isolation).  Returns (values, grads, params);
+    `value_grads`, if a dict, receives the per-value gradients."""
     params: Dict[str, Tensor] = {} if parameters is None else {k: v.clone() for k, v in parameters.items()}
     oid = graph.objective_id()
     values = _forward(graph, shapes, inputs, params)
-    grads = compute_parameter_gradients(graph, values, oid, params)
+    grads = compute_parameter_gradients(graph, values, oid, params, value_grads)
     return values, grads, params
 
 

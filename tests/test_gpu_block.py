@@ -66,3 +66,63 @@ def test_block_forward_backward_and_sgd(cuda_ctx):
     for name, t in want_params.items():
         assert frob(ex.parameter(name), t.data) < 1e-5, name
     ex.close()
+
+
+@pytest.mark.parametrize("shape", [[2, 3, 64, 32], [1, 2, 1024, 32]])
+def test_attention_core_with_fused_scale_and_masked_softmax(cuda_ctx, shape):
+    """softmax(causal_mask(scale(q . k^T, c))) . v, training semantics: the
+    executor folds the scale into the GEMM's alpha and runs mask+softmax as
+    one kernel (forward and backward); values and the gradients reaching q,
+    k and v must match the op-by-op oracle.  Row widths that are multiples
+    of 1024 take the register-resident softmax."""
+    from tysor_b200.graph import GraphBuilder
+    from tysor_b200.runtime import CudaGraphExecutor
+    b = GraphBuilder()
+    q, k, v = b.param("q"), b.param("k"), b.param("v")
+    kt = b.call("transpose", k, 2, 3)
+    s = b.call("scale", b.call("matmul", q, kt), 0.17)
+    p = b.let("p", b.apply(b.ctor("Softmax"), b.call("causal_mask", s)))
+    out = b.let("out", b.call("matmul", p, v))
+    b.ret(out)
+    b.train(objective="out", lr=0.0)
+    g = b.build()
+    rng = np.random.default_rng(3)
+    ins = {n: rng.standard_normal(shape).astype(np.float32) for n in ("q", "k", "v")}
+    shapes = {n: shape for n in ins}
+    vgrads = {}
+    values, _, _ = L.train_step_grads(g, shapes, inputs=ins, value_grads=vgrads)
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins)
+    ex.train(1, 0.0)
+    assert frob(ex.value(g.named["p"]).data, values[g.named["p"]][1].data) < 1e-5
+    assert frob(ex.value(out).data, values[out][1].data) < 1e-5
+    for name in ("q", "k", "v"):
+        vid = g.named[name]
+        assert frob(ex.value_grad(vid).data, vgrads[vid].data) < 1e-5, name
+    ex.close()
+
+
+def test_block_medium_uses_transposed_operand_copies(cuda_ctx):
+    """A size at which the executor transposes the M/N-contiguous operands of
+    the weight-gradient and attention matmuls before the GEMM (operand
+    elements x 2000 <= GEMM FLOPs): gradients and the updated parameters must
+    still match the oracle, and nothing may be NaN."""
+    from tysor_b200.runtime import CudaGraphExecutor
+    cfg = dict(batch=1, seq=512, d_model=512, n_heads=4, n_kv_heads=2, hidden=1024, eps=1e-6, lr=1e-5)
+    g = llama_block(**cfg)
+    T = cfg["seq"]
+    shapes = {"x": [T, cfg["d_model"]]}
+    x = np.random.default_rng(2).standard_normal((T, cfg["d_model"])).astype(np.float32)
+    params = params_for(g, seed=9)
+    oparams = {k: L.Tensor(list(v.shape), v.reshape(-1).copy()) for k, v in params.items()}
+    L.set_threads(16)
+    values, grads, _ = L.train_step_grads(g, shapes, inputs={"x": x}, parameters=oparams)
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs={"x": x}, parameters=params)
+    losses = ex.train(1, 0.0)
+    assert np.isfinite(losses).all()
+    out_id = g.outputs[0]
+    assert frob(ex.value(out_id).data, values[out_id][1].data) < 1e-5
+    for name, gt in grads.items():
+        got = ex.parameter_grad(name)
+        assert np.isfinite(got).all(), name
+        assert frob(got, gt.data) < 1e-4, name
+    ex.close()

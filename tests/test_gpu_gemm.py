@@ -142,3 +142,39 @@ def test_dispatch_matmul_metal_signature(cuda_ctx):
     X, W, O = DeviceBuffer.from_array(cuda_ctx, x), DeviceBuffer.from_array(cuda_ctx, w), DeviceBuffer.zeros(cuda_ctx, 8)
     native.check(native.lib().tysor_cuda_dispatch_matmul(cuda_ctx.handle, X.handle, W.handle, O.handle, 2, 4, 3))
     np.testing.assert_array_equal(O.read().reshape(2, 4), oracle_mm(x, w))
+
+
+def test_two_sm_pair_kernel_opt_in():
+    """The cta_group::2 (cluster pair) form, enabled with
+    TYSOR_CUDA_GEMM_2SM=1, against the oracle for both operand layouts; run
+    in a child process because the switch is read at load time."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import sys, numpy as np
+sys.path[:0] = [".", "oracle"]
+import local as L
+from tysor_b200 import native
+from tysor_b200.runtime import CudaContext, DeviceBuffer
+ctx = CudaContext(0)
+lib = native.lib()
+rng = np.random.default_rng(4)
+for (m, n, k, ta, tb) in [(512, 512, 256, False, False), (640, 768, 96, False, True), (300, 520, 64, True, False)]:
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    A = DeviceBuffer.from_array(ctx, np.ascontiguousarray(a.T) if ta else a)
+    B = DeviceBuffer.from_array(ctx, np.ascontiguousarray(b.T) if tb else b)
+    C = DeviceBuffer.zeros(ctx, m * n)
+    native.check(lib.tysor_cuda_dispatch_matmul_ex(ctx.handle, 1, m, n, k, A.handle, ta, m if ta else k, 0,
+                 B.handle, tb, k if tb else n, 0, C.handle, n, 0, None, 1.0, False, False))
+    got = C.read().reshape(m, n).astype(np.float64)
+    want = L.matmul(L.Tensor([m, k], a.reshape(-1).copy()), L.Tensor([k, n], b.reshape(-1).copy())).data.reshape(m, n)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err < 1e-5, (m, n, k, ta, tb, err)
+print("ok")
+'''
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, TYSOR_CUDA_GEMM_2SM="1")
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr

@@ -77,13 +77,26 @@ enum GemmMode : int {
   kGemmExact = 2,   // CUDA-core fp32, products and sums in k order (bit-exact)
 };
 
-// Scratch the strict-mode GEMM needs: one "lo" copy of each operand.
+// Scratch the strict-mode GEMM needs: one "lo" copy of each operand, laid
+// out like the operand.  With `presplit` set the copies already hold
+// lo(A), lo(B) and the launcher does not recompute them.
 struct GemmScratch {
   float* a_lo;
   float* b_lo;
   int64_t a_elems;
   int64_t b_elems;
+  int presplit = 0;
 };
+
+// Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
+extern bool g_two_sm_enabled;
+
+// lo(x) = x - tf32_trunc(x) over n contiguous elements.
+void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st);
+// Per batch item b: hi_t[b][c][r] = x[b][r][c] and lo_t = lo(hi_t) (lo_t may
+// be null), for a contiguous [batch][rows][cols] x.
+void launch_split_transpose(const float* x, float* hi_t, float* lo_t, int64_t batch, int64_t rows,
+                            int64_t cols, cudaStream_t st);
 
 // Returns the number of elements of scratch each operand needs in strict
 // mode (0 when the call runs on the CUDA-core path).

@@ -133,6 +133,7 @@ struct Executor {
   Slot* scratch = nullptr;
   void* arena = nullptr;
   bool setup_done = false;
+  bool stepped = false;  // a train step of this plan has run eagerly
   bool capture = true;
   bool allreduce = false;
   cudaGraphExec_t exec = nullptr;
@@ -160,9 +161,15 @@ struct Executor {
     vgrad.clear();
     params.clear();
     param_order.clear();
+    prep_cache.clear();
+    deferred_matmul.clear();
+    folded_scale.clear();
+    masked_input.clear();
+    grad_alias.clear();
     loss = grad_block = scratch = nullptr;
     scratch_floats = 0;
     setup_done = false;
+    stepped = false;
   }
 
   Slot* alloc(size_t n) {
@@ -333,36 +340,112 @@ struct Executor {
   }
 
   // ---- GEMM step --------------------------------------------------------------
+  // A matmul operand as the tensor-core kernel will read it: `hi` holds the
+  // values (possibly a transposed copy), `lo` (strict mode) their low parts
+  // in the same layout.
+  struct Prepared {
+    Slot* hi = nullptr;
+    Slot* lo = nullptr;
+    bool trans = false;
+    int64_t ld = 0, bs = 0;
+  };
+  std::map<std::tuple<Slot*, bool, int64_t, int64_t, int64_t, int64_t, int64_t>, std::pair<Slot*, Slot*>>
+      prep_cache;
+  int plan_matmul_mode = kGemmStrict;
+
+  static bool tma_aligned(int64_t ld, int64_t bs, int batch) {
+    return (ld % 4) == 0 && (batch == 1 || (bs % 4) == 0);
+  }
+
+  // Prepares operand X (A if is_a, else B) of a GEMM once per step: the
+  // low-part split for strict mode, and for an M/N-contiguous operand that
+  // is small next to the GEMM's work, a transposed copy so the kernel reads
+  // both operands K-major (its fastest form).  Values are immutable within
+  // a step once produced, so one preparation serves every later GEMM that
+  // reads the same operand the same way.
+  Prepared prepare(std::vector<StepFn>& out, Slot* x, bool is_a, bool trans, int64_t ld, int64_t bs,
+                   int batch, int64_t M, int64_t N, int64_t K) {
+    const int64_t R = is_a ? (trans ? K : M) : (trans ? N : K);
+    const int64_t C = is_a ? (trans ? M : K) : (trans ? K : N);
+    const bool mn_major = is_a ? trans : !trans;
+    const bool contiguous = ld == C && (batch == 1 || bs == R * C);
+    const double flops = 2.0 * batch * (double)M * N * K;
+    const bool transpose = mn_major && contiguous && (double)batch * R * C * 2000.0 <= flops;
+    const bool strict = plan_matmul_mode == kGemmStrict;
+    Prepared p;
+    p.hi = x;
+    p.trans = trans;
+    p.ld = ld;
+    p.bs = bs;
+    if (!transpose && !strict) return p;
+    // The cache holds memory objects (a copy of the stored [R][C] matrix,
+    // transposed or not, and its low part); how a GEMM reads them (its
+    // trans flag) is rebuilt for each caller.
+    auto key = std::make_tuple(x, transpose, R, C, ld, bs, (int64_t)batch);
+    auto it = prep_cache.find(key);
+    std::pair<Slot*, Slot*> mem;
+    if (it != prep_cache.end()) {
+      mem = it->second;
+    } else if (transpose) {
+      const int64_t n = (int64_t)batch * R * C;
+      mem = {alloc((size_t)n), strict ? alloc((size_t)n) : nullptr};
+      Slot *src = x, *hi = mem.first, *lo = mem.second;
+      out.push_back([=](cudaStream_t st) {
+        launch_split_transpose(src->p, hi->p, lo ? lo->p : nullptr, batch, R, C, st);
+      });
+      prep_cache[key] = mem;
+    } else {
+      const int64_t span = (int64_t)(batch - 1) * bs + (R - 1) * ld + C;
+      mem = {x, alloc((size_t)span)};
+      Slot *src = x, *lo = mem.second;
+      out.push_back([=](cudaStream_t st) { launch_split_lo(src->p, lo->p, span, st); });
+      prep_cache[key] = mem;
+    }
+    p.hi = mem.first;
+    p.lo = mem.second;
+    if (transpose) {  // the copy is stored [C][R]
+      p.trans = !trans;
+      p.ld = R;
+      p.bs = R * C;
+    }
+    return p;
+  }
+
   void gemm_step(std::vector<StepFn>& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
                  Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu) {
-    // Scratch for the split operands (strict mode): bound by the operand spans.
-    const int64_t span_a = (batch - 1) * sa + (ta ? (K - 1) * lda + M : (M - 1) * lda + K);
-    const int64_t span_b = (batch - 1) * sb + (tb ? (N - 1) * ldb + K : (K - 1) * ldb + N);
-    need_scratch((size_t)(span_a + span_b + 128));
+    Prepared pa, pb;
+    pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
+    pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
+    const bool tc = plan_matmul_mode != kGemmExact && K > 0 && tma_aligned(lda, sa, batch) &&
+                    tma_aligned(ldb, sb, batch);
+    if (tc) {
+      pa = prepare(out, a, true, ta, lda, sa, batch, M, N, K);
+      pb = prepare(out, b, false, tb, ldb, sb, batch, M, N, K);
+    }
     Context* cx = ctx;
-    Slot** scr = &scratch;
+    const int mode_now = plan_matmul_mode;
     out.push_back([=](cudaStream_t st) {
-      GemmOperand A{a->p, ta, lda, sa};
-      GemmOperand B{b->p, tb, ldb, sb};
+      GemmOperand A{pa.hi->p, pa.trans, pa.ld, pa.bs};
+      GemmOperand B{pb.hi->p, pb.trans, pb.ld, pb.bs};
       GemmOutput O{c->p, ldc, sc};
       GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0};
-      GemmScratch s{nullptr, nullptr, 0, 0};
-      int64_t na = 0, nb = 0;
-      gemm_scratch_need(batch, M, N, K, A, B, cx->matmul_mode, &na, &nb);
-      if (na + nb > 0) {
-        const int64_t pad = (na + 63) & ~(int64_t)63;
-        s.a_lo = (*scr)->p;
-        s.b_lo = (*scr)->p + pad;
-        s.a_elems = na;
-        s.b_elems = nb;
+      GemmScratch s{nullptr, nullptr, 0, 0, 1};
+      if (pa.lo && pb.lo) {
+        s.a_lo = pa.lo->p;
+        s.b_lo = pb.lo->p;
+        s.a_elems = (int64_t)pa.lo->n;
+        s.b_elems = (int64_t)pb.lo->n;
       }
-      gemm_launch(batch, M, N, K, A, B, O, ep, cx->matmul_mode, s, cx->d_err, st);
+      gemm_launch(batch, M, N, K, A, B, O, ep, mode_now, s, cx->d_err, st);
     });
   }
 
-  // C = lhs . rhs for rank 2, or batched over equal leading dims.
-  HVal plan_matmul(const HVal& l, const HVal& r, std::vector<StepFn>& out) {
+  // C = alpha * lhs . rhs for rank 2, or batched over equal leading dims.
+  // shape_only: check and return the result's shape without planning work
+  // (the value is produced later, folded into its consumer).
+  HVal plan_matmul(const HVal& l, const HVal& r, std::vector<StepFn>& out, bool shape_only = false,
+                   float alpha = 1.0f) {
     if (l.shape.size() < 2 || r.shape.size() < 2) fail("matmul currently requires rank-2 tensors");
     if (l.shape.size() != r.shape.size()) fail("matmul currently requires rank-2 tensors");
     for (size_t i = 0; i + 2 < l.shape.size(); ++i)
@@ -375,10 +458,25 @@ struct Executor {
     const int batch = (int)numel(os);
     os.push_back(m);
     os.push_back(n);
+    if (shape_only) {
+      HVal o;
+      o.t = HVal::Tensor;
+      o.shape = os;
+      return o;
+    }
     HVal o = new_tensor(os);
     gemm_step(out, batch, m, n, k, l.slot, false, k, m * k, r.slot, false, n, k * n, o.slot, n, m * n,
-              nullptr, 1.0f, false, false);
+              nullptr, alpha, false, false);
     return o;
+  }
+
+  // The scale node of a folded matmul: one GEMM with alpha = the constant.
+  HVal plan_folded_scale(const GNode& node) {
+    const int m = folded_scale.at(node.output);
+    float f = 1.0f;
+    scales_by_const(node, m, &f);
+    const auto& ops = deferred_matmul.at(m);
+    return plan_matmul(val(ops.first), val(ops.second), forward, false, f);
   }
 
   // ---- forward planning --------------------------------------------------------
@@ -453,6 +551,7 @@ struct Executor {
   }
 
   HVal plan_binary(const GNode& node) {
+    if (folded_scale.count(node.output)) return plan_folded_scale(node);
     const HVal& l = val(node.inputs[0]);
     const HVal& r = val(node.inputs[1]);
     const int op = binop_code(node.binop);
@@ -488,11 +587,76 @@ struct Executor {
     return h;
   }
 
+  // ---- fusions --------------------------------------------------------------
+  // Values consumed by exactly one node (and not returned or used as the
+  // objective) can be folded into that consumer without changing any result
+  // the reference defines:
+  //  * matmul -> scale-by-constant: the constant becomes the GEMM's alpha
+  //    (the product is rounded once, as the two ops in sequence round it);
+  //  * causal_mask -> Softmax: one masked-softmax kernel (same arithmetic),
+  //    and in training one kernel for both backward rules.
+  std::vector<std::vector<int>> consumers;  // node indices reading each value
+  std::vector<int> external_uses;           // returned / objective
+  std::map<int, std::pair<int, int>> deferred_matmul;  // matmul out -> (lhs, rhs)
+  std::map<int, int> folded_scale;          // scale node out -> matmul out
+  std::map<int, int> masked_input;          // causal_mask out -> its input
+  std::map<int, std::pair<Slot*, float>> grad_alias;   // value -> (grad slot, factor)
+
+  void build_uses() {
+    consumers.assign(values.size(), {});
+    external_uses.assign(values.size(), 0);
+    for (size_t i = 0; i < nodes.size(); ++i)
+      for (int in : nodes[i].inputs) consumers[in].push_back((int)i);
+    for (int o : outputs) external_uses[o]++;
+    if (objective >= 0) external_uses[objective]++;
+  }
+
+  const GNode* sole_consumer(int id) const {
+    if (external_uses[id] != 0 || consumers[id].size() != 1) return nullptr;
+    return &nodes[consumers[id][0]];
+  }
+
+  const GNode* producer_node(int id) const {
+    for (const GNode& n : nodes)
+      if (n.output == id) return &n;
+    return nullptr;
+  }
+
+  // True if `s` scales tensor `m` by a constant, with the constant in *f.
+  bool scales_by_const(const GNode& s, int m, float* f) const {
+    int c = -1;
+    if (s.kind == kNPrimitive && s.op == "scale" && s.inputs.size() == 2 && s.inputs[0] == m) c = s.inputs[1];
+    if (s.kind == kNBinary && s.binop == '*' && s.inputs.size() == 2) {
+      if (s.inputs[0] == m && s.inputs[1] != m) c = s.inputs[1];
+      else if (s.inputs[1] == m && s.inputs[0] != m) c = s.inputs[0];
+    }
+    if (c < 0) return false;
+    const GNode* p = producer_node(c);
+    if (!p || p->kind != kNConst) return false;
+    *f = (float)(p->ckind == 0 ? (double)p->ival : p->ckind == 1 ? p->fval : (p->ival ? 1.0 : 0.0));
+    return true;
+  }
+
+  bool is_softmax_apply_of(const GNode& p, int x) const {
+    if (p.kind != kNApply || p.inputs.size() != 2 || p.inputs[1] != x) return false;
+    const GNode* c = producer_node(p.inputs[0]);
+    return c && c->kind == kNCtor && c->op == "Softmax";
+  }
+
   HVal plan_primitive(const GNode& node) {
     if (node.op == "matmul") {
       const HVal& l = val(node.inputs.at(0));
       const HVal& r = val(node.inputs.at(1));
       if (l.t != HVal::Tensor || r.t != HVal::Tensor) fail("Graph executor expected tensor value");
+      const GNode* s = sole_consumer(node.output);
+      float f;
+      if (s && scales_by_const(*s, node.output, &f)) {
+        // Planned by the scale node; here only the shape (errors unchanged).
+        HVal o = plan_matmul(l, r, forward, true);
+        deferred_matmul[node.output] = {node.inputs[0], node.inputs[1]};
+        folded_scale[s->output] = node.output;
+        return o;
+      }
       return plan_matmul(l, r, forward);
     }
     if (node.op == "relu") {
@@ -504,6 +668,7 @@ struct Executor {
       return o;
     }
     if (node.op == "scale") {
+      if (folded_scale.count(node.output)) return plan_folded_scale(node);
       const HVal& x = tensor(node.inputs.at(0), "scale");
       const float s = (float)number(val(node.inputs.at(1)));
       HVal o = new_tensor(x.shape);
@@ -598,6 +763,16 @@ struct Executor {
       if (x.shape.size() < 2) fail("causal_mask expects rank >= 2");
       const int64_t q = x.shape[x.shape.size() - 2], k = x.shape.back();
       const int64_t outer = numel(x.shape) / (q * k > 0 ? q * k : 1);
+      const GNode* p = sole_consumer(node.output);
+      // --backward rejects causal_mask (backward.rs:354-383), so the fusion
+      // (which would also fuse its backward) is used in --run and --train only.
+      if (p && mode != kModeBackward && is_softmax_apply_of(*p, node.output) && x.slot) {
+        masked_input[node.output] = node.inputs[0];
+        HVal o;
+        o.t = HVal::Tensor;
+        o.shape = x.shape;
+        return o;
+      }
       HVal o = new_tensor(x.shape);
       Slot *a = x.slot, *c = o.slot;
       forward.push_back([=](cudaStream_t st) { launch_causal_mask(a->p, c->p, outer, q, k, st); });
@@ -757,7 +932,15 @@ struct Executor {
           if (x.shape.empty()) fail("softmax requires a tensor with at least one dimension");
           const int64_t w = x.shape.back();
           if (w == 0 || n % w != 0) fail("softmax requires the last dimension to divide the data length");
-          forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
+          auto mi = masked_input.find(node.inputs.at(1));
+          if (mi != masked_input.end()) {
+            Slot* src = val(mi->second).slot;
+            const int64_t q = x.shape[x.shape.size() - 2];
+            const int64_t outer = n / (q * w);
+            forward.push_back([=](cudaStream_t st) { launch_masked_softmax(src->p, c->p, outer, q, w, st); });
+          } else {
+            forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
+          }
         } else {
           if (!(cl.prob >= 0.0 && cl.prob < 1.0)) fail("dropout probability must be in [0, 1)");
           const float keep = (float)(1.0 - cl.prob);
@@ -818,20 +1001,21 @@ struct Executor {
     });
   }
   // d(lhs) of lhs.rhs: g . rhs^T ; d(rhs): lhs^T . g  (layers.rs:521-527)
+  // `alpha` scales the incoming gradient (a folded scale-by-constant).
   void emit_matmul_grads(Slot* g, const HVal& l, const HVal& r, int lid, int rid, bool want_l,
-                         bool want_r) {
+                         bool want_r, float alpha = 1.0f) {
     const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
     std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
     const int batch = (int)numel(lead);
     if (want_l) {
       auto [d, acc] = contrib(lid);
       gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr,
-                1.0f, acc, false);
+                alpha, acc, false);
     }
     if (want_r) {
       auto [d, acc] = contrib(rid);
       gemm_step(backward, batch, k, n, m, l.slot, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr,
-                1.0f, acc, false);
+                alpha, acc, false);
     }
   }
 
@@ -849,11 +1033,28 @@ struct Executor {
     const bool train = mode == kModeTrain;
     for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
       const GNode& node = *it;
+      Slot* g = nullptr;
+      float galpha = 1.0f;
       auto gi = vgrad.find(node.output);
-      if (gi == vgrad.end()) continue;
-      Slot* g = gi->second;
+      if (gi != vgrad.end()) {
+        g = gi->second;
+      } else {
+        auto ai = grad_alias.find(node.output);
+        if (ai == grad_alias.end()) continue;
+        g = ai->second.first;
+        galpha = ai->second.second;
+      }
       const HVal& out = val(node.output);
       const int64_t n = out.t == HVal::Tensor ? numel(out.shape) : 0;
+      auto fs = folded_scale.find(node.output);
+      if (fs != folded_scale.end()) {
+        // The matmul's only gradient is this node's, times the constant:
+        // handed to the matmul's backward GEMMs as their alpha.
+        float f = 1.0f;
+        scales_by_const(node, fs->second, &f);
+        grad_alias[fs->second] = {g, f};
+        continue;
+      }
       switch (node.kind) {
         case kNConst:
         case kNCtor: break;
@@ -895,7 +1096,7 @@ struct Executor {
           if (node.op == "matmul") {
             const HVal& l = val(node.inputs[0]);
             const HVal& r = val(node.inputs[1]);
-            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true);
+            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true, galpha);
           } else if (node.op == "relu") {
             auto [d, acc] = contrib(node.inputs[0]);
             Slot* y = out.slot;
@@ -1056,6 +1257,19 @@ struct Executor {
         return;
       }
       case HVal::Act: {
+        auto mi = masked_input.find(xi);
+        if (cl.act == "Softmax" && mi != masked_input.end()) {
+          // Softmax(causal_mask(x)): both backward rules in one pass, straight
+          // into x's gradient (the mask's output never holds a gradient).
+          auto [d, acc] = contrib(mi->second);
+          Slot* ys = out.slot;
+          const int64_t q = out.shape[out.shape.size() - 2], k = out.shape.back();
+          const int64_t outer = n / (q * k);
+          backward.push_back([=](cudaStream_t st) {
+            launch_masked_softmax_backward(ys->p, g->p, d->p, outer, q, k, acc, st);
+          });
+          return;
+        }
         auto [d, acc] = contrib(xi);
         Slot* xs = x.slot;
         Slot* ys = out.slot;
@@ -1155,9 +1369,11 @@ struct Executor {
   }
 
   void plan(int m) {
-    if (!dirty && mode == m) return;
+    if (!dirty && mode == m && plan_matmul_mode == ctx->matmul_mode) return;
     release();
     mode = m;
+    plan_matmul_mode = ctx->matmul_mode;
+    build_uses();
     plan_forward();
     if (mode != kModeRun) plan_backward();
     if (mode == kModeTrain) plan_update();
@@ -1327,7 +1543,9 @@ bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losse
     };
     for (int it = 0; it < iterations; ++it) {
       const int64_t l0 = g_launches.load();
-      if (e->capture && it > 0) {
+      // The first step of a plan runs eagerly (it configures kernels); every
+      // later step, in this call or a later one, replays the captured graph.
+      if (e->capture && e->stepped) {
         if (!e->exec) {
           cudaGraph_t g = nullptr;
           TYSOR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
@@ -1347,6 +1565,7 @@ bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losse
       } else {
         step();
         e->last_launches = g_launches.load() - l0;
+        e->stepped = true;
       }
       TYSOR_CUDA(cudaMemcpyAsync(d_losses + it, e->loss->p, sizeof(float), cudaMemcpyDeviceToDevice, st));
     }

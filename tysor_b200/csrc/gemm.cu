@@ -398,6 +398,289 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM form (tcgen05 cta_group::2).  A cluster of two CTAs computes a
+// 256 x BN tile: each CTA stages its own 128 rows of A and half (BN/2 rows or
+// columns) of B; the even CTA's MMA thread issues M=256 MMAs that read both
+// CTAs' shared memory and write each CTA's 128-lane accumulator.  Per SM this
+// halves the B operand traffic through shared memory (TMA writes and MMA
+// reads), which bounds the 1-SM tile.  Both CTAs' TMA loads complete on the
+// even CTA's "full" barrier; MMA completion is multicast to both CTAs'
+// "empty" / "chunk full" barriers; both CTAs' accumulator warps release a
+// chunk buffer on the even CTA's "chunk empty" barrier.  No TMA load uses
+// multicast.
+// ---------------------------------------------------------------------------
+
+template <int BN, bool kStrict>
+struct PipeCfg2 {
+  static constexpr int kA = BM * BK * 4;             // this CTA's 128 rows of A
+  static constexpr int kB = (BN / 2) * BK * 4;       // this CTA's half of B
+  static constexpr int kStageBytes = kStrict ? 2 * (kA + kB) : (kA + kB);
+  static constexpr int kStagesRaw = (192 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of this CTA's shared variable `local` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+// Loads into this CTA's shared memory; the transaction bytes complete on the
+// even CTA's barrier (the peer bit of the barrier address cleared).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar & 0xFEFFFFFFu), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// MMA completion signalled on the barrier at this offset in both CTAs.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
+template <int BN, bool kStrict, bool kAmn, bool kBmn>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
+    gemm_tf32_2sm_kernel(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_alo,
+                         const __grid_constant__ CUtensorMap map_b,
+                         const __grid_constant__ CUtensorMap map_blo, GemmOutput out,
+                         GemmEpilogue ep, int M, int N, int K, int* err) {
+  using Cfg = PipeCfg2<BN, kStrict>;
+  constexpr int kA = Cfg::kA;
+  constexpr int kB = Cfg::kB;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kStageBytes = Cfg::kStageBytes;
+  constexpr uint32_t kTxBytes = 2 * kStageBytes;  // both CTAs' loads
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr int kHalf = BN / 2;
+  constexpr int kBH = BN / 2;  // rows (K-major) or columns (MN-major) of B per CTA
+  constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kAmn ? 1u : 0u) << 15) |
+                              ((kBmn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(256 >> 4) << 24);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + kStages * kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* tfull_bar = bars + 2 * kStages;
+  uint64_t* tempty_bar = bars + 2 * kStages + 2;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kStages + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  // Pair index -> (row pair, column tile), column tiles fastest: consecutive
+  // pairs share their A rows, so A streams from HBM once while the (smaller)
+  // B panel stays in L2.
+  const int n_tiles = (N + BN - 1) / BN;
+  const int pair = blockIdx.x >> 1;
+  const int m0 = (pair / n_tiles) * 256 + (int)rank * BM;  // this CTA's rows
+  const int n0 = (pair % n_tiles) * BN;
+  const int nb0 = n0 + (int)rank * kBH;  // this CTA's half of B
+  const int bz = blockIdx.z;
+  const int num_kb = (K + BK - 1) / BK;
+  const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull_bar[b]), 1);
+      mbar_init(smem_u32(&tempty_bar[b]), 2 * kAccWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    // TMA producer (both CTAs).
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int s = kb % kStages;
+      if (kb >= kStages) ok = mbar_wait(smem_u32(&empty_bar[s]), ((kb / kStages) - 1) & 1, err);
+      if (!ok) break;
+      const uint32_t fb = smem_u32(&full_bar[s]);
+      if (leader) mbar_expect_tx(fb, kTxBytes);
+      const uint32_t base = smem_u32(smem + s * kStageBytes);
+      const int k0 = kb * BK;
+      const int nmaps = kStrict ? 2 : 1;
+      for (int h = 0; h < nmaps; ++h) {
+        const CUtensorMap* ma = h ? &map_alo : &map_a;
+        const CUtensorMap* mb = h ? &map_blo : &map_b;
+        const uint32_t ta = base + h * kA;
+        const uint32_t tb = base + nmaps * kA + h * kB;
+        if (kAmn) {
+#pragma unroll
+          for (int i = 0; i < BM / 32; ++i) tma_load_3d_pair(ta + i * 2048, ma, fb, m0 + 32 * i, k0, bz);
+        } else {
+          tma_load_3d_pair(ta, ma, fb, k0, m0, bz);
+        }
+        if (kBmn) {
+#pragma unroll
+          for (int i = 0; i < kBH / 32; ++i) tma_load_3d_pair(tb + i * 2048, mb, fb, nb0 + 32 * i, k0, bz);
+        } else {
+          tma_load_3d_pair(tb, mb, fb, k0, nb0, bz);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // MMA issuer (even CTA only): M=256 over both CTAs' operands.
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int s = kb % kStages;
+      const int chunk = kb / kChunkKb;
+      const int buf = chunk & 1;
+      const bool first = (kb % kChunkKb) == 0;
+      const bool last = (kb % kChunkKb) == kChunkKb - 1 || kb == num_kb - 1;
+      if (first && chunk >= 2) {
+        ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((chunk >> 1) - 1) & 1, err);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      ok = mbar_wait(smem_u32(&full_bar[s]), (kb / kStages) & 1, err);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(buf * BN);
+      const uint32_t base = smem_u32(smem + s * kStageBytes);
+      const int nmaps = kStrict ? 2 : 1;
+      const uint32_t ta = base, talo = base + kA;
+      const uint32_t tb = base + nmaps * kA, tblo = tb + kB;
+#pragma unroll
+      for (int j = 0; j < BK / 8; ++j) {
+        const uint64_t da = operand_desc(ta, kAmn, j);
+        const uint64_t db = operand_desc(tb, kBmn, j);
+        const uint32_t acc = (first && j == 0) ? 0u : 1u;
+        if (kStrict) {
+          umma_tf32_pair(d, operand_desc(talo, kAmn, j), db, kIdesc, acc);
+          umma_tf32_pair(d, da, operand_desc(tblo, kBmn, j), kIdesc, 1u);
+          umma_tf32_pair(d, da, db, kIdesc, 1u);
+        } else {
+          umma_tf32_pair(d, da, db, kIdesc, acc);
+        }
+      }
+      umma_commit_pair(smem_u32(&empty_bar[s]));
+      if (last) umma_commit_pair(smem_u32(&tfull_bar[buf]));
+    }
+  }
+  __syncwarp();
+
+  if (warp >= 2) {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    float acc[kHalf];
+#pragma unroll
+    for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
+    bool have = true;
+    for (int chunk = 0; chunk < nchunks; ++chunk) {
+      const int buf = chunk & 1;
+      have = mbar_wait(smem_u32(&tfull_bar[buf]), (chunk >> 1) & 1, err);
+      if (!have) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
+#pragma unroll
+      for (int c = 0; c < kHalf; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c + i] = acc[c + i] + __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[buf]), 0));
+    }
+
+    const int row = m0 + quad * 32 + lane;
+    const int col0 = n0 + half * kHalf;
+    if (have && row < M && col0 < N) {
+      float* crow = out.ptr + (int64_t)bz * out.batch_stride + (int64_t)row * out.ld + col0;
+      const bool vec_ok = ((out.ld & 3) == 0) && ((((uintptr_t)out.ptr) & 15) == 0) &&
+                          ((out.batch_stride & 3) == 0) && (col0 + kHalf <= N);
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
+        float r = acc[i] * ep.alpha;
+        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
+        if (ep.relu) r = fmaxf(r, 0.0f);
+        acc[i] = r;
+      }
+      if (vec_ok) {
+        float4* dst = (float4*)crow;
+#pragma unroll
+        for (int q = 0; q < kHalf / 4; ++q) {
+          float4 w = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+          if (ep.accumulate) {
+            const float4 o = dst[q];
+            w.x = o.x + w.x;
+            w.y = o.y + w.y;
+            w.z = o.z + w.z;
+            w.w = o.w + w.w;
+          }
+          dst[q] = w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i)
+          if (col0 + i < N) crow[i] = ep.accumulate ? crow[i] + acc[i] : acc[i];
+      }
+    }
+  }
+
+  // Neither CTA may leave (releasing its shared memory and tensor memory)
+  // while the pair's MMAs can still read or write them.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // lo(x) = x - tf32_trunc(x), elementwise over a contiguous span.
 __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n >> 2;
@@ -417,6 +700,31 @@ __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__
        i += (int64_t)gridDim.x * blockDim.x) {
     float v = x[i];
     lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  }
+}
+
+// Transposed copy of a [batch][rows][cols] tensor plus the lo part of the
+// copy, through 32 x 32 shared-memory tiles (coalesced on both sides).
+__global__ void split_transpose_kernel(const float* __restrict__ x, float* __restrict__ hi_t,
+                                       float* __restrict__ lo_t, int64_t rows, int64_t cols) {
+  __shared__ float tile[32][33];
+  const int64_t b = blockIdx.z;
+  const float* xb = x + b * rows * cols;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = xb[r * cols + c];
+  }
+  __syncthreads();
+  float* hb = hi_t + b * rows * cols;
+  float* lb = lo_t ? lo_t + b * rows * cols : nullptr;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) {
+      const float v = tile[threadIdx.x][i];
+      hb[c * rows + r] = v;
+      if (lb) lb[c * rows + r] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    }
   }
 }
 
@@ -526,6 +834,37 @@ void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+template <int BN, bool S, bool AMN, bool BMN>
+void launch_tc2(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
+                const CUtensorMap& mblo, const GemmOutput& C, const GemmEpilogue& ep, int batch,
+                int M, int N, int K, int* d_err, cudaStream_t st) {
+  constexpr int smem = PipeCfg2<BN, S>::kSmem;
+  auto kern = gemm_tf32_2sm_kernel<BN, S, AMN, BMN>;
+  static bool configured = false;
+  if (!configured) {
+    TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((unsigned)(2 * ceil_div(M, 256) * ceil_div(N, BN)), 1u, (unsigned)batch);
+  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, C, ep, M, N, K, d_err);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <int BN, bool S>
+void dispatch_layout2(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
+                      const CUtensorMap& mb, const CUtensorMap& mblo, const GemmOutput& C,
+                      const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
+                      cudaStream_t st) {
+  if (amn) {
+    if (bmn) launch_tc2<BN, S, true, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc2<BN, S, true, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  } else {
+    if (bmn) launch_tc2<BN, S, false, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc2<BN, S, false, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  }
+}
+
 template <int BN, bool S>
 void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
                      const CUtensorMap& mb, const CUtensorMap& mblo, const GemmOutput& C,
@@ -541,6 +880,33 @@ void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMa
 }
 
 }  // namespace
+
+// The 2-SM (cluster pair) kernel is opt-in (TYSOR_CUDA_GEMM_2SM=1).  It
+// relieves shared-memory bandwidth, which only binds when an operand is
+// M/N-major; the executor hands the GEMM K-major operands, for which the
+// 1-SM kernel already runs at the 3xTF32 tensor-core ceiling, and the pair
+// form showed step-to-step variance in the block benchmark.
+bool g_two_sm_enabled = [] {
+  const char* v = getenv("TYSOR_CUDA_GEMM_2SM");
+  return v && v[0] == '1';
+}();
+
+void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  split_lo_kernel<<<elementwise_blocks(n / 4 + 1, 256), 256, 0, st>>>(x, lo, n);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+void launch_split_transpose(const float* x, float* hi_t, float* lo_t, int64_t batch, int64_t rows,
+                            int64_t cols, cudaStream_t st) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return;
+  if (batch > 65535 || ceil_div(rows, 32) > 65535) throw CudaError("split_transpose: grid too large");
+  dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32), (unsigned)batch);
+  split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi_t, lo_t, rows, cols);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
 
 void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
                        const GemmOperand& B, int mode, int64_t* a_elems, int64_t* b_elems) {
@@ -577,21 +943,28 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     gemm_scratch_need(batch, M, N, K, A, B, mode, &na, &nb);
     if (scratch.a_lo == nullptr || scratch.b_lo == nullptr || scratch.a_elems < na ||
         scratch.b_elems < nb)
-      throw CudaError("strict matmul needs scratch for the split operands");
-    split_lo_kernel<<<elementwise_blocks(na / 4 + 1, 256), 256, 0, st>>>(A.ptr, scratch.a_lo, na);
-    split_lo_kernel<<<elementwise_blocks(nb / 4 + 1, 256), 256, 0, st>>>(B.ptr, scratch.b_lo, nb);
-    TYSOR_CUDA(cudaGetLastError());
-    g_launches.fetch_add(2, std::memory_order_relaxed);
+      throw CudaError("strict matmul needs scratch for the split operands (batch " + std::to_string(batch) +
+                      ", M " + std::to_string(M) + ", N " + std::to_string(N) + ", K " + std::to_string(K) +
+                      ", A needs " + std::to_string(na) + " has " + std::to_string(scratch.a_elems) +
+                      (scratch.a_lo ? "" : " (none)") + ", B needs " + std::to_string(nb) + " has " +
+                      std::to_string(scratch.b_elems) + (scratch.b_lo ? "" : " (none)") + ")");
+    if (!scratch.presplit) {
+      launch_split_lo(A.ptr, scratch.a_lo, na, st);
+      launch_split_lo(B.ptr, scratch.b_lo, nb, st);
+    }
     alo = scratch.a_lo;
     blo = scratch.b_lo;
   }
   const int BN = N <= 128 ? 128 : 256;
+  // The 2-SM form needs a full 256-row pair tile to be worth its cluster.
+  const bool two_sm = g_two_sm_enabled && BN == 256 && M >= 256;
   const bool amn = A.trans, bmn = !B.trans;
   // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
   const uint64_t a_in = amn ? M : K, a_out = amn ? K : M;
   const uint64_t b_in = bmn ? N : K, b_out = bmn ? K : N;
   const uint32_t a_box_in = amn ? 32 : BK, a_box_out = amn ? BK : BM;
-  const uint32_t b_box_in = bmn ? 32 : BK, b_box_out = bmn ? BK : (uint32_t)BN;
+  const uint32_t b_rows = two_sm ? (uint32_t)BN / 2 : (uint32_t)BN;
+  const uint32_t b_box_in = bmn ? 32 : BK, b_box_out = bmn ? BK : b_rows;
   const CUtensorMapSwizzle a_sw = amn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapSwizzle b_sw = bmn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap ma = make_map(A.ptr, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
@@ -601,7 +974,10 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     malo = make_map(alo, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
     mblo = make_map(blo, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
   }
-  if (BN == 128) {
+  if (two_sm) {
+    if (strict) dispatch_layout2<256, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    else dispatch_layout2<256, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+  } else if (BN == 128) {
     if (strict) dispatch_layout<128, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
     else dispatch_layout<128, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
   } else {

@@ -352,6 +352,147 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
   }
 }
 
+// Register-resident row softmax for widths of 1024 * VPT: each of 256
+// threads keeps VPT float4 of its row, so the row is read from HBM once and
+// written once.  With `masked`, row r's entries with col > r % q read as
+// -1e4 (causal_mask fused in front).  Same arithmetic as softmax_kernel.
+template <int VPT>
+__global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restrict__ x,
+                                                          float* __restrict__ out, int64_t rows,
+                                                          int q, int masked) {
+  __shared__ float red[33];
+  constexpr int kWidth = 1024 * VPT;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int qi = masked ? (int)(r % q) : kWidth;
+    const float4* xr = (const float4*)(x + r * kWidth);
+    float4 v[VPT];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int j = threadIdx.x + i * 256;
+      const int c = 4 * j;
+      // Fully masked float4 groups are not read: their value is -1e4 whatever x holds.
+      float4 t = c > qi ? make_float4(-1.0e4f, -1.0e4f, -1.0e4f, -1.0e4f) : xr[j];
+      if (c + 0 > qi) t.x = -1.0e4f;
+      if (c + 1 > qi) t.y = -1.0e4f;
+      if (c + 2 > qi) t.z = -1.0e4f;
+      if (c + 3 > qi) t.w = -1.0e4f;
+      v[i] = t;
+      m = fmaxf(fmaxf(fmaxf(m, t.x), fmaxf(t.y, t.z)), t.w);
+    }
+    m = block_max(m, red);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      v[i].x = expf(v[i].x - m);
+      v[i].y = expf(v[i].y - m);
+      v[i].z = expf(v[i].z - m);
+      v[i].w = expf(v[i].w - m);
+      s += v[i].x;
+      s += v[i].y;
+      s += v[i].z;
+      s += v[i].w;
+    }
+    const float d = fmaxf(block_sum(s, red), 1.1920928955078125e-7f);
+    float4* yr = (float4*)(out + r * kWidth);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float4 t = v[i];
+      t.x = t.x / d;
+      t.y = t.y / d;
+      t.z = t.z / d;
+      t.w = t.w / d;
+      yr[threadIdx.x + i * 256] = t;
+    }
+  }
+}
+
+// Row r of [outer*q] rows of width k; row index within its q x k block is
+// r % q.  Values with col > row read as -1e4.
+__global__ void masked_softmax_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                      int64_t rows, int q, int width) {
+  __shared__ float red[33];
+  const bool vec = (width & 3) == 0 && aligned16(x) && aligned16(out);
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int qi = (int)(r % q);
+    const float* xr = x + r * width;
+    float* yr = out + r * width;
+    float m = -INFINITY;
+    if (vec) {
+      for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
+        const float4 v = ((const float4*)xr)[j];
+        const int c = 4 * j;
+        m = fmaxf(m, c + 0 > qi ? -1.0e4f : v.x);
+        m = fmaxf(m, c + 1 > qi ? -1.0e4f : v.y);
+        m = fmaxf(m, c + 2 > qi ? -1.0e4f : v.z);
+        m = fmaxf(m, c + 3 > qi ? -1.0e4f : v.w);
+      }
+    } else {
+      for (int j = threadIdx.x; j < width; j += blockDim.x) m = fmaxf(m, j > qi ? -1.0e4f : xr[j]);
+    }
+    m = block_max(m, red);
+    float s = 0.0f;
+    if (vec) {
+      for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
+        const float4 v = ((const float4*)xr)[j];
+        const int c = 4 * j;
+        s += expf((c + 0 > qi ? -1.0e4f : v.x) - m);
+        s += expf((c + 1 > qi ? -1.0e4f : v.y) - m);
+        s += expf((c + 2 > qi ? -1.0e4f : v.z) - m);
+        s += expf((c + 3 > qi ? -1.0e4f : v.w) - m);
+      }
+    } else {
+      for (int j = threadIdx.x; j < width; j += blockDim.x) s += expf((j > qi ? -1.0e4f : xr[j]) - m);
+    }
+    const float d = fmaxf(block_sum(s, red), 1.1920928955078125e-7f);
+    if (vec) {
+      for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
+        const float4 v = ((const float4*)xr)[j];
+        const int c = 4 * j;
+        float4 o;
+        o.x = expf((c + 0 > qi ? -1.0e4f : v.x) - m) / d;
+        o.y = expf((c + 1 > qi ? -1.0e4f : v.y) - m) / d;
+        o.z = expf((c + 2 > qi ? -1.0e4f : v.z) - m) / d;
+        o.w = expf((c + 3 > qi ? -1.0e4f : v.w) - m) / d;
+        ((float4*)yr)[j] = o;
+      }
+    } else {
+      for (int j = threadIdx.x; j < width; j += blockDim.x) yr[j] = expf((j > qi ? -1.0e4f : xr[j]) - m) / d;
+    }
+  }
+}
+
+__global__ void masked_softmax_backward_kernel(const float* __restrict__ y, const float* __restrict__ g,
+                                               float* __restrict__ dx, int64_t n, int64_t q, int64_t k,
+                                               int accumulate) {
+  const bool vec = (k & 3) == 0 && aligned16(y) && aligned16(g) && aligned16(dx);
+  if (vec) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n >> 2);
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t e = i << 2;
+      const int64_t col = e % k, row = (e / k) % q;
+      const float4 yv = ((const float4*)y)[i], gv = ((const float4*)g)[i];
+      float4 v;
+      v.x = col + 0 > row ? 0.0f : (yv.x * (1.0f - yv.x)) * gv.x;
+      v.y = col + 1 > row ? 0.0f : (yv.y * (1.0f - yv.y)) * gv.y;
+      v.z = col + 2 > row ? 0.0f : (yv.z * (1.0f - yv.z)) * gv.z;
+      v.w = col + 3 > row ? 0.0f : (yv.w * (1.0f - yv.w)) * gv.w;
+      if (accumulate) {
+        const float4 o = ((float4*)dx)[i];
+        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+      }
+      ((float4*)dx)[i] = v;
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t col = i % k, row = (i / k) % q;
+      const float v = col > row ? 0.0f : (y[i] * (1.0f - y[i])) * g[i];
+      dx[i] = accumulate ? dx[i] + v : v;
+    }
+  }
+}
+
 __global__ void cross_entropy_kernel(const float* __restrict__ logits,
                                      const float* __restrict__ target, float* __restrict__ loss,
                                      int64_t rows, int width) {
@@ -709,6 +850,8 @@ int row_threads(int64_t width) {
 
 int row_blocks(int64_t rows) { return (int)(rows < 148 * 64 ? (rows < 1 ? 1 : rows) : 148 * 64); }
 
+bool aligned16_host(const void* p) { return (((uintptr_t)p) & 15) == 0; }
+
 void check_launch() {
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -839,9 +982,47 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
   check_launch();
 }
 
+// Launches the register-resident form when the width allows; false if not.
+bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
+                 cudaStream_t st);
+
 void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st) {
   if (rows <= 0) return;
+  if (softmax_reg(x, out, rows, width, 1, 0, st)) return;
   softmax_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(x, out, rows, (int)width);
+  check_launch();
+}
+
+bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
+                 cudaStream_t st) {
+  if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out)) return false;
+  const int blocks = row_blocks(rows);
+  switch (width / 1024) {
+    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
+    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
+    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
+    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
+    default: return false;
+  }
+  check_launch();
+  return true;
+}
+
+void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
+                           cudaStream_t st) {
+  const int64_t rows = outer * q;
+  if (rows <= 0) return;
+  if (softmax_reg(x, out, rows, k, q, 1, st)) return;
+  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k);
+  check_launch();
+}
+
+void launch_masked_softmax_backward(const float* y, const float* g, float* dx, int64_t outer,
+                                    int64_t q, int64_t k, int accumulate, cudaStream_t st) {
+  const int64_t n = outer * q * k;
+  if (n <= 0) return;
+  masked_softmax_backward_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
+      y, g, dx, n, q, k, accumulate);
   check_launch();
 }
 

@@ -61,6 +61,16 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
                                    cudaStream_t st);
 
 void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st);
+// Softmax of causal_mask(x) over [outer][q][k] in one pass: entries with
+// col > row take the mask's -1e4 (layers.rs:217-236), then the row softmax
+// (tensor.rs:235-260) — the same arithmetic as the two ops in sequence.
+void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
+                           cudaStream_t st);
+// Backward of Softmax(causal_mask(x)) with the reference rules: the
+// diagonal softmax term y(1-y)g (layers.rs:350-364), then the mask zeroes
+// col > row (layers.rs:418-436): dx (+)= col > row ? 0 : y(1-y)g.
+void launch_masked_softmax_backward(const float* y, const float* g, float* dx, int64_t outer,
+                                    int64_t q, int64_t k, int accumulate, cudaStream_t st);
 void launch_cross_entropy(const float* logits, const float* target, float* loss, int64_t rows,
                           int64_t width, cudaStream_t st);
 void launch_cross_entropy_backward(const float* logits, const float* target, float* grad,

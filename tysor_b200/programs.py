@@ -296,7 +296,7 @@ def mlp_train(d_in: int = 1024, d_hidden: int = 4096, d_out: int = 1024, lr: flo
 
 def llama_block(batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: int = 16,
                 n_kv_heads: int = 4, hidden: int = 5632, theta: float = 10000.0,
-                eps: float = 1e-6, lr: float = 1e-3) -> Graph:
+                eps: float = 1e-6, lr: float = 1e-3, mse_target: bool = False) -> Graph:
     """Llama-style decoder block (the structure of examples/llama.ty's
     DecoderBlock with GroupedQueryAttention and SwiGLU), written with the
     batched-matmul / transpose / RMSNorm extensions:
@@ -308,11 +308,15 @@ def llama_block(batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: i
     [B, S, H, hd], transpose to [B, H, S, hd], RoPE on q and k, repeat_kv on
     k and v, scores = q @ k^T scaled by 1/sqrt(hd), causal_mask, Softmax,
     @ v, transpose back and flatten.  The objective is the block output (its
-    gradient seed is all ones, as for any objective, executor.rs:579)."""
+    gradient seed is all ones, as for any objective, executor.rs:579), or with
+    `mse_target` the squared error against a `target` input,
+    `d = out - target; loss = d * d` (summed by the trainer), which keeps a
+    training run bounded."""
     hd = d_model // n_heads
     rep = n_heads // n_kv_heads
     b = GraphBuilder("block")
     x = b.param("x")
+    target = b.param("target") if mse_target else None
     n1 = b.let("attn_norm", b.ctor("RMSNorm", d_model, eps))
     qp = b.let("q_proj", b.ctor("linear", d_model, n_heads * hd, False))
     kp = b.let("k_proj", b.ctor("linear", d_model, n_kv_heads * hd, False))
@@ -347,8 +351,13 @@ def llama_block(batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: i
     gate = b.apply(act, b.apply(gp, hn2))
     ff = b.binary("*", gate, b.apply(up, hn2))
     out = b.let("out", b.binary("+", h, b.apply(dp, ff)))
-    b.ret(out)
-    b.train(objective="out", lr=lr, iterations=1)
+    if target is not None:
+        d = b.let("d", b.binary("-", out, target))
+        b.ret(b.let("loss", b.binary("*", d, d)))
+        b.train(objective="loss", lr=lr, iterations=1)
+    else:
+        b.ret(out)
+        b.train(objective="out", lr=lr, iterations=1)
     return b.build()
 
 
