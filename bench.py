@@ -249,16 +249,28 @@ def run_ours(args, rank, world, local_rank, dist):
 
     # end to end through the public API: pinned host x and target -> device,
     # one step, loss back to the host, every step.
-    e2e_steps = max(2, min(args.steps, 5))
+    e2e_steps = max(5, args.steps)
     if dist is not None:
         dist.barrier()
     ctx.synchronize()
+    e2e_sampler = ClockSampler(gpu_index_for(local_rank)) if rank == 0 else None
+    if e2e_sampler:
+        e2e_sampler.start()
+        time.sleep(0.5)
     t0 = time.perf_counter()
+    upload_ms, step_wall = [], []
     for _ in range(e2e_steps):
+        t1 = time.perf_counter()
+        u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        u0.record(stream)
         for name, arr in pinned.items():
             native.check(lib.tysor_cuda_graph_upload_input(ex.handle, name.encode(), native.fptr(arr), arr.size))
+        u1.record(stream)
         ex.train(1, LR)  # returns the step's loss on the host
+        step_wall.append((time.perf_counter() - t1) * 1e3)
+        upload_ms.append(u0.elapsed_time(u1))
     e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_clocks = e2e_sampler.stop() if e2e_sampler else None
     if dist is not None:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -321,7 +333,9 @@ def run_ours(args, rank, world, local_rank, dist):
                        "last_loss": losses[-1] if losses else None},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(world * tokens / e2e_s, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(x.nbytes + tgt.nbytes), "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": int(x.nbytes + tgt.nbytes), "d2h_bytes_per_step": 4,
+                    "h2d_ms_per_step": [round(v, 2) for v in upload_ms],
+                    "wall_ms_per_step": [round(v, 2) for v in step_wall], "clocks": e2e_clocks},
             "gpu_launches": int(launches), "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -99,145 +99,143 @@ __global__ void fill_kernel(float* out, int64_t n, float v) {
     out[i] = v;
 }
 
-// Generic elementwise driver: F(i) computes element i; vectorised 4-wide
-// when every pointer involved is 16-byte aligned.
-template <typename F4, typename F1>
-__device__ __forceinline__ void ew_loop(int64_t n, bool vec, F4 f4, F1 f1) {
+// Generic elementwise driver.  out[i] = op(in_0[i], ..., in_{N-1}[i]), or
+// out[i] + op(...) with `acc` (the reference's add_in_place order).  When
+// every pointer is 16-byte aligned each thread moves kUnroll float4 per
+// input per iteration, all loads issued before the first use, so enough
+// bytes are in flight to keep HBM busy; ragged tails and unaligned views
+// take the scalar loop.  `out` may alias an input at the same index.
+constexpr int kUnroll = 4;
+
+template <int N>
+struct In {
+  const float* p[N > 0 ? N : 1];
+};
+
+template <int N, typename Op>
+__device__ __forceinline__ float4 ew_apply4(Op op, const float4 (&a)[N > 0 ? N : 1], float4 o, int acc) {
+  float s[N > 0 ? N : 1];
+  float4 r;
+#pragma unroll
+  for (int k = 0; k < N; ++k) s[k] = a[k].x;
+  r.x = op(s);
+#pragma unroll
+  for (int k = 0; k < N; ++k) s[k] = a[k].y;
+  r.y = op(s);
+#pragma unroll
+  for (int k = 0; k < N; ++k) s[k] = a[k].z;
+  r.z = op(s);
+#pragma unroll
+  for (int k = 0; k < N; ++k) s[k] = a[k].w;
+  r.w = op(s);
+  if (acc) r = make_float4(o.x + r.x, o.y + r.y, o.z + r.z, o.w + r.w);
+  return r;
+}
+
+template <int N, typename Op>
+__device__ __forceinline__ void ew_run(In<N> in, float* out, int64_t n, int acc, Op op) {
+  bool vec = aligned16(out);
+#pragma unroll
+  for (int k = 0; k < N; ++k) vec = vec && aligned16(in.p[k]);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   int64_t done = 0;
   if (vec) {
     const int64_t n4 = n >> 2;
-    for (int64_t i = t0; i < n4; i += stride) f4(i);
+    int64_t i = t0;
+    for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+      float4 a[kUnroll][N > 0 ? N : 1];
+      float4 o[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) a[u][k] = ((const float4*)in.p[k])[i + u * stride];
+        o[u] = acc ? ((const float4*)out)[i + u * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) ((float4*)out)[i + u * stride] = ew_apply4<N>(op, a[u], o[u], acc);
+    }
+    for (; i < n4; i += stride) {
+      float4 a[N > 0 ? N : 1];
+#pragma unroll
+      for (int k = 0; k < N; ++k) a[k] = ((const float4*)in.p[k])[i];
+      const float4 o = acc ? ((const float4*)out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ((float4*)out)[i] = ew_apply4<N>(op, a, o, acc);
+    }
     done = n4 << 2;
   }
-  for (int64_t i = done + t0; i < n; i += stride) f1(i);
+  for (int64_t e = done + t0; e < n; e += stride) {
+    float s[N > 0 ? N : 1];
+#pragma unroll
+    for (int k = 0; k < N; ++k) s[k] = in.p[k][e];
+    const float v = op(s);
+    out[e] = acc ? out[e] + v : v;
+  }
 }
 
-__global__ void unary_kernel(int op, const float* __restrict__ x, float* __restrict__ out,
-                             int64_t n, float p) {
-  const bool vec = aligned16(x) && aligned16(out);
-  ew_loop(
-      n, vec,
-      [&](int64_t i) {
-        float4 v = ((const float4*)x)[i];
-        v.x = apply_unary(op, v.x, p);
-        v.y = apply_unary(op, v.y, p);
-        v.z = apply_unary(op, v.z, p);
-        v.w = apply_unary(op, v.w, p);
-        ((float4*)out)[i] = v;
-      },
-      [&](int64_t i) { out[i] = apply_unary(op, x[i], p); });
+__global__ void unary_kernel(int op, const float* x, float* out, int64_t n, float p) {
+  ew_run<1>(In<1>{{x}}, out, n, 0, [=](const float (&a)[1]) { return apply_unary(op, a[0], p); });
 }
 
 __global__ void binary_tt_kernel(int op, const float* a, const float* b, float* out, int64_t n) {
-  const bool vec = aligned16(a) && aligned16(b) && aligned16(out);
-  ew_loop(
-      n, vec,
-      [&](int64_t i) {
-        float4 u = ((const float4*)a)[i], v = ((const float4*)b)[i];
-        ((float4*)out)[i] = make_float4(apply_binary(op, u.x, v.x), apply_binary(op, u.y, v.y),
-                                        apply_binary(op, u.z, v.z), apply_binary(op, u.w, v.w));
-      },
-      [&](int64_t i) { out[i] = apply_binary(op, a[i], b[i]); });
+  ew_run<2>(In<2>{{a, b}}, out, n, 0, [=](const float (&v)[2]) { return apply_binary(op, v[0], v[1]); });
 }
 
 __global__ void binary_ts_kernel(int op, const float* a, float s, float* out, int64_t n,
                                  int scalar_first) {
-  const bool vec = aligned16(a) && aligned16(out);
-  ew_loop(
-      n, vec,
-      [&](int64_t i) {
-        float4 u = ((const float4*)a)[i];
-        if (scalar_first)
-          u = make_float4(apply_binary(op, s, u.x), apply_binary(op, s, u.y),
-                          apply_binary(op, s, u.z), apply_binary(op, s, u.w));
-        else
-          u = make_float4(apply_binary(op, u.x, s), apply_binary(op, u.y, s),
-                          apply_binary(op, u.z, s), apply_binary(op, u.w, s));
-        ((float4*)out)[i] = u;
-      },
-      [&](int64_t i) {
-        out[i] = scalar_first ? apply_binary(op, s, a[i]) : apply_binary(op, a[i], s);
-      });
+  ew_run<1>(In<1>{{a}}, out, n, 0, [=](const float (&v)[1]) {
+    return scalar_first ? apply_binary(op, s, v[0]) : apply_binary(op, v[0], s);
+  });
 }
 
 __global__ void add_inplace_kernel(float* dst, const float* src, int64_t n) {
-  const bool vec = aligned16(dst) && aligned16(src);
-  ew_loop(
-      n, vec,
-      [&](int64_t i) {
-        float4 d = ((float4*)dst)[i], s = ((const float4*)src)[i];
-        ((float4*)dst)[i] = make_float4(d.x + s.x, d.y + s.y, d.z + s.z, d.w + s.w);
-      },
-      [&](int64_t i) { dst[i] = dst[i] + src[i]; });
+  ew_run<1>(In<1>{{src}}, dst, n, 1, [=](const float (&v)[1]) { return v[0]; });
 }
 
 __global__ void binary_acc_kernel(int op, const float* a, const float* b, float s, int mode,
                                   float* dst, int64_t n) {
   // mode 0: op(a[i], b[i]); 1: op(a[i], s); 2: op(s, a[i])
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = mode == 0 ? apply_binary(op, a[i], b[i])
-                              : (mode == 1 ? apply_binary(op, a[i], s) : apply_binary(op, s, a[i]));
-    dst[i] = dst[i] + v;
-  }
+  if (mode == 0)
+    ew_run<2>(In<2>{{a, b}}, dst, n, 1, [=](const float (&v)[2]) { return apply_binary(op, v[0], v[1]); });
+  else
+    ew_run<1>(In<1>{{a}}, dst, n, 1, [=](const float (&v)[1]) {
+      return mode == 1 ? apply_binary(op, v[0], s) : apply_binary(op, s, v[0]);
+    });
 }
 
 __global__ void div_rhs_grad_kernel(const float* g, const float* l, const float* r, float* dst,
                                     int64_t n, int accumulate) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float num = g[i] * l[i];
-    const float den = r[i] * r[i];
-    const float v = -(num / den);
-    dst[i] = accumulate ? dst[i] + v : v;
-  }
-}
-
-__device__ __forceinline__ void store_acc(float* dx, int64_t i, float v, int accumulate) {
-  dx[i] = accumulate ? dx[i] + v : v;
+  ew_run<3>(In<3>{{g, l, r}}, dst, n, accumulate, [=](const float (&v)[3]) {
+    const float num = v[0] * v[1];
+    const float den = v[2] * v[2];
+    return -(num / den);
+  });
 }
 
 __global__ void relu_backward_kernel(const float* y, const float* g, float* dx, int64_t n, int acc) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    store_acc(dx, i, g[i] * (y[i] > 0.0f ? 1.0f : 0.0f), acc);
+  ew_run<2>(In<2>{{y, g}}, dx, n, acc, [=](const float (&v)[2]) { return v[1] * (v[0] > 0.0f ? 1.0f : 0.0f); });
 }
 
 __global__ void silu_backward_kernel(const float* x, const float* g, float* dx, int64_t n, int acc) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = x[i];
+  ew_run<2>(In<2>{{x, g}}, dx, n, acc, [=](const float (&a)[2]) {
+    const float v = a[0];
     const float s = 1.0f / (1.0f + expf(-v));
     float t = v * s;
     t = t * (1.0f - s);
-    store_acc(dx, i, g[i] * (s + t), acc);
-  }
+    return a[1] * (s + t);
+  });
 }
 
 __global__ void softmax_backward_kernel(const float* y, const float* g, float* dx, int64_t n,
                                         int acc) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float t = y[i] * (1.0f - y[i]);
-    store_acc(dx, i, t * g[i], acc);
-  }
+  ew_run<2>(In<2>{{y, g}}, dx, n, acc, [=](const float (&a)[2]) {
+    const float t = a[0] * (1.0f - a[0]);
+    return t * a[1];
+  });
 }
 
 __global__ void sgd_kernel(float* p, const float* g, float lr, int64_t n) {
-  const bool vec = aligned16(p) && aligned16(g);
-  ew_loop(
-      n, vec,
-      [&](int64_t i) {
-        float4 w = ((float4*)p)[i], d = ((const float4*)g)[i];
-        w.x = w.x - lr * d.x;
-        w.y = w.y - lr * d.y;
-        w.z = w.z - lr * d.z;
-        w.w = w.w - lr * d.w;
-        ((float4*)p)[i] = w;
-      },
-      [&](int64_t i) { p[i] = p[i] - lr * g[i]; });
+  ew_run<2>(In<2>{{p, g}}, p, n, 0, [=](const float (&a)[2]) { return a[0] - lr * a[1]; });
 }
 
 // ---- row reductions -------------------------------------------------------------
@@ -318,12 +316,78 @@ __global__ void rms_gain_backward_kernel(const float* __restrict__ x, const floa
   }
 }
 
-// out[j] (+)= sum_b partial[b][j], b in order.
+// Register-resident form for widths of 1024 * VPT: 256 threads, each
+// owning VPT float4 columns.  The gain and the block's partial column sums
+// stay in registers; x and dy are read once per row.
+template <int VPT>
+__global__ void __launch_bounds__(256) rms_gain_backward_reg_kernel(
+    const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ dy,
+    float* __restrict__ dx, float* __restrict__ partial, int64_t rows, float eps, int acc_dx,
+    int rows_per_block) {
+  __shared__ float red[33];
+  constexpr int kWidth = 1024 * VPT;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
+  const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
+  float4 gv[VPT], pv[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    gv[i] = ((const float4*)g)[threadIdx.x + i * 256];
+    pv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t r = r0; r < r1; ++r) {
+    const float4* xr = (const float4*)(x + r * kWidth);
+    const float4* dr = (const float4*)(dy + r * kWidth);
+    float4* or_ = (float4*)(dx + r * kWidth);
+    float4 xv[VPT], dv[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      xv[i] = xr[threadIdx.x + i * 256];
+      dv[i] = dr[threadIdx.x + i * 256];
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      acc += xv[i].x * xv[i].x;
+      acc += xv[i].y * xv[i].y;
+      acc += xv[i].z * xv[i].z;
+      acc += xv[i].w * xv[i].w;
+    }
+    const float ms = block_sum(acc, red) / (float)kWidth;
+    const float scale = 1.0f / sqrtf(ms + eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float4 v = make_float4(dv[i].x * gv[i].x, dv[i].y * gv[i].y, dv[i].z * gv[i].z, dv[i].w * gv[i].w);
+      if (acc_dx) {
+        const float4 o = or_[threadIdx.x + i * 256];
+        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+      }
+      or_[threadIdx.x + i * 256] = v;
+      pv[i].x = pv[i].x + dv[i].x * (xv[i].x * scale);
+      pv[i].y = pv[i].y + dv[i].y * (xv[i].y * scale);
+      pv[i].z = pv[i].z + dv[i].z * (xv[i].z * scale);
+      pv[i].w = pv[i].w + dv[i].w * (xv[i].w * scale);
+    }
+  }
+  float4* prow = (float4*)(partial + (int64_t)blockIdx.x * kWidth);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) prow[threadIdx.x + i * 256] = pv[i];
+}
+
+// out[j] (+)= sum_b partial[b][j], b in order; eight partial rows are
+// loaded ahead of their (ordered) additions.
 __global__ void sum_partials_kernel(const float* partial, float* out, int nblocks, int width,
                                     int accumulate) {
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < width; j += gridDim.x * blockDim.x) {
     float acc = 0.0f;
-    for (int b = 0; b < nblocks; ++b) acc = acc + partial[(int64_t)b * width + j];
+    int b = 0;
+    for (; b + 8 <= nblocks; b += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = partial[(int64_t)(b + u) * width + j];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = acc + v[u];
+    }
+    for (; b < nblocks; ++b) acc = acc + partial[(int64_t)b * width + j];
     out[j] = accumulate ? out[j] + acc : acc;
   }
 }
@@ -471,12 +535,14 @@ __global__ void masked_softmax_backward_kernel(const float* __restrict__ y, cons
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t e = i << 2;
       const int64_t col = e % k, row = (e / k) % q;
-      const float4 yv = ((const float4*)y)[i], gv = ((const float4*)g)[i];
-      float4 v;
-      v.x = col + 0 > row ? 0.0f : (yv.x * (1.0f - yv.x)) * gv.x;
-      v.y = col + 1 > row ? 0.0f : (yv.y * (1.0f - yv.y)) * gv.y;
-      v.z = col + 2 > row ? 0.0f : (yv.z * (1.0f - yv.z)) * gv.z;
-      v.w = col + 3 > row ? 0.0f : (yv.w * (1.0f - yv.w)) * gv.w;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col <= row) {  // groups wholly above the diagonal read nothing
+        const float4 yv = ((const float4*)y)[i], gv = ((const float4*)g)[i];
+        v.x = (yv.x * (1.0f - yv.x)) * gv.x;
+        v.y = col + 1 > row ? 0.0f : (yv.y * (1.0f - yv.y)) * gv.y;
+        v.z = col + 2 > row ? 0.0f : (yv.z * (1.0f - yv.z)) * gv.z;
+        v.w = col + 3 > row ? 0.0f : (yv.w * (1.0f - yv.w)) * gv.w;
+      }
       if (accumulate) {
         const float4 o = ((float4*)dx)[i];
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
@@ -493,22 +559,150 @@ __global__ void masked_softmax_backward_kernel(const float* __restrict__ y, cons
   }
 }
 
+// Row statistics in one read of the row: m = max_j x_j and
+// d = max(sum_j exp(x_j - m), f32::EPSILON), kept per thread as a running
+// (max, sum) pair rescaled when the max grows, then merged across the
+// block.  kCeUnroll float4 per thread are in flight per iteration.
+constexpr int kCeUnroll = 4;
+
+__device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;  // both empty
+  s = s * expf(m - mm) + s2 * expf(m2 - mm);
+  m = mm;
+}
+
+__device__ __forceinline__ void ms_add4(float& m, float& s, float4 v) {
+  const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+  if (mx > m) {
+    s = s * expf(m - mx);
+    m = mx;
+  }
+  s += expf(v.x - m);
+  s += expf(v.y - m);
+  s += expf(v.z - m);
+  s += expf(v.w - m);
+}
+
+// `red` holds >= 66 floats.  Every thread gets (m, d).
+__device__ void row_stats(const float* __restrict__ xr, int width, bool vec, float* red, float* m_out,
+                          float* d_out) {
+  float m = -INFINITY, s = 0.0f;
+  if (vec) {
+    const float4* x4 = (const float4*)xr;
+    const int n4 = width >> 2;
+    int j = threadIdx.x;
+    for (; j + (kCeUnroll - 1) * (int)blockDim.x < n4; j += kCeUnroll * blockDim.x) {
+      float4 v[kCeUnroll];
+#pragma unroll
+      for (int u = 0; u < kCeUnroll; ++u) v[u] = x4[j + u * blockDim.x];
+#pragma unroll
+      for (int u = 0; u < kCeUnroll; ++u) ms_add4(m, s, v[u]);
+    }
+    for (; j < n4; j += blockDim.x) ms_add4(m, s, x4[j]);
+  } else {
+    for (int j = threadIdx.x; j < width; j += blockDim.x) {
+      const float v = xr[j];
+      if (v > m) {
+        s = s * expf(m - v);
+        m = v;
+      }
+      s += expf(v - m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_merge(m, s, m2, s2);
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    red[w] = m;
+    red[32 + w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    m = lane < nw ? red[lane] : -INFINITY;
+    s = lane < nw ? red[32 + lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      ms_merge(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      red[64] = m;
+      red[65] = s;
+    }
+  }
+  __syncthreads();
+  *m_out = red[64];
+  *d_out = fmaxf(red[65], 1.1920928955078125e-7f);  // max(sum, f32::EPSILON)
+}
+
+// loss[r] = -sum_j t_j * ln(max(p_j, 1e-6)), p = softmax(x_r)  (layers.rs:301-324)
 __global__ void cross_entropy_kernel(const float* __restrict__ logits,
                                      const float* __restrict__ target, float* __restrict__ loss,
                                      int64_t rows, int width) {
-  __shared__ float red[33];
+  __shared__ float red[66];
+  const bool vec = (width & 3) == 0 && aligned16(logits) && aligned16(target);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = logits + r * width;
     const float* tr = target + r * width;
     float m, d;
-    row_max_sum(xr, width, red, &m, &d);
+    row_stats(xr, width, vec, red, &m, &d);
     float acc = 0.0f;
-    for (int j = threadIdx.x; j < width; j += blockDim.x) {
-      const float p = fmaxf(expf(xr[j] - m) / d, 1e-6f);
-      acc += tr[j] * logf(p);
+    if (vec) {
+      const int n4 = width >> 2;
+      for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+        const float4 x = ((const float4*)xr)[j], t = ((const float4*)tr)[j];
+        acc += t.x * logf(fmaxf(expf(x.x - m) / d, 1e-6f));
+        acc += t.y * logf(fmaxf(expf(x.y - m) / d, 1e-6f));
+        acc += t.z * logf(fmaxf(expf(x.z - m) / d, 1e-6f));
+        acc += t.w * logf(fmaxf(expf(x.w - m) / d, 1e-6f));
+      }
+    } else {
+      for (int j = threadIdx.x; j < width; j += blockDim.x)
+        acc += tr[j] * logf(fmaxf(expf(xr[j] - m) / d, 1e-6f));
     }
     acc = block_sum(acc, red);
     if (threadIdx.x == 0) loss[r] = 0.0f - acc;
+  }
+}
+
+// Writes softmax(x_r) - t_r into grad_r (or adds it), where t_r is the dense
+// target row or, with labels, the one-hot row of label `lab`.
+__device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const float* __restrict__ tr,
+                                            long long lab, float* __restrict__ gr, int width, bool vec,
+                                            float m, float d, int accumulate) {
+  if (vec) {
+    const int n4 = width >> 2;
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      const float4 x = ((const float4*)xr)[j];
+      float4 t;
+      if (tr) {
+        t = ((const float4*)tr)[j];
+      } else {
+        const int c = 4 * j;
+        t = make_float4(c == lab ? 1.0f : 0.0f, c + 1 == lab ? 1.0f : 0.0f, c + 2 == lab ? 1.0f : 0.0f,
+                        c + 3 == lab ? 1.0f : 0.0f);
+      }
+      float4 v = make_float4(expf(x.x - m) / d - t.x, expf(x.y - m) / d - t.y, expf(x.z - m) / d - t.z,
+                             expf(x.w - m) / d - t.w);
+      if (accumulate) {
+        const float4 o = ((const float4*)gr)[j];
+        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+      }
+      ((float4*)gr)[j] = v;
+    }
+  } else {
+    for (int j = threadIdx.x; j < width; j += blockDim.x) {
+      const float t = tr ? tr[j] : (j == lab ? 1.0f : 0.0f);
+      const float v = expf(xr[j] - m) / d - t;
+      gr[j] = accumulate ? gr[j] + v : v;
+    }
   }
 }
 
@@ -516,15 +710,12 @@ __global__ void cross_entropy_backward_kernel(const float* __restrict__ logits,
                                               const float* __restrict__ target,
                                               float* __restrict__ grad, int64_t rows, int width,
                                               int accumulate) {
-  __shared__ float red[33];
+  __shared__ float red[66];
+  const bool vec = (width & 3) == 0 && aligned16(logits) && aligned16(target) && aligned16(grad);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float* xr = logits + r * width;
     float m, d;
-    row_max_sum(xr, width, red, &m, &d);
-    for (int j = threadIdx.x; j < width; j += blockDim.x) {
-      const float v = expf(xr[j] - m) / d - target[r * width + j];
-      grad[r * width + j] = accumulate ? grad[r * width + j] + v : v;
-    }
+    row_stats(logits + r * width, width, vec, red, &m, &d);
+    ce_grad_row(logits + r * width, target + r * width, -1, grad + r * width, width, vec, m, d, accumulate);
   }
 }
 
@@ -532,11 +723,12 @@ __global__ void cross_entropy_labels_kernel(const float* __restrict__ logits,
                                             const float* __restrict__ labels,
                                             float* __restrict__ loss, int64_t rows, int width,
                                             int* err) {
-  __shared__ float red[33];
+  __shared__ float red[66];
+  const bool vec = (width & 3) == 0 && aligned16(logits);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = logits + r * width;
     float m, d;
-    row_max_sum(xr, width, red, &m, &d);
+    row_stats(xr, width, vec, red, &m, &d);
     if (threadIdx.x == 0) {
       const long long lab = rust_f32_to_i64(labels[r]);
       if (lab < 0 || lab >= width) {
@@ -554,21 +746,17 @@ __global__ void cross_entropy_labels_backward_kernel(const float* __restrict__ l
                                                      const float* __restrict__ labels,
                                                      float* __restrict__ grad, int64_t rows,
                                                      int width, int accumulate, int* err) {
-  __shared__ float red[33];
+  __shared__ float red[66];
+  const bool vec = (width & 3) == 0 && aligned16(logits) && aligned16(grad);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float* xr = logits + r * width;
-    float m, d;
-    row_max_sum(xr, width, red, &m, &d);
     const long long lab = rust_f32_to_i64(labels[r]);
     if (lab < 0 || lab >= width) {
       if (threadIdx.x == 0) atomicCAS(err, 0, (int)kErrIndexRange);
       continue;
     }
-    for (int j = threadIdx.x; j < width; j += blockDim.x) {
-      float v = expf(xr[j] - m) / d;
-      if (j == lab) v = v - 1.0f;
-      grad[r * width + j] = accumulate ? grad[r * width + j] + v : v;
-    }
+    float m, d;
+    row_stats(logits + r * width, width, vec, red, &m, &d);
+    ce_grad_row(logits + r * width, nullptr, lab, grad + r * width, width, vec, m, d, accumulate);
   }
 }
 
@@ -852,6 +1040,10 @@ int row_blocks(int64_t rows) { return (int)(rows < 148 * 64 ? (rows < 1 ? 1 : ro
 
 bool aligned16_host(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 
+// Loss rows: 512 threads with kCeUnroll float4 in flight each keep enough
+// bytes outstanding while letting 4 rows share an SM.
+int ce_threads(int64_t width) { return width >= 2048 ? 512 : row_threads(width); }
+
 void check_launch() {
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -961,7 +1153,7 @@ void launch_rms_norm_gain(const float* x, const float* g, float* out, int64_t ro
 }
 
 static int64_t rms_gain_rows_per_block(int64_t rows) {
-  int64_t rpb = ceil_div(rows, 148 * 4);
+  int64_t rpb = ceil_div(rows, 148 * 2);
   return rpb < 1 ? 1 : rpb;
 }
 
@@ -975,10 +1167,22 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
   if (rows <= 0) return;
   const int64_t rpb = rms_gain_rows_per_block(rows);
   const int nb = (int)ceil_div(rows, rpb);
-  rms_gain_backward_kernel<<<nb, row_threads(width), 0, st>>>(x, g, dy, dx, partial, rows,
-                                                              (int)width, eps, acc_dx, (int)rpb);
+  const bool reg = width % 1024 == 0 && width / 1024 <= 8 && ((width / 1024) & (width / 1024 - 1)) == 0 &&
+                   aligned16_host(x) && aligned16_host(g) && aligned16_host(dy) && aligned16_host(dx) &&
+                   aligned16_host(partial);
+  if (reg) {
+    switch (width / 1024) {
+      case 1: rms_gain_backward_reg_kernel<1><<<nb, 256, 0, st>>>(x, g, dy, dx, partial, rows, eps, acc_dx, (int)rpb); break;
+      case 2: rms_gain_backward_reg_kernel<2><<<nb, 256, 0, st>>>(x, g, dy, dx, partial, rows, eps, acc_dx, (int)rpb); break;
+      case 4: rms_gain_backward_reg_kernel<4><<<nb, 256, 0, st>>>(x, g, dy, dx, partial, rows, eps, acc_dx, (int)rpb); break;
+      default: rms_gain_backward_reg_kernel<8><<<nb, 256, 0, st>>>(x, g, dy, dx, partial, rows, eps, acc_dx, (int)rpb); break;
+    }
+  } else {
+    rms_gain_backward_kernel<<<nb, row_threads(width), 0, st>>>(x, g, dy, dx, partial, rows,
+                                                                (int)width, eps, acc_dx, (int)rpb);
+  }
   check_launch();
-  sum_partials_kernel<<<(int)ceil_div(width, 256), 256, 0, st>>>(partial, dg, nb, (int)width, acc_dg);
+  sum_partials_kernel<<<(int)ceil_div(width, 128), 128, 0, st>>>(partial, dg, nb, (int)width, acc_dg);
   check_launch();
 }
 
@@ -1029,7 +1233,7 @@ void launch_masked_softmax_backward(const float* y, const float* g, float* dx, i
 void launch_cross_entropy(const float* logits, const float* target, float* loss, int64_t rows,
                           int64_t width, cudaStream_t st) {
   if (rows <= 0) return;
-  cross_entropy_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(logits, target, loss, rows,
+  cross_entropy_kernel<<<row_blocks(rows), ce_threads(width), 0, st>>>(logits, target, loss, rows,
                                                                         (int)width);
   check_launch();
 }
@@ -1037,7 +1241,7 @@ void launch_cross_entropy(const float* logits, const float* target, float* loss,
 void launch_cross_entropy_backward(const float* logits, const float* target, float* grad,
                                    int64_t rows, int64_t width, int accumulate, cudaStream_t st) {
   if (rows <= 0) return;
-  cross_entropy_backward_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(
+  cross_entropy_backward_kernel<<<row_blocks(rows), ce_threads(width), 0, st>>>(
       logits, target, grad, rows, (int)width, accumulate);
   check_launch();
 }
@@ -1045,7 +1249,7 @@ void launch_cross_entropy_backward(const float* logits, const float* target, flo
 void launch_cross_entropy_labels(const float* logits, const float* labels, float* loss,
                                  int64_t rows, int64_t width, int* err, cudaStream_t st) {
   if (rows <= 0) return;
-  cross_entropy_labels_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(
+  cross_entropy_labels_kernel<<<row_blocks(rows), ce_threads(width), 0, st>>>(
       logits, labels, loss, rows, (int)width, err);
   check_launch();
 }
@@ -1054,7 +1258,7 @@ void launch_cross_entropy_labels_backward(const float* logits, const float* labe
                                           int64_t rows, int64_t width, int accumulate, int* err,
                                           cudaStream_t st) {
   if (rows <= 0) return;
-  cross_entropy_labels_backward_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(
+  cross_entropy_labels_backward_kernel<<<row_blocks(rows), ce_threads(width), 0, st>>>(
       logits, labels, grad, rows, (int)width, accumulate, err);
   check_launch();
 }
@@ -1194,7 +1398,7 @@ void launch_colsum(const float* g, float* out, float* partial, int64_t rows, int
   colsum_partial_kernel<<<dim3((unsigned)ceil_div(width, 256), (unsigned)chunks), 256, 0, st>>>(
       g, partial, rows, width, rpc);
   check_launch();
-  sum_partials_kernel<<<(int)ceil_div(width, 256), 256, 0, st>>>(partial, out, (int)chunks,
+  sum_partials_kernel<<<(int)ceil_div(width, 128), 128, 0, st>>>(partial, out, (int)chunks,
                                                                   (int)width, accumulate);
   check_launch();
 }
