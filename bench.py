@@ -1,24 +1,38 @@
-"""Benchmark: Llama-style decoder block, forward + backward + SGD update,
-tokens/s on 1..N B200 GPUs (one process per GPU, batch-sharded data parallel
-with an NCCL gradient all-reduce), through the tysor CUDA backend.
+"""Benchmark: training steps through the tysor CUDA backend on 1..N B200 GPUs
+(one process per GPU, batch-sharded data parallel with an NCCL gradient
+all-reduce).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload block|mlp|lm]
 
-Workload (per GPU): batch 8 x seq 2048 tokens, d_model 2048, 16 query heads
-/ 4 KV heads (repeat_kv), head_dim 128, RoPE theta 1e4, causal mask,
-RMSNorm (gain, eps 1e-6), SwiGLU hidden 5632; fp32 storage, strict 3xTF32
-tensor-core matmuls.  Inputs x ~ N(0,1) (seeded per rank), weights
-~ N(0, 0.02), gains ~ N(1, 0.02), all generated on the host from fixed
-seeds.  One step = forward, squared error against a seeded N(0,1) target
-(`d = out - target; loss = d * d`, summed as the reference sums objectives),
-backward (every parameter and input gradient), gradient all-reduce (N > 1)
-and SGD (lr 1e-6: the loss is a sum over 33.6M elements, not a mean).  Every tensor of a step is
-larger than the 126 MB L2 (x alone is 134 MB, the attention scores 2.1 GB),
-so no L2 flush is needed between steps.
+`block` (the default, the headline metric): Llama-style decoder block,
+forward + backward + SGD, tokens/s.  Per GPU: batch 8 x seq 2048 tokens,
+d_model 2048, 16 query heads / 4 KV heads (repeat_kv), head_dim 128, RoPE
+theta 1e4, causal mask, RMSNorm (gain, eps 1e-6), SwiGLU hidden 5632; fp32
+storage, strict 3xTF32 tensor-core matmuls.  Inputs x ~ N(0,1) (seeded per
+rank), weights ~ N(0, 0.02), gains ~ N(1, 0.02), all generated on the host
+from fixed seeds.  One step = forward, squared error against a seeded
+N(0,1) target (`d = out - target; loss = d * d`, summed as the reference
+sums objectives), backward (every parameter and input gradient), gradient
+all-reduce (N > 1) and SGD (lr 1e-6: the loss is a sum over 33.6M
+elements, not a mean).  Every tensor of a step is larger than the 126 MB L2
+(x alone is 134 MB, the attention scores 2.1 GB), so no L2 flush is needed
+between steps.
+
+`mlp`: two-layer MLP training, x and target [8192, 1024] ~ N(0,1) sharded by
+rows across the GPUs (strong scaling), Linear(1024->4096)+bias, ReLU,
+Linear(4096->1024)+bias, weights N(0, 0.02), biases 0, mean squared error
+(squared errors scaled by 1 / (8192 * 1024) before the trainer's sum), SGD
+lr 1e-3; rows/s.
+
+`lm`: 4-layer Llama-style LM (the block above x 4, token embedding vocab
+32000, final RMSNorm, tied output projection, next-token cross entropy on
+token ids U[0, 32000)), 8 sequences of 2048 per GPU (weak scaling), SGD
+lr 1e-3 on the per-token mean loss (applied as lr / tokens); tokens/s.
 
 `--impl reference` times the reference's own CPU algorithm (the oracle's C
 restatement of src/runtime/*.rs and src/training/*.rs) on the host cores for
-the same metric, on a bounded sample (one sequence per step).
+the same metric, on a bounded sample of the workload.
 """
 from __future__ import annotations
 
@@ -35,82 +49,223 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "Llama-block fwd+bwd tokens/s"
-B_PER_GPU, SEQ, D_MODEL, HEADS, KV_HEADS, FFN = 8, 2048, 2048, 16, 4, 5632
-LR = 1e-6  # the objective sums 33.6M squared errors (reference semantics: a sum, not a mean)
+D_MODEL, HEADS, KV_HEADS, FFN, VOCAB = 2048, 16, 4, 5632, 32000
 
 
-def block_graph(batch: int, seq: int):
-    from tysor_b200.programs import llama_block
-    return llama_block(batch=batch, seq=seq, d_model=D_MODEL, n_heads=HEADS, n_kv_heads=KV_HEADS,
-                       hidden=FFN, lr=LR, mse_target=True)
-
-
-def block_parameters(graph, seed: int = 1234):
-    """Seeded initial values for every trainable parameter of the block:
-    linear weights N(0, 0.02) of shape [in, out]; RMSNorm gains N(1, 0.02)."""
-    rng = np.random.default_rng(seed)
-    consts = {n.output: n.const for n in graph.nodes if n.kind == "const"}
-    params = {}
-    for n in graph.nodes:
-        if n.kind != "ctor":
-            continue
-        if n.op == "linear":
-            i, o = consts[n.inputs[0]], consts[n.inputs[1]]
-            params[f"linear_{n.output}_weight"] = (0.02 * rng.standard_normal(i * o)).astype(np.float32)
-        elif n.op == "RMSNorm":
-            h = consts[n.inputs[0]]
-            params[f"rmsnorm_{n.output}_gain"] = (1.0 + 0.02 * rng.standard_normal(h)).astype(np.float32)
-    return params
-
-
-def block_input(batch: int, seq: int, seed: int):
-    rng = np.random.default_rng(seed)
-    return rng.standard_normal(batch * seq * D_MODEL, dtype=np.float32)
-
-
-def block_flops(batch: int, seq: int) -> float:
-    from tysor_b200.programs import llama_block_flops
-    return llama_block_flops(batch, seq, D_MODEL, HEADS, KV_HEADS, FFN)
-
-
-# ---- CPU baseline (the oracle) ----------------------------------------------------------
-
-def cpu_sample(seconds_budget: float = 20.0):
-    """Time one fwd+bwd+SGD step of the block on the host with the oracle.
-    The sample is one sequence; its length is the largest of 2048/1024/512
-    whose estimated time (from a calibration matmul) fits the budget."""
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import local as L
-    cores = os.cpu_count() or 1
-    L.set_threads(cores)
+    L.set_threads(os.cpu_count() or 1)
+    return L
+
+
+def _oracle_params(L, params):
+    return {k: L.Tensor(list(v.shape), np.ascontiguousarray(v, np.float32).reshape(-1).copy())
+            for k, v in params.items()}
+
+
+def _calibrate(L) -> float:
+    """GFLOP/s of the oracle's matmul on this host (one [512,2048]x[2048,2048])."""
     a = L.Tensor([512, 2048], np.ones(512 * 2048, np.float32))
     b = L.Tensor([2048, 2048], np.ones(2048 * 2048, np.float32))
     t0 = time.perf_counter()
     L.matmul(a, b)
-    gflops = 2 * 512 * 2048 * 2048 / (time.perf_counter() - t0) / 1e9
-    seq = 512
-    for s in (2048, 1024):
-        if block_flops(1, s) / (gflops * 1e9) <= seconds_budget:
-            seq = s
-            break
-    g = block_graph(1, seq)
-    params = {k: L.Tensor([v.size], v) for k, v in block_parameters(g).items()}
-    # parameter shapes as the graph expects them
-    consts = {n.output: n.const for n in g.nodes if n.kind == "const"}
-    for n in g.nodes:
-        if n.kind == "ctor" and n.op == "linear":
-            params[f"linear_{n.output}_weight"].shape = [consts[n.inputs[0]], consts[n.inputs[1]]]
-    x = block_input(1, seq, 7)
-    t = block_input(1, seq, 8)
-    t0 = time.perf_counter()
-    losses, _ = L.train(g, {"x": [seq, D_MODEL], "target": [seq, D_MODEL]}, inputs={"x": x, "target": t},
-                        parameters=params, iterations=1)
-    dt = time.perf_counter() - t0
-    return {"value": seq / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"1 sequence x {seq} tokens, one fwd+bwd+SGD step of the same block "
-                      f"({dt:.1f} s; oracle matmul calibrated at {gflops:.1f} GFLOP/s)",
-            "seconds": dt, "seq": seq}
+    return 2 * 512 * 2048 * 2048 / (time.perf_counter() - t0) / 1e9
+
+
+# ---- workloads ------------------------------------------------------------------------------
+
+class Block:
+    key = "block"
+    metric = "Llama-block fwd+bwd tokens/s"
+    unit = "tokens/s"
+    scaling = "weak"
+    lr = 1e-6  # the objective sums 33.6M squared errors (reference semantics: a sum, not a mean)
+    batch, seq = 8, 2048
+    l2 = "working set larger than L2 (x 134 MB, scores 2.1 GB)"
+    # dominant GEMM as the executor issues it: [16384, 2048] . [5632, 2048]^T (both K-major)
+    roof_gemm = (16384, FFN, D_MODEL)
+
+    def graph(self, world, batch=None, seq=None):
+        from tysor_b200.programs import llama_block
+        return llama_block(batch=batch or self.batch, seq=seq or self.seq, d_model=D_MODEL, n_heads=HEADS,
+                           n_kv_heads=KV_HEADS, hidden=FFN, lr=self.lr, mse_target=True)
+
+    def step_lr(self, world):
+        return self.lr
+
+    def units(self, world):
+        return self.batch * self.seq  # tokens per rank per step
+
+    def total_units(self, world):
+        return self.units(world) * world
+
+    def shapes(self, world, tokens=None):
+        t = tokens or self.units(world)
+        return {"x": [t, D_MODEL], "target": [t, D_MODEL]}
+
+    def inputs(self, rank, world, tokens=None):
+        t = tokens or self.units(world)
+        return {"x": np.random.default_rng(1000 + rank).standard_normal(t * D_MODEL, dtype=np.float32),
+                "target": np.random.default_rng(2000 + rank).standard_normal(t * D_MODEL, dtype=np.float32)}
+
+    def config(self, world):
+        return {"workload": "llama_block fwd+bwd+sgd (B=8/GPU, S=2048, d=2048, H=16, KV=4, hd=128, ffn=5632)",
+                "model": "llama_block", "global_batch": self.batch * world, "seq_len": self.seq,
+                "parallelism": f"dp{world}", "l2": self.l2}
+
+    def cpu_sample(self, budget):
+        """One fwd+bwd+SGD step of the block for one sequence, the longest of
+        2048/1024/512 tokens whose estimated oracle time fits the budget."""
+        from tysor_b200.programs import llama_block_flops, random_parameters
+        L = _oracle()
+        gflops = _calibrate(L)
+        seq = 512
+        for s in (2048, 1024):
+            if llama_block_flops(1, s, D_MODEL, HEADS, KV_HEADS, FFN) / (gflops * 1e9) <= budget:
+                seq = s
+                break
+        g = self.graph(1, batch=1, seq=seq)
+        params = _oracle_params(L, random_parameters(g, 1234))
+        ins = self.inputs(7, 1, tokens=seq)
+        t0 = time.perf_counter()
+        L.train(g, self.shapes(1, tokens=seq), inputs=ins, parameters=params, iterations=1)
+        dt = time.perf_counter() - t0
+        return {"units": seq, "seconds": dt,
+                "sample": f"1 sequence x {seq} tokens, one fwd+bwd+SGD step of the same block "
+                          f"({dt:.1f} s; oracle matmul calibrated at {gflops:.1f} GFLOP/s)"}
+
+
+class Mlp:
+    key = "mlp"
+    metric = "two-layer MLP train rows/s"
+    unit = "rows/s"
+    scaling = "strong"
+    lr = 1e-3
+    rows, d_in, d_hidden = 8192, 1024, 4096
+    l2 = "inputs 33.6 MB and weights 16.8 MB per layer fit L2; hidden [8192,4096] 134 MB does not"
+    roof_gemm = (8192, 4096, 1024)
+
+    def graph(self, world, **kw):
+        from tysor_b200.programs import mlp_train
+        # MSE over the global batch: every rank scales its squared errors by
+        # 1 / (8192 * 1024), so the all-reduced gradient is the mean's.
+        return mlp_train(self.d_in, self.d_hidden, self.d_in, lr=self.lr, iterations=1,
+                         loss_scale=1.0 / (self.rows * self.d_in))
+
+    def step_lr(self, world):
+        return self.lr
+
+    def units(self, world):
+        from tysor_b200.dist import shard_rows
+        lo, hi = shard_rows(self.rows, 0, world)
+        return hi - lo  # rows of rank 0 (the shards are equal at 1/2/4/8 GPUs)
+
+    def total_units(self, world):
+        return self.rows
+
+    def shapes(self, world, tokens=None):
+        r = tokens or self.units(world)
+        return {"x": [r, self.d_in], "target": [r, self.d_in]}
+
+    def inputs(self, rank, world, tokens=None):
+        from tysor_b200.dist import shard_rows
+        if tokens is not None:
+            lo, n = 0, tokens
+        else:
+            lo, hi = shard_rows(self.rows, rank, world)
+            n = hi - lo
+        x = np.random.default_rng(0).standard_normal((self.rows, self.d_in), dtype=np.float32)
+        t = np.random.default_rng(1).standard_normal((self.rows, self.d_in), dtype=np.float32)
+        return {"x": np.ascontiguousarray(x[lo:lo + n]).reshape(-1),
+                "target": np.ascontiguousarray(t[lo:lo + n]).reshape(-1)}
+
+    def config(self, world):
+        return {"workload": "mlp train (x, target [8192,1024], 1024->4096->1024, relu, bias, MSE, SGD 1e-3)",
+                "model": "mlp", "global_batch": self.rows, "seq_len": 1, "parallelism": f"dp{world}",
+                "l2": self.l2}
+
+    def cpu_sample(self, budget):
+        from tysor_b200.programs import random_parameters
+        L = _oracle()
+        gflops = _calibrate(L)
+        per_row = 6 * 2 * self.d_in * self.d_hidden
+        rows = int(max(64, min(self.rows, budget * gflops * 1e9 / per_row)) // 64 * 64)
+        g = self.graph(1)
+        params = _oracle_params(L, random_parameters(g, 1234))
+        ins = self.inputs(0, 1, tokens=rows)
+        t0 = time.perf_counter()
+        L.train(g, self.shapes(1, tokens=rows), inputs=ins, parameters=params, iterations=1)
+        dt = time.perf_counter() - t0
+        return {"units": rows, "seconds": dt,
+                "sample": f"{rows} of the 8192 rows, one fwd+bwd+SGD step ({dt:.1f} s)"}
+
+
+class Lm:
+    key = "lm"
+    metric = "4-layer LM train tokens/s"
+    unit = "tokens/s"
+    scaling = "weak"
+    # lr 1e-3 on the mean over the step's tokens.  The trainer sums the
+    # per-token losses and cross_entropy's backward is softmax - target
+    # whatever the upstream gradient (layers.rs:479-488), so a scale on the
+    # loss would not reach the gradients: the mean is taken in the rate,
+    # lr / tokens (all ranks' tokens: the all-reduce sums their gradients).
+    base_lr = 1e-3
+    layers, batch, seq = 4, 8, 2048
+    l2 = "working set larger than L2 (logits 2.1 GB, scores 2.1 GB per layer)"
+    # dominant GEMM: the tied head [16384, 2048] . E^T with E [32000, 2048] (K-major)
+    roof_gemm = (16384, VOCAB, D_MODEL)
+
+    def graph(self, world, batch=None, seq=None):
+        from tysor_b200.programs import llama_lm
+        b, s = batch or self.batch, seq or self.seq
+        return llama_lm(layers=self.layers, batch=b, seq=s, d_model=D_MODEL, n_heads=HEADS,
+                        n_kv_heads=KV_HEADS, hidden=FFN, vocab=VOCAB, lr=self.base_lr / (b * s * world),
+                        iterations=1)
+
+    def units(self, world):
+        return self.batch * self.seq
+
+    def total_units(self, world):
+        return self.units(world) * world
+
+    def step_lr(self, world):
+        return self.base_lr / self.total_units(world)
+
+    def shapes(self, world, tokens=None):
+        t = tokens or self.units(world)
+        return {"ids": [t], "labels": [t]}
+
+    def inputs(self, rank, world, tokens=None):
+        t = tokens or self.units(world)
+        seq = self.seq if tokens is None else t
+        ids = np.random.default_rng(3000 + rank).integers(0, VOCAB, (t // seq, seq + 1))
+        return {"ids": np.ascontiguousarray(ids[:, :-1]).astype(np.float32).reshape(-1),
+                "labels": np.ascontiguousarray(ids[:, 1:]).astype(np.float32).reshape(-1)}
+
+    def config(self, world):
+        return {"workload": "4-layer llama LM train (8 seqs/GPU x 2048, d=2048, H=16, KV=4, ffn=5632, "
+                            "vocab 32000 tied, next-token CE, SGD 1e-3 on the per-token mean = lr/tokens)",
+                "model": "llama_lm_4l", "global_batch": self.batch * world, "seq_len": self.seq,
+                "parallelism": f"dp{world}", "l2": self.l2}
+
+    def cpu_sample(self, budget):
+        from tysor_b200.programs import random_parameters
+        L = _oracle()
+        seq = 256
+        g = self.graph(1, batch=1, seq=seq)
+        params = _oracle_params(L, random_parameters(g, 1234))
+        ins = self.inputs(0, 1, tokens=seq)
+        t0 = time.perf_counter()
+        L.train(g, self.shapes(1, tokens=seq), inputs=ins, parameters=params, iterations=1)
+        dt = time.perf_counter() - t0
+        return {"units": seq, "seconds": dt,
+                "sample": f"1 sequence x {seq} tokens (not 2048: attention is cheaper per token at this "
+                          f"length), one fwd+bwd+SGD step of the same 4-layer LM ({dt:.1f} s)"}
+
+
+WORKLOADS = {w.key: w for w in (Block(), Mlp(), Lm())}
 
 
 # ---- clocks ---------------------------------------------------------------------------------
@@ -182,22 +337,65 @@ def measured_peaks():
 
 # ---- our arm -------------------------------------------------------------------------------
 
+def roofline(ctx, lib, stream, m, n, k):
+    """The dominant strict matmul, timed alone with events on the library's
+    stream, in the layout the executor hands the kernel (A [m,k] and B
+    [n,k], both K-major); the split kernels that make the operands' low
+    parts run inside each call."""
+    import torch
+    from tysor_b200 import native
+    from tysor_b200.runtime import DeviceBuffer
+    A = DeviceBuffer.zeros(ctx, m * k)
+    Bw = DeviceBuffer.zeros(ctx, k * n)
+    C = DeviceBuffer.zeros(ctx, m * n)
+    A.write(np.random.default_rng(3).standard_normal(m * k, dtype=np.float32))
+    Bw.write(0.02 * np.random.default_rng(4).standard_normal(k * n, dtype=np.float32))
+
+    def call():
+        native.check(lib.tysor_cuda_dispatch_matmul_ex(ctx.handle, 1, m, n, k, A.handle, False, k, 0, Bw.handle,
+                                                       True, k, 0, C.handle, n, 0, None, 1.0, False, False))
+    for _ in range(3):
+        call()
+    ctx.synchronize()
+    reps = 20
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(reps):
+        call()
+    e2.record(stream)
+    ctx.synchronize()
+    e2.synchronize()
+    call_ms = s2.elapsed_time(e2) / reps
+    peaks, src = measured_peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    achieved = 2.0 * m * n * k / (call_ms / 1000.0) / 1e12
+    for buf in (A, Bw, C):
+        buf.free()
+    return {"bound": "tensor", "kernel": "matmul strict 3xTF32 (split_lo x2 + gemm_tf32_kernel<256,1,0,0>)",
+            "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
+            "tensor_pipe_frac": round(3 * achieved / tf32_peak, 4), "traffic": None,
+            "ms_per_launch": round(call_ms, 4),
+            "peak_source": f"{src}: bf16_tflops {peaks['bf16_tflops']} x 0.5 (tf32 rate is half of bf16)",
+            "note": "strict 3xTF32 issues 3 tensor-core MMAs per product: frac is capped at 0.333; "
+                    "tensor_pipe_frac counts all three"}
+
+
 def run_ours(args, rank, world, local_rank, dist):
     import torch
     from tysor_b200 import native
-    from tysor_b200.runtime import CudaContext, CudaGraphExecutor, DeviceBuffer
+    from tysor_b200.programs import random_parameters
+    from tysor_b200.runtime import CudaContext, CudaGraphExecutor
 
+    wl = WORKLOADS[args.workload]
     torch.cuda.set_device(local_rank)
     ctx = CudaContext(local_rank)
     lib = native.lib()
     stream = torch.cuda.ExternalStream(lib.tysor_cuda_context_stream(ctx.handle))
-    graph = block_graph(B_PER_GPU, SEQ)
-    tokens = B_PER_GPU * SEQ
-    x = block_input(B_PER_GPU, SEQ, 1000 + rank)
-    tgt = block_input(B_PER_GPU, SEQ, 2000 + rank)
-    params = block_parameters(graph)
-    shapes = {"x": [tokens, D_MODEL], "target": [tokens, D_MODEL]}
-    ex = CudaGraphExecutor(ctx, graph, shapes, inputs={"x": x, "target": tgt}, parameters=params)
+    graph = wl.graph(world)
+    inputs = wl.inputs(rank, world)
+    params = random_parameters(graph, 1234)
+    ex = CudaGraphExecutor(ctx, graph, wl.shapes(world), inputs=inputs, parameters=params)
 
     if world > 1:
         uid = np.zeros(128, np.uint8)
@@ -211,11 +409,12 @@ def run_ours(args, rank, world, local_rank, dist):
         ex.enable_allreduce(True)
 
     # warm-up (plans buffers, captures the step as a CUDA graph)
-    ex.train(args.warmup, LR)
+    lr = wl.step_lr(world)
+    ex.train(args.warmup, lr)
     # From here the inputs are device-resident: later calls do not re-upload
-    # them unless asked (the e2e loop below uploads both every step).
+    # them unless asked (the e2e loop below uploads them every step).
     pinned, keep = {}, []
-    for name, arr in (("x", x), ("target", tgt)):
+    for name, arr in inputs.items():
         keep.append(torch.from_numpy(arr).pin_memory())  # holds the pinned pages
         pinned[name] = keep[-1].numpy()
         native.check(lib.tysor_cuda_graph_upload_input(ex.handle, name.encode(), native.fptr(pinned[name]),
@@ -231,8 +430,13 @@ def run_ours(args, rank, world, local_rank, dist):
         sampler.start()
         time.sleep(0.5)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # A ~20 ms spin kernel ahead of the start event keeps the stream busy
+    # while the host enqueues the K steps, so a host-side stall (the boxes
+    # are VMs) cannot open gaps inside the timed region.
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(20e-3 * 1.9e9))
     start.record(stream)
-    losses = ex.train(args.steps, LR)
+    losses = ex.train(args.steps, lr)
     end.record(stream)
     ctx.synchronize()
     end.synchronize()
@@ -245,10 +449,11 @@ def run_ours(args, rank, world, local_rank, dist):
         ms = float(t.item())
         dist.barrier()
     ms_per_step = ms / args.steps
-    value = world * tokens / (ms_per_step / 1000.0)
+    total_units = wl.total_units(world)
+    value = total_units / (ms_per_step / 1000.0)
 
-    # end to end through the public API: pinned host x and target -> device,
-    # one step, loss back to the host, every step.
+    # end to end through the public API: every step uploads this rank's
+    # inputs from pinned host memory, runs one step and reads the loss back.
     e2e_steps = max(5, args.steps)
     if dist is not None:
         dist.barrier()
@@ -266,7 +471,7 @@ def run_ours(args, rank, world, local_rank, dist):
         for name, arr in pinned.items():
             native.check(lib.tysor_cuda_graph_upload_input(ex.handle, name.encode(), native.fptr(arr), arr.size))
         u1.record(stream)
-        ex.train(1, LR)  # returns the step's loss on the host
+        ex.train(1, lr)  # returns the step's loss on the host
         step_wall.append((time.perf_counter() - t1) * 1e3)
         upload_ms.append(u0.elapsed_time(u1))
     e2e_s = (time.perf_counter() - t0) / e2e_steps
@@ -276,66 +481,29 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
-    # roofline of the dominant kernel: the strict matmul of the SwiGLU
-    # projections ([16384, 2048] x [2048, 5632]), timed alone with events.
-    roof = None
-    if rank == 0:
-        m, n, k = tokens, FFN, D_MODEL
-        A = DeviceBuffer.zeros(ctx, m * k)
-        Bw = DeviceBuffer.zeros(ctx, k * n)
-        C = DeviceBuffer.zeros(ctx, m * n)
-        A.write(np.random.default_rng(3).standard_normal(m * k, dtype=np.float32))
-        Bw.write(0.02 * np.random.default_rng(4).standard_normal(k * n, dtype=np.float32))
-
-        def call():
-            native.check(lib.tysor_cuda_dispatch_matmul_ex(ctx.handle, 1, m, n, k, A.handle, False, k, 0, Bw.handle,
-                                                           False, n, 0, C.handle, n, 0, None, 1.0, False, False))
-        for _ in range(3):
-            call()
-        ctx.synchronize()
-        reps = 20
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record(stream)
-        for _ in range(reps):
-            call()
-        e2.record(stream)
-        ctx.synchronize()
-        e2.synchronize()
-        call_ms = s2.elapsed_time(e2) / reps
-        peaks, src = measured_peaks()
-        tf32_peak = peaks["bf16_tflops"] / 2.0
-        achieved = 2.0 * m * n * k / (call_ms / 1000.0) / 1e12
-        roof = {"bound": "tensor", "kernel": "matmul strict 3xTF32 (split_lo x2 + gemm_tf32_kernel)",
-                "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
-                "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4), "traffic": None,
-                "ms_per_launch": round(call_ms, 4),
-                "peak_source": f"{src}: bf16_tflops {peaks['bf16_tflops']} x 0.5 (tf32 rate is half of bf16)",
-                "note": "strict 3xTF32 issues 3 tensor-core MMAs per product: its ceiling is frac = 0.333"}
-        for buf in (A, Bw, C):
-            buf.free()
+    roof = roofline(ctx, lib, stream, *wl.roof_gemm) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample()
-        cpu.pop("seconds", None)
-        cpu.pop("seq", None)
+        info = wl.cpu_sample(args.ref_budget)
+        cpu = {"value": info["units"] / info["seconds"], "unit": wl.unit, "cores": os.cpu_count() or 1,
+               "kind": "port", "sample": info["sample"]}
 
     if rank == 0:
+        cfg = wl.config(world)
+        cfg["last_loss"] = losses[-1] if losses else None
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core matmul)",
-            "data": "synthetic, seeded: x~N(0,1), W~N(0,0.02), gain~N(1,0.02)",
-            "config": {"workload": "llama_block fwd+bwd+sgd (B=8/GPU, S=2048, d=2048, H=16, KV=4, hd=128, ffn=5632)",
-                       "model": "llama_block", "global_batch": B_PER_GPU * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world}", "l2": "working set larger than L2 (x 134 MB, scores 2.1 GB)",
-                       "last_loss": losses[-1] if losses else None},
-            "roofline": roof, "cpu_baseline": cpu,
-            "e2e": {"value": round(world * tokens / e2e_s, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(x.nbytes + tgt.nbytes), "d2h_bytes_per_step": 4,
+            "data": "synthetic, seeded on the host (inputs N(0,1) or U ids, weights N(0,0.02), gains N(1,0.02))",
+            "config": cfg, "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(total_units / e2e_s, 1), "unit": wl.unit,
+                    "h2d_bytes_per_step": int(sum(a.nbytes for a in inputs.values())), "d2h_bytes_per_step": 4,
                     "h2d_ms_per_step": [round(v, 2) for v in upload_ms],
-                    "wall_ms_per_step": [round(v, 2) for v in step_wall], "clocks": e2e_clocks},
+                    "wall_ms_per_step": [round(v, 2) for v in step_wall],
+                    "median_wall_ms": round(float(np.median(step_wall)), 2), "clocks": e2e_clocks},
             "gpu_launches": int(launches), "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -345,29 +513,33 @@ def run_ours(args, rank, world, local_rank, dist):
     ctx.close()
 
 
-# ---- reference arm ----------------------------------------------------------------------------
+# ---- reference arm --------------------------------------------------------------------------
 
 def run_reference(args, rank, world):
+    """The oracle (the reference's CPU algorithm restated in C) on this
+    host's cores; rank 0 only."""
     if rank != 0:
         return
+    wl = WORKLOADS[args.workload]
     samples = []
     info = None
     for i in range(args.warmup + args.steps):
-        info = cpu_sample(seconds_budget=args.ref_budget)
+        info = wl.cpu_sample(args.ref_budget)
         if i >= args.warmup:
             samples.append(info["seconds"])
     sec = float(np.median(samples))
-    value = info["seq"] / sec
+    value = info["units"] / sec
+    cores = os.cpu_count() or 1
+    cfg = wl.config(world)
+    cfg["parallelism"] = "cpu"
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded",
-        "config": {"workload": "llama_block fwd+bwd+sgd (d=2048, H=16, KV=4, hd=128, ffn=5632)",
-                   "model": "llama_block", "sample_seq_len": info["seq"], "parallelism": "cpu"},
-        "impl": "reference",
-        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+        "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded",
+        "config": cfg, "impl": "reference",
+        "cpu_baseline": {"value": round(value, 2), "unit": wl.unit, "cores": cores, "kind": "port",
                          "sample": info["sample"]},
-        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 2), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -378,6 +550,7 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="block", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--ref-budget", type=float, default=12.0, help="seconds per reference sample step")
     args = p.parse_args()

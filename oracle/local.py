@@ -693,6 +693,8 @@ def _forward(graph, shapes, inputs, parameters: Optional[Dict[str, Tensor]]):
             val = _binary_forward(node, values)
         elif node.kind == "primitive":
             val = ("tensor", _primitive_forward(node, values))
+        elif node.kind == "call" and node.op == "tied_logits":
+            val = ("tensor", _tied_logits_forward(node, values, parameters))
         elif node.kind == "call":
             val = ("tensor", _library_call_forward(node, values))
         elif node.kind == "ctor":
@@ -707,6 +709,32 @@ def _forward(graph, shapes, inputs, parameters: Optional[Dict[str, Tensor]]):
             raise OracleError(f"unknown node kind {node.kind}")
         values[node.output] = val
     return values
+
+
+def _tied_weight(cl: "Closure", parameters) -> Tensor:
+    """The embedding table an Embedding constructor owns: the named train
+    parameter (created on first use, as apply does) or the constant
+    pattern of --run."""
+    if parameters is None:
+        return embedding_weight(cl.num, cl.dim)
+    name = embedding_weight_name(cl.ctor_id)
+    if name not in parameters:
+        parameters[name] = embedding_weight(cl.num, cl.dim)
+    return parameters[name]
+
+
+def _tied_logits_forward(node, values, parameters) -> Tensor:
+    """Extension (no reference counterpart): `tied_logits(h, emb)` is the
+    tied output projection h . E^T with E the [num, dim] table of the
+    Embedding constructor `emb`."""
+    x = _tensor(values[node.inputs[0]])
+    callee = values.get(node.inputs[1])
+    if callee is None or callee[0] != "closure" or callee[1].kind != "embedding":
+        raise OracleError("tied_logits expects an Embedding constructor as its second argument")
+    cl = callee[1]
+    if len(x.shape) != 2 or x.shape[1] != cl.dim:
+        raise OracleError(f"tied_logits expects [rows, {cl.dim}] input, got {x.shape}")
+    return matmul(x, transpose_last2(_tied_weight(cl, parameters)))
 
 
 def _apply_forward(cl: Closure, x: Tensor, parameters):
@@ -980,6 +1008,11 @@ def compute_parameter_gradients(graph, values, oid, parameters, value_grads=None
             elif op == "transpose":
                 _acc(vgrads, node.inputs[0],
                      transpose(g, _int(values[node.inputs[1]]), _int(values[node.inputs[2]])))
+            elif op == "tied_logits":
+                cl = values[node.inputs[1]][1]
+                w = _tied_weight(cl, parameters)
+                _acc(vgrads, node.inputs[0], matmul(g, w))
+                _acc(pgrads, embedding_weight_name(cl.ctor_id), matmul(transpose_last2(g), _tensor(x)))
         elif k == "apply":
             cl = values[node.inputs[0]][1]
             x = _tensor(values.get(node.inputs[1]))

@@ -718,6 +718,20 @@ struct Executor {
       forward.push_back([=](cudaStream_t st) { launch_cross_entropy(a->p, t->p, c->p, rows, w, st); });
       return o;
     }
+    if (op == "tied_logits") {
+      // Extension: h . E^T with E the [num, dim] table of an Embedding
+      // constructor (tied output projection).  E is read K-major, as stored.
+      const HVal& x = tensor(node.inputs.at(0), "tied_logits");
+      const HVal& cl = val(node.inputs.at(1));
+      if (cl.t != HVal::Embedding) fail("tied_logits expects an Embedding constructor as its second argument");
+      if (x.shape.size() != 2 || x.shape[1] != cl.dim)
+        fail("tied_logits expects [rows, " + std::to_string(cl.dim) + "] input, got " + shape_str(x.shape));
+      Slot* w = tied_weight_slot(cl);
+      const int64_t m = x.shape[0], n = cl.num, k = cl.dim;
+      HVal o = new_tensor({m, n});
+      gemm_step(forward, 1, m, n, k, x.slot, false, k, 0, w, true, k, 0, o.slot, n, 0, nullptr, 1.0f, false, false);
+      return o;
+    }
     if (op == "reshape") {
       const HVal& x = tensor(node.inputs.at(0), "reshape");
       std::vector<int64_t> s;
@@ -860,6 +874,13 @@ struct Executor {
   std::string linear_bias_name(int id) { return "linear_" + std::to_string(id) + "_bias"; }
   std::string embedding_weight_name(int id) { return "embedding_" + std::to_string(id) + "_weight"; }
   std::string gain_name(int id) { return "rmsnorm_" + std::to_string(id) + "_gain"; }
+
+  // Table of an Embedding constructor: named parameter (train, created on
+  // first use) or the constant pattern.
+  Slot* tied_weight_slot(const HVal& cl) {
+    if (mode == kModeTrain) return ensure_param(embedding_weight_name(cl.ctor_id), {cl.num, cl.dim}, 2).value;
+    return const_pattern({cl.num, cl.dim}, 2);
+  }
 
   // Weight of a linear apply: named parameter (train) or constant pattern.
   Slot* linear_weight_slot(const HVal& cl, int64_t in_f) {
@@ -1159,6 +1180,19 @@ struct Executor {
       return;
     }
     if (!train) fail("Unsupported library op '" + op + "' in graph backward");
+    if (op == "tied_logits") {
+      // dh (+)= g . E  and  dE (+)= g^T . h  (g: [m, num], E: [num, dim])
+      const HVal& cl = val(node.inputs.at(1));
+      Slot* w = tied_weight_slot(cl);
+      const int64_t m = x.shape[0], nv = cl.num, k = cl.dim;
+      {
+        auto [d, acc] = contrib(xi);
+        gemm_step(backward, 1, m, k, nv, g, false, nv, 0, w, false, k, 0, d, k, 0, nullptr, 1.0f, acc, false);
+      }
+      auto [dw, accw] = param_contrib(embedding_weight_name(cl.ctor_id));
+      gemm_step(backward, 1, nv, k, m, g, true, nv, 0, x.slot, false, k, 0, dw, k, 0, nullptr, 1.0f, accw, false);
+      return;
+    }
     if (op == "reshape" || op == "flatten_heads") {
       if (numel(x.shape) != n) fail("reshape backward requires matching element counts");
       emit_copy(g, xi, n);

@@ -34,6 +34,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 16;  // fp32 elements of K per stage (64 bytes)
 constexpr int kThreads = 128;
+constexpr int kGroupM = 16;  // tile rows per raster group of the 1-SM kernel
 constexpr int kStages = 4;
 constexpr long long kWaitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
 
@@ -225,8 +226,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
+  // Grouped raster: consecutive CTAs take kGroupM tile rows of one tile
+  // column before moving to the next column, so the CTAs resident at once
+  // share a band of A rows and a few B columns in L2 instead of each wave
+  // streaming all of B (an [N, K] operand larger than L2 would otherwise be
+  // re-read from HBM once per tile row).
+  const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  const int per_group = kGroupM * tiles_n;
+  const int first_m = (int)(blockIdx.x / per_group) * kGroupM;
+  const int gsize = min(tiles_m - first_m, kGroupM);
+  const int in_group = (int)(blockIdx.x % per_group);
+  const int m0 = (first_m + in_group % gsize) * BM;
+  const int n0 = (in_group / gsize) * BN;
   const int bz = blockIdx.z;
   const int num_kb = (K + BK - 1) / BK;
   const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
@@ -828,7 +839,7 @@ void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  dim3 grid((unsigned)ceil_div(N, BN), (unsigned)ceil_div(M, BM), (unsigned)batch);
+  dim3 grid((unsigned)(ceil_div(N, BN) * ceil_div(M, BM)), 1u, (unsigned)batch);
   kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, C, ep, M, N, K, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);

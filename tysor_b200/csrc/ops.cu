@@ -173,8 +173,10 @@ __device__ __forceinline__ void ew_run(In<N> in, float* out, int64_t n, int acc,
   }
 }
 
-__global__ void unary_kernel(int op, const float* x, float* out, int64_t n, float p) {
-  ew_run<1>(In<1>{{x}}, out, n, 0, [=](const float (&a)[1]) { return apply_unary(op, a[0], p); });
+// The op is a template argument so the per-element body has no branch.
+template <int OP>
+__global__ void unary_kernel(const float* x, float* out, int64_t n, float p) {
+  ew_run<1>(In<1>{{x}}, out, n, 0, [=](const float (&a)[1]) { return apply_unary(OP, a[0], p); });
 }
 
 __global__ void binary_tt_kernel(int op, const float* a, const float* b, float* out, int64_t n) {
@@ -564,6 +566,7 @@ __global__ void masked_softmax_backward_kernel(const float* __restrict__ y, cons
 // (max, sum) pair rescaled when the max grows, then merged across the
 // block.  kCeUnroll float4 per thread are in flight per iteration.
 constexpr int kCeUnroll = 4;
+constexpr int kCeGradUnroll = 2;  // the gradient pass holds x, t and the old gradient per float4
 
 __device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2) {
   const float mm = fmaxf(m, m2);
@@ -643,7 +646,7 @@ __device__ void row_stats(const float* __restrict__ xr, int width, bool vec, flo
 }
 
 // loss[r] = -sum_j t_j * ln(max(p_j, 1e-6)), p = softmax(x_r)  (layers.rs:301-324)
-__global__ void cross_entropy_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 2) cross_entropy_kernel(const float* __restrict__ logits,
                                      const float* __restrict__ target, float* __restrict__ loss,
                                      int64_t rows, int width) {
   __shared__ float red[66];
@@ -656,7 +659,23 @@ __global__ void cross_entropy_kernel(const float* __restrict__ logits,
     float acc = 0.0f;
     if (vec) {
       const int n4 = width >> 2;
-      for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+      int j = threadIdx.x;
+      for (; j + (kCeUnroll - 1) * (int)blockDim.x < n4; j += kCeUnroll * blockDim.x) {
+        float4 x[kCeUnroll], t[kCeUnroll];
+#pragma unroll
+        for (int u = 0; u < kCeUnroll; ++u) {
+          x[u] = ((const float4*)xr)[j + u * blockDim.x];
+          t[u] = ((const float4*)tr)[j + u * blockDim.x];
+        }
+#pragma unroll
+        for (int u = 0; u < kCeUnroll; ++u) {
+          acc += t[u].x * logf(fmaxf(expf(x[u].x - m) / d, 1e-6f));
+          acc += t[u].y * logf(fmaxf(expf(x[u].y - m) / d, 1e-6f));
+          acc += t[u].z * logf(fmaxf(expf(x[u].z - m) / d, 1e-6f));
+          acc += t[u].w * logf(fmaxf(expf(x[u].w - m) / d, 1e-6f));
+        }
+      }
+      for (; j < n4; j += blockDim.x) {
         const float4 x = ((const float4*)xr)[j], t = ((const float4*)tr)[j];
         acc += t.x * logf(fmaxf(expf(x.x - m) / d, 1e-6f));
         acc += t.y * logf(fmaxf(expf(x.y - m) / d, 1e-6f));
@@ -673,29 +692,51 @@ __global__ void cross_entropy_kernel(const float* __restrict__ logits,
 }
 
 // Writes softmax(x_r) - t_r into grad_r (or adds it), where t_r is the dense
-// target row or, with labels, the one-hot row of label `lab`.
+// target row or, with labels, the one-hot row of label `lab`.  The row was
+// just read by row_stats, so x comes from L2 here; kCeUnroll float4 per
+// thread are loaded ahead of their use.
+__device__ __forceinline__ float4 ce_grad4(float4 x, float4 t, float m, float d) {
+  return make_float4(expf(x.x - m) / d - t.x, expf(x.y - m) / d - t.y, expf(x.z - m) / d - t.z,
+                     expf(x.w - m) / d - t.w);
+}
+
+__device__ __forceinline__ float4 onehot4(int c, long long lab) {
+  return make_float4(c == lab ? 1.0f : 0.0f, c + 1 == lab ? 1.0f : 0.0f, c + 2 == lab ? 1.0f : 0.0f,
+                     c + 3 == lab ? 1.0f : 0.0f);
+}
+
 __device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const float* __restrict__ tr,
                                             long long lab, float* __restrict__ gr, int width, bool vec,
                                             float m, float d, int accumulate) {
   if (vec) {
     const int n4 = width >> 2;
-    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
-      const float4 x = ((const float4*)xr)[j];
-      float4 t;
-      if (tr) {
-        t = ((const float4*)tr)[j];
-      } else {
-        const int c = 4 * j;
-        t = make_float4(c == lab ? 1.0f : 0.0f, c + 1 == lab ? 1.0f : 0.0f, c + 2 == lab ? 1.0f : 0.0f,
-                        c + 3 == lab ? 1.0f : 0.0f);
+    const float4* x4 = (const float4*)xr;
+    const float4* t4 = (const float4*)tr;
+    float4* g4 = (float4*)gr;
+    int j = threadIdx.x;
+    for (; j + (kCeGradUnroll - 1) * (int)blockDim.x < n4; j += kCeGradUnroll * blockDim.x) {
+      float4 x[kCeGradUnroll], t[kCeGradUnroll], o[kCeGradUnroll];
+#pragma unroll
+      for (int u = 0; u < kCeGradUnroll; ++u) {
+        const int jj = j + u * blockDim.x;
+        x[u] = x4[jj];
+        t[u] = tr ? t4[jj] : onehot4(4 * jj, lab);
+        o[u] = accumulate ? g4[jj] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      float4 v = make_float4(expf(x.x - m) / d - t.x, expf(x.y - m) / d - t.y, expf(x.z - m) / d - t.z,
-                             expf(x.w - m) / d - t.w);
+#pragma unroll
+      for (int u = 0; u < kCeGradUnroll; ++u) {
+        float4 v = ce_grad4(x[u], t[u], m, d);
+        if (accumulate) v = make_float4(o[u].x + v.x, o[u].y + v.y, o[u].z + v.z, o[u].w + v.w);
+        g4[j + u * blockDim.x] = v;
+      }
+    }
+    for (; j < n4; j += blockDim.x) {
+      float4 v = ce_grad4(x4[j], tr ? t4[j] : onehot4(4 * j, lab), m, d);
       if (accumulate) {
-        const float4 o = ((const float4*)gr)[j];
+        const float4 o = g4[j];
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
       }
-      ((float4*)gr)[j] = v;
+      g4[j] = v;
     }
   } else {
     for (int j = threadIdx.x; j < width; j += blockDim.x) {
@@ -706,7 +747,7 @@ __device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const 
   }
 }
 
-__global__ void cross_entropy_backward_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 2) cross_entropy_backward_kernel(const float* __restrict__ logits,
                                               const float* __restrict__ target,
                                               float* __restrict__ grad, int64_t rows, int width,
                                               int accumulate) {
@@ -719,7 +760,7 @@ __global__ void cross_entropy_backward_kernel(const float* __restrict__ logits,
   }
 }
 
-__global__ void cross_entropy_labels_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 2) cross_entropy_labels_kernel(const float* __restrict__ logits,
                                             const float* __restrict__ labels,
                                             float* __restrict__ loss, int64_t rows, int width,
                                             int* err) {
@@ -742,7 +783,7 @@ __global__ void cross_entropy_labels_kernel(const float* __restrict__ logits,
   }
 }
 
-__global__ void cross_entropy_labels_backward_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 2) cross_entropy_labels_backward_kernel(const float* __restrict__ logits,
                                                      const float* __restrict__ labels,
                                                      float* __restrict__ grad, int64_t rows,
                                                      int width, int accumulate, int* err) {
@@ -1065,7 +1106,14 @@ void launch_fill(float* out, int64_t n, float value, cudaStream_t st) {
 
 void launch_unary(int op, const float* x, float* out, int64_t n, float param, cudaStream_t st) {
   if (n <= 0) return;
-  unary_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(op, x, out, n, param);
+  const int blocks = elementwise_blocks((n + 3) / 4, kThreads);
+  switch (op) {
+    case kUnaryRelu: unary_kernel<kUnaryRelu><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
+    case kUnarySilu: unary_kernel<kUnarySilu><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
+    case kUnaryScale: unary_kernel<kUnaryScale><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
+    case kUnaryNeg: unary_kernel<kUnaryNeg><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
+    default: unary_kernel<-1><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
+  }
   check_launch();
 }
 

@@ -16,6 +16,8 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List
 
+import numpy as np
+
 from .graph import Graph, GraphBuilder
 
 
@@ -279,17 +281,23 @@ def matmul_relu() -> Graph:
 
 
 def mlp_train(d_in: int = 1024, d_hidden: int = 4096, d_out: int = 1024, lr: float = 1e-3,
-              iterations: int = 100) -> Graph:
+              iterations: int = 100, loss_scale: float = None) -> Graph:
     """Linear(d_in->d_hidden)+bias, ReLU, Linear(d_hidden->d_out)+bias, squared
     error summed over all elements (the reference has no MSE op; the loss is
-    `d = y - target; d * d`, summed by the trainer, executor.rs:810)."""
+    `d = y - target; d * d`, summed by the trainer, executor.rs:810).  With
+    `loss_scale` = 1 / (elements of the global batch) the squared errors are
+    scaled before the trainer sums them, which makes the objective the mean
+    squared error."""
     b = GraphBuilder()
     x, t = b.param("x"), b.param("target")
     l1 = b.let("l1", b.ctor("linear", d_in, d_hidden, True))
     l2 = b.let("l2", b.ctor("linear", d_hidden, d_out, True))
     y = b.let("y", b.apply(l2, b.call("relu", b.apply(l1, x))))
     d = b.let("d", b.binary("-", y, t))
-    b.ret(b.let("loss", b.binary("*", d, d)))
+    sq = b.binary("*", d, d)
+    if loss_scale is not None:
+        sq = b.call("scale", sq, float(loss_scale))
+    b.ret(b.let("loss", sq))
     b.train(objective="loss", lr=lr, iterations=iterations)
     return b.build()
 
@@ -312,45 +320,10 @@ def llama_block(batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: i
     `mse_target` the squared error against a `target` input,
     `d = out - target; loss = d * d` (summed by the trainer), which keeps a
     training run bounded."""
-    hd = d_model // n_heads
-    rep = n_heads // n_kv_heads
     b = GraphBuilder("block")
     x = b.param("x")
     target = b.param("target") if mse_target else None
-    n1 = b.let("attn_norm", b.ctor("RMSNorm", d_model, eps))
-    qp = b.let("q_proj", b.ctor("linear", d_model, n_heads * hd, False))
-    kp = b.let("k_proj", b.ctor("linear", d_model, n_kv_heads * hd, False))
-    vp = b.let("v_proj", b.ctor("linear", d_model, n_kv_heads * hd, False))
-    op = b.let("o_proj", b.ctor("linear", n_heads * hd, d_model, False))
-    n2 = b.let("ffn_norm", b.ctor("RMSNorm", d_model, eps))
-    gp = b.let("gate_proj", b.ctor("linear", d_model, hidden, False))
-    up = b.let("up_proj", b.ctor("linear", d_model, hidden, False))
-    dp = b.let("down_proj", b.ctor("linear", hidden, d_model, False))
-    act = b.let("act", b.ctor("SiLU"))
-    sm = b.let("softmax", b.ctor("Softmax"))
-
-    hn = b.let("hn", b.apply(n1, x))
-
-    def heads(t, nh):
-        t = b.call("reshape", t, batch, seq, nh, hd)
-        return b.call("transpose", t, 1, 2)
-
-    q = b.let("q", b.call("rope", heads(b.apply(qp, hn), n_heads), hd, theta))
-    k = b.let("k", b.call("rope", heads(b.apply(kp, hn), n_kv_heads), hd, theta))
-    v = b.let("v", heads(b.apply(vp, hn), n_kv_heads))
-    k = b.let("k", b.call("repeat_kv", k, rep))
-    v = b.let("v", b.call("repeat_kv", v, rep))
-    kt = b.call("transpose", k, 2, 3)
-    scores = b.call("scale", b.call("matmul", q, kt), 1.0 / (hd ** 0.5))
-    probs = b.let("probs", b.apply(sm, b.call("causal_mask", scores)))
-    ctx = b.call("matmul", probs, v)
-    ctx = b.call("reshape", b.call("transpose", ctx, 1, 2), batch * seq, n_heads * hd)
-    h = b.let("h", b.binary("+", x, b.apply(op, ctx)))
-
-    hn2 = b.let("hn2", b.apply(n2, h))
-    gate = b.apply(act, b.apply(gp, hn2))
-    ff = b.binary("*", gate, b.apply(up, hn2))
-    out = b.let("out", b.binary("+", h, b.apply(dp, ff)))
+    out = b.let("out", decoder_block(b, x, batch, seq, d_model, n_heads, n_kv_heads, hidden, theta, eps))
     if target is not None:
         d = b.let("d", b.binary("-", out, target))
         b.ret(b.let("loss", b.binary("*", d, d)))
@@ -359,6 +332,85 @@ def llama_block(batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: i
         b.ret(out)
         b.train(objective="out", lr=lr, iterations=1)
     return b.build()
+
+
+def decoder_block(b: GraphBuilder, x, batch: int, seq: int, d_model: int, n_heads: int, n_kv_heads: int,
+                  hidden: int, theta: float, eps: float, prefix: str = ""):
+    """Appends one decoder block to `b` and returns its output value (see
+    llama_block); `prefix` keeps the named values of stacked blocks apart."""
+    hd = d_model // n_heads
+    rep = n_heads // n_kv_heads
+    P = prefix
+    n1 = b.let(P + "attn_norm", b.ctor("RMSNorm", d_model, eps))
+    qp = b.let(P + "q_proj", b.ctor("linear", d_model, n_heads * hd, False))
+    kp = b.let(P + "k_proj", b.ctor("linear", d_model, n_kv_heads * hd, False))
+    vp = b.let(P + "v_proj", b.ctor("linear", d_model, n_kv_heads * hd, False))
+    op = b.let(P + "o_proj", b.ctor("linear", n_heads * hd, d_model, False))
+    n2 = b.let(P + "ffn_norm", b.ctor("RMSNorm", d_model, eps))
+    gp = b.let(P + "gate_proj", b.ctor("linear", d_model, hidden, False))
+    up = b.let(P + "up_proj", b.ctor("linear", d_model, hidden, False))
+    dp = b.let(P + "down_proj", b.ctor("linear", hidden, d_model, False))
+    act = b.let(P + "act", b.ctor("SiLU"))
+    sm = b.let(P + "softmax", b.ctor("Softmax"))
+
+    hn = b.let(P + "hn", b.apply(n1, x))
+
+    def heads(t, nh):
+        t = b.call("reshape", t, batch, seq, nh, hd)
+        return b.call("transpose", t, 1, 2)
+
+    q = b.let(P + "q", b.call("rope", heads(b.apply(qp, hn), n_heads), hd, theta))
+    k = b.let(P + "k", b.call("rope", heads(b.apply(kp, hn), n_kv_heads), hd, theta))
+    v = b.let(P + "v", heads(b.apply(vp, hn), n_kv_heads))
+    k = b.let(P + "k", b.call("repeat_kv", k, rep))
+    v = b.let(P + "v", b.call("repeat_kv", v, rep))
+    kt = b.call("transpose", k, 2, 3)
+    scores = b.call("scale", b.call("matmul", q, kt), 1.0 / (hd ** 0.5))
+    probs = b.let(P + "probs", b.apply(sm, b.call("causal_mask", scores)))
+    ctx = b.call("matmul", probs, v)
+    ctx = b.call("reshape", b.call("transpose", ctx, 1, 2), batch * seq, n_heads * hd)
+    h = b.let(P + "h", b.binary("+", x, b.apply(op, ctx)))
+
+    hn2 = b.let(P + "hn2", b.apply(n2, h))
+    gate = b.apply(act, b.apply(gp, hn2))
+    ff = b.binary("*", gate, b.apply(up, hn2))
+    return b.binary("+", h, b.apply(dp, ff))
+
+
+def llama_lm(layers: int = 4, batch: int = 8, seq: int = 2048, d_model: int = 2048, n_heads: int = 16,
+             n_kv_heads: int = 4, hidden: int = 5632, vocab: int = 32000, theta: float = 10000.0,
+             eps: float = 1e-6, lr: float = 1e-3, iterations: int = 50) -> Graph:
+    """Llama-style language model for next-token training:
+
+        x      = Embedding(vocab, d_model)(ids)          ids: [batch*seq] token ids
+        x      = decoder_block(x)  (x layers)
+        logits = tied_logits(RMSNorm(x), embedding)      [batch*seq, vocab]
+        loss   = cross_entropy(logits, labels)           labels: [batch*seq] ids
+
+    The output projection is tied to the embedding table (the `tied_logits`
+    extension); `labels` holds the next token of every position, and the
+    trainer sums the per-row losses (executor.rs:810)."""
+    b = GraphBuilder("lm")
+    ids, labels = b.param("ids"), b.param("labels")
+    emb = b.let("embed", b.ctor("Embedding", vocab, d_model))
+    x = b.let("x0", b.apply(emb, ids))
+    for i in range(layers):
+        x = b.let(f"x{i + 1}", decoder_block(b, x, batch, seq, d_model, n_heads, n_kv_heads, hidden, theta, eps,
+                                             prefix=f"l{i}_"))
+    norm = b.let("final_norm", b.ctor("RMSNorm", d_model, eps))
+    logits = b.let("logits", b.call("tied_logits", b.apply(norm, x), emb))
+    b.ret(b.let("loss", b.call("cross_entropy", logits, labels)))
+    b.train(objective="loss", lr=lr, iterations=iterations)
+    return b.build()
+
+
+def llama_lm_flops(layers: int, batch: int, seq: int, d_model: int, n_heads: int, n_kv_heads: int,
+                   hidden: int, vocab: int) -> float:
+    """Forward + backward FLOPs of one llama_lm step as executed (attention
+    over the full materialised score matrix; 3x the forward FLOPs)."""
+    t = batch * seq
+    head = 2.0 * t * d_model * vocab
+    return 3.0 * (layers * llama_block_flops(batch, seq, d_model, n_heads, n_kv_heads, hidden) / 3.0 + head)
 
 
 def llama_block_flops(batch: int, seq: int, d_model: int, n_heads: int, n_kv_heads: int,
@@ -372,3 +424,32 @@ def llama_block_flops(batch: int, seq: int, d_model: int, n_heads: int, n_kv_hea
     proj = 2 * t * d_model * (d_model + 2 * kv + d_model) + 2 * t * d_model * hidden * 3
     attn = 2 * 2 * batch * n_heads * seq * seq * hd
     return 3.0 * (proj + attn)
+
+
+def random_parameters(graph: Graph, seed: int = 1234, std: float = 0.02) -> Dict[str, np.ndarray]:
+    """Seeded initial values for every trainable parameter a graph's
+    constructors create under the train executor's names
+    (training/executor.rs:152-221): linear weights [in, out] and embedding
+    tables [num, dim] N(0, std), linear biases 0, RMSNorm gains N(1, std).
+    Constructors are visited in graph order, so a seed fixes every value."""
+    rng = np.random.default_rng(seed)
+    consts = {n.output: n.const for n in graph.nodes if n.kind == "const"}
+    params: Dict[str, np.ndarray] = {}
+    for n in graph.nodes:
+        if n.kind != "ctor":
+            continue
+        if n.op == "linear":
+            args = [consts[i] for i in n.inputs]
+            if len(args) < 2 or isinstance(args[1], bool):
+                raise ValueError("random_parameters needs linear(in, out[, bias]) constructors")
+            i, o = int(args[0]), int(args[1])
+            params[f"linear_{n.output}_weight"] = (std * rng.standard_normal((i, o))).astype(np.float32)
+            if len(args) > 2 and bool(args[2]):
+                params[f"linear_{n.output}_bias"] = np.zeros(o, np.float32)
+        elif n.op == "Embedding":
+            num, dim = int(consts[n.inputs[0]]), int(consts[n.inputs[1]])
+            params[f"embedding_{n.output}_weight"] = (std * rng.standard_normal((num, dim))).astype(np.float32)
+        elif n.op == "RMSNorm":
+            h = int(consts[n.inputs[0]])
+            params[f"rmsnorm_{n.output}_gain"] = (1.0 + std * rng.standard_normal(h)).astype(np.float32)
+    return params
