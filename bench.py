@@ -421,14 +421,17 @@ def run_ours(args, rank, world, local_rank, dist):
                                                        pinned[name].size))
     ctx.synchronize()
 
+    # Rank 0 samples clocks.  Every rank waits out the sampler's start-up
+    # and then meets the others, so no rank's timed region includes waiting
+    # for a peer in the first all-reduce.
     sampler = ClockSampler(gpu_index_for(local_rank)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    time.sleep(0.5)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     ctx.synchronize()
-    if sampler:
-        sampler.start()
-        time.sleep(0.5)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # A ~20 ms spin kernel ahead of the start event keeps the stream busy
     # while the host enqueues the K steps, so a host-side stall (the boxes
@@ -455,13 +458,13 @@ def run_ours(args, rank, world, local_rank, dist):
     # end to end through the public API: every step uploads this rank's
     # inputs from pinned host memory, runs one step and reads the loss back.
     e2e_steps = max(5, args.steps)
-    if dist is not None:
-        dist.barrier()
-    ctx.synchronize()
     e2e_sampler = ClockSampler(gpu_index_for(local_rank)) if rank == 0 else None
     if e2e_sampler:
         e2e_sampler.start()
-        time.sleep(0.5)
+    time.sleep(0.5)
+    if dist is not None:
+        dist.barrier()
+    ctx.synchronize()
     t0 = time.perf_counter()
     upload_ms, step_wall = [], []
     for _ in range(e2e_steps):
