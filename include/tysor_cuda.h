@@ -224,6 +224,12 @@ bool tysor_cuda_graph_backward(void* graph);
 /* --train: `iterations` SGD steps (executor.rs:764-816); losses[i] receives
  * the summed objective of step i (may be NULL). */
 bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losses);
+/* Extension (no reference counterpart): one train step launched op by op
+ * with a CUDA event after each planned step item (forward, backward, update
+ * order); item_ms[i] (i < capacity) receives item i's device time and
+ * *n_items the item count.  A profiling aid: the step is not captured. */
+bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int capacity,
+                                   int* n_items);
 /* Shape and value of any tensor value by id after a run. */
 int tysor_cuda_graph_value_rank(void* graph, int value_id);
 bool tysor_cuda_graph_value_shape(void* graph, int value_id, int64_t* dims);

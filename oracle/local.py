@@ -1095,5 +1095,7 @@ def train_step_grads(graph, shapes, inputs=None, parameters=None, value_grads=No
 # ---- text output (tensor.rs:36-69, executor.rs:794-814) -------------------------
 
 def format_tensor(t: Tensor) -> str:
-    vals = ", ".join(f"{float(v):.4f}" for v in t.data)
+    """tensor.rs:48-69 print_tensor_body; Rust's `{:.4}` prints every NaN as
+    `NaN` and infinities as `inf` / `-inf`."""
+    vals = ", ".join("NaN" if float(v) != float(v) else f"{float(v):.4f}" for v in t.data)
     return f"shape=[{', '.join(str(d) for d in t.shape)}] dtype={t.dtype}\nvalues=[{vals}]"

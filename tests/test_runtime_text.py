@@ -1,0 +1,34 @@
+"""The text the CUDA backend prints for a tensor (runtime.format_tensor)
+against the reference's print_tensor_body (tensor.rs:48-69) as the oracle
+restates it: shape list, dtype, and every value with Rust's `{:.4}`."""
+import numpy as np
+
+import local as L
+from tysor_b200.runtime import HostTensor, format_tensor
+
+
+def _both(shape, values, dtype="float32"):
+    data = np.asarray(values, np.float32)
+    got = format_tensor(HostTensor(list(shape), data, dtype))
+    want = L.format_tensor(L.Tensor(list(shape), data.copy(), dtype))
+    return got, want
+
+
+def test_known_answer():
+    got, _ = _both([2, 3], [0.125, 0.25, 0.375, 0.5, 0.625, 0.75])
+    assert got == "shape=[2, 3] dtype=float32\nvalues=[0.1250, 0.2500, 0.3750, 0.5000, 0.6250, 0.7500]"
+
+
+def test_special_values_print_like_rust():
+    got, want = _both([6], [np.nan, np.inf, -np.inf, -0.0, 1e20, -123.45675])
+    assert got == want
+    assert got.split("\n")[1] == "values=[NaN, inf, -inf, -0.0000, 100000002004087734272.0000, -123.4567]"
+
+
+def test_rounding_matches_the_oracle_on_random_values():
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([rng.standard_normal(500), rng.uniform(-1e4, 1e4, 500),
+                           np.round(rng.uniform(-10, 10, 200), 5)]).astype(np.float32)
+    got, want = _both([len(vals)], vals, "float16")
+    assert got == want
+    assert got.startswith(f"shape=[{len(vals)}] dtype=float16\n")

@@ -138,13 +138,19 @@ struct Executor {
   bool allreduce = false;
   cudaGraphExec_t exec = nullptr;
   int64_t last_launches = 0;
+  int64_t step_launches = 0;   // kernels of one train step (forward, backward, update)
+  float* loss_hist = nullptr;  // per-step losses of one train call (device)
+  int loss_hist_cap = 0;
 
   void run_uploads() {
     for (auto& [name, fn] : upload)
       if (!device_inputs.count(name)) fn(ctx->stream);
   }
 
-  ~Executor() { release(); }
+  ~Executor() {
+    release();
+    if (loss_hist) cudaFree(loss_hist);
+  }
 
   void release() {
     if (exec) cudaGraphExecDestroy(exec);
@@ -1568,8 +1574,17 @@ bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losse
     e->ensure_setup();
     e->run_uploads();
     cudaStream_t st = e->ctx->stream;
-    float* d_losses = nullptr;
-    if (iterations > 0) TYSOR_CUDA(cudaMallocAsync(&d_losses, sizeof(float) * iterations, st));
+    if (iterations > e->loss_hist_cap) {
+      // Grown outside any capture; the step loop itself allocates nothing.
+      TYSOR_CUDA(cudaStreamSynchronize(st));
+      if (e->loss_hist) TYSOR_CUDA(cudaFree(e->loss_hist));
+      e->loss_hist = nullptr;
+      e->loss_hist_cap = 0;
+      const int cap = iterations < 1024 ? 1024 : iterations;
+      TYSOR_CUDA(cudaMalloc(&e->loss_hist, sizeof(float) * cap));
+      e->loss_hist_cap = cap;
+    }
+    float* d_losses = e->loss_hist;
     auto step = [&]() {
       e->run_list(e->forward);
       e->run_list(e->backward);
@@ -1593,24 +1608,63 @@ bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losse
           TYSOR_CUDA(cudaStreamEndCapture(st, &g));
           TYSOR_CUDA(cudaGraphInstantiate(&e->exec, g, 0));
           cudaGraphDestroy(g);
-          e->last_launches = g_launches.load() - l0;
+          e->step_launches = g_launches.load() - l0;
         }
         TYSOR_CUDA(cudaGraphLaunch(e->exec, st));
       } else {
         step();
-        e->last_launches = g_launches.load() - l0;
+        e->step_launches = g_launches.load() - l0;
         e->stepped = true;
       }
-      TYSOR_CUDA(cudaMemcpyAsync(d_losses + it, e->loss->p, sizeof(float), cudaMemcpyDeviceToDevice, st));
+      // The step's loss is kept by a one-element copy kernel (no copy-engine
+      // work between the steps' kernels).
+      launch_unary(kUnaryCopy, e->loss->p, d_losses + it, 1, 0.0f, st);
+      e->last_launches = e->step_launches + 1;  // kernels per step, the loss copy included
     }
     std::vector<float> host(iterations > 0 ? iterations : 1);
-    if (iterations > 0) {
+    if (iterations > 0)
       TYSOR_CUDA(cudaMemcpyAsync(host.data(), d_losses, sizeof(float) * iterations, cudaMemcpyDeviceToHost, st));
-      TYSOR_CUDA(cudaFreeAsync(d_losses, st));
-    }
     e->ctx->sync_and_check();
     if (losses)
       for (int i = 0; i < iterations; ++i) losses[i] = host[i];
+  });
+}
+
+bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int capacity,
+                                   int* n_items) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (!n_items) throw CudaError("n_items must not be null");
+    e->plan(kModeTrain);
+    e->lr_f = (float)lr;
+    e->ensure_setup();
+    e->run_uploads();
+    cudaStream_t st = e->ctx->stream;
+    std::vector<const StepFn*> items;
+    for (const auto* list : {&e->forward, &e->backward, &e->update})
+      for (const StepFn& f : *list) items.push_back(&f);
+    std::vector<cudaEvent_t> ev(items.size() + 1, nullptr);
+    try {
+      for (auto& x : ev) TYSOR_CUDA(cudaEventCreate(&x));
+      TYSOR_CUDA(cudaEventRecord(ev[0], st));
+      for (size_t i = 0; i < items.size(); ++i) {
+        (*items[i])(st);
+        TYSOR_CUDA(cudaEventRecord(ev[i + 1], st));
+      }
+      e->ctx->sync_and_check();
+      e->stepped = true;
+      *n_items = (int)items.size();
+      for (size_t i = 0; i < items.size() && (int)i < capacity; ++i) {
+        float ms = 0.0f;
+        TYSOR_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        if (item_ms) item_ms[i] = ms;
+      }
+    } catch (...) {
+      for (auto& x : ev)
+        if (x) cudaEventDestroy(x);
+      throw;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
   });
 }
 

@@ -5,6 +5,8 @@
         `ncu --metrics gpu__time_duration.sum --csv` launch list
     python -m tysor_b200.profiling report prof.ncu-rep
         the headline metrics of an `ncu --set full` capture
+    python -m tysor_b200.profiling traffic gpurun_out/sweep_ncu.csv
+        per-launch duration and DRAM bytes of a `--metrics` capture
 """
 from __future__ import annotations
 
@@ -66,6 +68,33 @@ def report(path: str) -> str:
     return "\n".join(out)
 
 
+def traffic(path: str) -> str:
+    """Per launch of a `ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,
+    dram__bytes_write.sum --csv` log: duration, DRAM bytes read and written,
+    and the DRAM bandwidth they imply."""
+    text = open(path).read().splitlines()
+    start = next(i for i, line in enumerate(text) if line.startswith('"ID"'))
+    rows = list(csv.reader(text[start:]))
+    hdr = rows[0]
+    ii, ki, mi, ui, vi = (hdr.index(k) for k in ("ID", "Kernel Name", "Metric Name", "Metric Unit", "Metric Value"))
+    per = collections.OrderedDict()
+    for r in rows[1:]:
+        if len(r) <= vi:
+            continue
+        name = r[ki].split("(")[0].replace("(anonymous namespace)::", "")
+        scale = UNIT_NS.get(r[ui], 1.0) if r[mi] == "gpu__time_duration.sum" else \
+            {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(r[ui], 1.0)
+        per.setdefault((r[ii], name), {})[r[mi]] = float(r[vi].replace(",", "")) * scale
+    out = ["| launch | kernel | time us | DRAM read MB | DRAM write MB | DRAM GB/s |", "|---:|---|---:|---:|---:|---:|"]
+    for (lid, name), m in per.items():
+        t = m.get("gpu__time_duration.sum", 0.0)
+        rd = m.get("dram__bytes_read.sum", 0.0)
+        wr = m.get("dram__bytes_write.sum", 0.0)
+        bw = (rd + wr) / t if t else 0.0
+        out.append(f"| {lid} | `{name}` | {t / 1e3:.1f} | {rd / 1e6:.1f} | {wr / 1e6:.1f} | {bw:.0f} |")
+    return "\n".join(out)
+
+
 if __name__ == "__main__":
     kind, path = sys.argv[1], sys.argv[2]
-    print(launches(path) if kind == "launches" else report(path))
+    print({"launches": launches, "report": report, "traffic": traffic}[kind](path))

@@ -118,9 +118,16 @@ class HostTensor:
     dtype: str = "float32"
 
 
+def _format_value(v: float) -> str:
+    """Rust's `{:.4}` for an f32 (tensor.rs:63-66): correctly rounded fixed
+    point, `inf` / `-inf`, and `NaN` for every NaN."""
+    v = float(v)
+    return "NaN" if v != v else f"{v:.4f}"
+
+
 def format_tensor(t: HostTensor) -> str:
     """tensor.rs:48-69 print_tensor_body."""
-    vals = ", ".join(f"{float(v):.4f}" for v in t.data)
+    vals = ", ".join(_format_value(v) for v in t.data)
     return f"shape=[{', '.join(str(d) for d in t.shape)}] dtype={t.dtype}\nvalues=[{vals}]"
 
 
@@ -191,6 +198,17 @@ class CudaGraphExecutor:
         losses = np.zeros(max(it, 1), dtype=np.float32)
         check(self._lib.tysor_cuda_graph_train(self.handle, it, rate, fptr(losses)), "train")
         return [float(x) for x in losses[:it]]
+
+    def train_traced(self, lr: Optional[float] = None) -> np.ndarray:
+        """One train step launched op by op; returns each planned step
+        item's device milliseconds (forward, backward, update order)."""
+        rate = self.graph.lr if lr is None else float(lr)
+        n = ctypes.c_int(0)
+        check(self._lib.tysor_cuda_graph_train_traced(self.handle, rate, None, 0, ctypes.byref(n)), "train_traced")
+        ms = np.zeros(max(n.value, 1), dtype=np.float32)
+        check(self._lib.tysor_cuda_graph_train_traced(self.handle, rate, fptr(ms), ms.size, ctypes.byref(n)),
+              "train_traced")
+        return ms[:n.value]
 
     # --- results -------------------------------------------------------------
     def shape(self, value_id: int) -> List[int]:
