@@ -194,14 +194,46 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+// Tile stores from shared memory (bulk async proxy).  `add` reduces into
+// global memory (C = C + tile, round-to-nearest), which is the accumulate
+// epilogue's `existing + new`.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z,
+                                             bool add) {
+  if (add)
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            (uint64_t)map),
+        "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+  else
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     (uint64_t)map),
+                 "r"(src), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
+// Output staging for the tile-store epilogue: boxes of 32 columns x BM rows
+// (128-byte rows, 128-byte swizzle: 16-byte chunk j of row r sits at chunk
+// j ^ (r & 7)), so a warp writing 32 rows' chunk j touches every bank.
+__device__ __forceinline__ uint32_t c_stage_addr(uint32_t base, int box, int row, int chunk) {
+  return base + (uint32_t)box * (BM * 128) + (uint32_t)row * 128 + (uint32_t)((chunk ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 template <int BN, bool kStrict, bool kAmn, bool kBmn>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_blo, GemmOutput out,
-                     GemmEpilogue ep, int M, int N, int K, int* err) {
+                     const __grid_constant__ CUtensorMap map_blo,
+                     const __grid_constant__ CUtensorMap map_c, GemmOutput out,
+                     GemmEpilogue ep, int M, int N, int K, int c_tma, int* err) {
   using Cfg = PipeCfg<BN, kStrict>;
+  static_assert(Cfg::kStages * Cfg::kStageBytes >= BM * BN * 4, "output staging must fit the stage ring");
   constexpr int kA = Cfg::kA;
   constexpr int kB = Cfg::kB;
   constexpr int kStages = Cfg::kStages;
@@ -352,26 +384,30 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
+      // 16 columns per load keep acc[] and the loaded values within the
+      // 168 registers a thread has with 10 warps per SM (3 per SMSP).
 #pragma unroll
-      for (int c = 0; c < kHalf; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
+      for (int c = 0; c < kHalf; c += 16) {
+        float r[16];
+        tmem_ld16(taddr + c, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[c + i] = acc[c + i] + __uint_as_float(r[i]);
+        for (int i = 0; i < 16; ++i) acc[c + i] = acc[c + i] + r[i];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[buf]));
     }
 
-    // Epilogue: alpha, bias, relu, accumulate-into-C, store.
-    const int row = m0 + quad * 32 + lane;
+    // Epilogue: alpha, bias, relu, then the tile goes through shared memory.
+    // The stage ring is idle once the last chunk has been read (every MMA
+    // has completed), so the 128 x BN tile is staged there; TMA then writes
+    // it in 32-column boxes (full 128-byte rows rather than one 16-byte piece
+    // per row per store), or, where C's strides rule TMA out, all 256
+    // threads copy it out row-contiguously.
     const int col0 = n0 + half * kHalf;
-    if (have && row < M && col0 < N) {
-      float* crow = out.ptr + (int64_t)bz * out.batch_stride + (int64_t)row * out.ld + col0;
-      const bool vec_ok = ((out.ld & 3) == 0) && ((((uintptr_t)out.ptr) & 15) == 0) &&
-                          ((out.batch_stride & 3) == 0) && (col0 + kHalf <= N);
+    const uint32_t sbase = smem_u32(smem);
+    if (have) {
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) {
         float r = acc[i] * ep.alpha;
@@ -379,24 +415,41 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (ep.relu) r = fmaxf(r, 0.0f);
         acc[i] = r;
       }
-      if (vec_ok) {
-        float4* dst = (float4*)crow;
+      const int r_local = quad * 32 + lane;
 #pragma unroll
-        for (int q = 0; q < kHalf / 4; ++q) {
-          float4 w = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-          if (ep.accumulate) {
-            const float4 o = dst[q];
-            w.x = o.x + w.x;
-            w.y = o.y + w.y;
-            w.z = o.z + w.z;
-            w.w = o.w + w.w;
-          }
-          dst[q] = w;
-        }
-      } else {
+      for (int b = 0; b < kHalf / 32; ++b)
 #pragma unroll
-        for (int i = 0; i < kHalf; ++i)
-          if (col0 + i < N) crow[i] = ep.accumulate ? crow[i] + acc[i] : acc[i];
+        for (int j = 0; j < 8; ++j)
+          st_shared_f4(c_stage_addr(sbase, half * (kHalf / 32) + b, r_local, j), acc[b * 32 + 4 * j],
+                       acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kAccWarps) : "memory");
+    if (c_tma) {
+      if (warp == 2 && lane == 0) {
+#pragma unroll 1
+        for (int b = 0; b < BN / 32; ++b)
+          if (n0 + 32 * b < N)
+            tma_store_3d(&map_c, sbase + (uint32_t)b * (BM * 128), n0 + 32 * b, m0, bz, ep.accumulate);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      }
+    } else {
+      const int t = tid - 64;
+      float* cbase = out.ptr + (int64_t)bz * out.batch_stride;
+#pragma unroll 1
+      for (int idx = t; idx < BM * (BN / 4); idx += 32 * kAccWarps) {
+        const int r = idx / (BN / 4), c4 = idx % (BN / 4);
+        const int grow = m0 + r, gcol = n0 + 4 * c4;
+        if (grow >= M || gcol >= N) continue;
+        float v[4];
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                     : "r"(c_stage_addr(sbase, c4 >> 3, r, c4 & 7)));
+        float* dst = cbase + (int64_t)grow * out.ld + gcol;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (gcol + q < N) dst[q] = ep.accumulate ? dst[q] + v[q] : v[q];
       }
     }
   }
@@ -830,8 +883,8 @@ int64_t operand_span(const GemmOperand& X, int batch, int64_t rows, int64_t cols
 
 template <int BN, bool S, bool AMN, bool BMN>
 void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
-               const CUtensorMap& mblo, const GemmOutput& C, const GemmEpilogue& ep, int batch,
-               int M, int N, int K, int* d_err, cudaStream_t st) {
+               const CUtensorMap& mblo, const CUtensorMap& mc, int c_tma, const GemmOutput& C,
+               const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfg<BN, S>::kSmem;
   auto kern = gemm_tf32_kernel<BN, S, AMN, BMN>;
   static bool configured = false;
@@ -840,7 +893,7 @@ void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
     configured = true;
   }
   dim3 grid((unsigned)(ceil_div(N, BN) * ceil_div(M, BM)), 1u, (unsigned)batch);
-  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, C, ep, M, N, K, d_err);
+  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, mc, C, ep, M, N, K, c_tma, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
@@ -878,15 +931,15 @@ void dispatch_layout2(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorM
 
 template <int BN, bool S>
 void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
-                     const CUtensorMap& mb, const CUtensorMap& mblo, const GemmOutput& C,
-                     const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
-                     cudaStream_t st) {
+                     const CUtensorMap& mb, const CUtensorMap& mblo, const CUtensorMap& mc, int c_tma,
+                     const GemmOutput& C, const GemmEpilogue& ep, int batch, int M, int N, int K,
+                     int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_tc<BN, S, true, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else launch_tc<BN, S, true, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_tc<BN, S, true, true>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc<BN, S, true, false>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
   } else {
-    if (bmn) launch_tc<BN, S, false, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else launch_tc<BN, S, false, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_tc<BN, S, false, true>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc<BN, S, false, false>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
   }
 }
 
@@ -988,12 +1041,19 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
   if (two_sm) {
     if (strict) dispatch_layout2<256, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
     else dispatch_layout2<256, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-  } else if (BN == 128) {
-    if (strict) dispatch_layout<128, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else dispatch_layout<128, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
   } else {
-    if (strict) dispatch_layout<256, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else dispatch_layout<256, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    // The tile-store epilogue needs C's rows and batches on 16-byte strides.
+    const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
+    const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
+    CUtensorMap mc = ma;
+    if (c_tma) mc = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (BN == 128) {
+      if (strict) dispatch_layout<128, true>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+      else dispatch_layout<128, false>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    } else {
+      if (strict) dispatch_layout<256, true>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+      else dispatch_layout<256, false>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    }
   }
   return 1;
 }

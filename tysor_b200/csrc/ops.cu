@@ -747,7 +747,7 @@ __device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const 
   }
 }
 
-__global__ void __launch_bounds__(512, 2) cross_entropy_backward_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 3) cross_entropy_backward_kernel(const float* __restrict__ logits,
                                               const float* __restrict__ target,
                                               float* __restrict__ grad, int64_t rows, int width,
                                               int accumulate) {
@@ -760,7 +760,7 @@ __global__ void __launch_bounds__(512, 2) cross_entropy_backward_kernel(const fl
   }
 }
 
-__global__ void __launch_bounds__(512, 2) cross_entropy_labels_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 4) cross_entropy_labels_kernel(const float* __restrict__ logits,
                                             const float* __restrict__ labels,
                                             float* __restrict__ loss, int64_t rows, int width,
                                             int* err) {
@@ -783,7 +783,7 @@ __global__ void __launch_bounds__(512, 2) cross_entropy_labels_kernel(const floa
   }
 }
 
-__global__ void __launch_bounds__(512, 2) cross_entropy_labels_backward_kernel(const float* __restrict__ logits,
+__global__ void __launch_bounds__(512, 3) cross_entropy_labels_backward_kernel(const float* __restrict__ logits,
                                                      const float* __restrict__ labels,
                                                      float* __restrict__ grad, int64_t rows,
                                                      int width, int accumulate, int* err) {

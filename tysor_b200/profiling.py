@@ -19,7 +19,11 @@ import sys
 UNIT_NS = {"ns": 1.0, "nsecond": 1.0, "us": 1e3, "usecond": 1e3, "ms": 1e6, "msecond": 1e6}
 
 
-def launches(path: str) -> str:
+def launches(path: str, foreign: str = "at::") -> str:
+    """Per-kernel launches, device time and share; kernels whose name
+    contains `foreign` (PyTorch's own helper kernels, e.g. the spin kernel
+    the bench runs before its timed region) are listed apart and left out of
+    the shares."""
     text = open(path).read().splitlines()
     start = next(i for i, line in enumerate(text) if line.startswith('"ID"'))
     rows = list(csv.reader(text[start:]))
@@ -32,11 +36,17 @@ def launches(path: str) -> str:
         name = r[ki].split("(")[0].replace("(anonymous namespace)::", "")
         agg[name][0] += 1
         agg[name][1] += float(r[vi].replace(",", "")) * UNIT_NS.get(r[ui], 1.0)
-    total = sum(v[1] for v in agg.values())
-    out = [f"{sum(v[0] for v in agg.values())} launches, {total / 1e6:.2f} ms total (cold-cache, serialised)",
-           "", "| kernel | launches | total ms | share |", "|---|---:|---:|---:|"]
-    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
-        out.append(f"| `{name}` | {n} | {t / 1e6:.3f} | {100 * t / total:.1f}% |")
+    ours = {k: v for k, v in agg.items() if foreign not in k}
+    other = {k: v for k, v in agg.items() if foreign in k}
+    total = sum(v[1] for v in ours.values())
+    out = [f"{sum(v[0] for v in ours.values())} launches of this library, {total / 1e6:.2f} ms total "
+           "(cold-cache, serialised)", "", "| kernel | launches | total ms | share |", "|---|---:|---:|---:|"]
+    for name, (n, t) in sorted(ours.items(), key=lambda kv: -kv[1][1]):
+        short = name.replace("tysor::", "").replace("<unnamed>::", "").replace("unnamed>::", "")
+        out.append(f"| `{short}` | {n} | {t / 1e6:.3f} | "
+                   f"{100 * t / total:.1f}% |")
+    for name, (n, t) in other.items():
+        out.append(f"\nNot counted (not this library's): `{name}` x{n}, {t / 1e6:.3f} ms.")
     return "\n".join(out)
 
 
