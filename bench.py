@@ -371,7 +371,7 @@ def roofline(ctx, lib, stream, m, n, k):
     achieved = 2.0 * m * n * k / (call_ms / 1000.0) / 1e12
     for buf in (A, Bw, C):
         buf.free()
-    return {"bound": "tensor", "kernel": "matmul strict 3xTF32 (split_lo x2 + gemm_tf32_kernel<256,1,0,0>)",
+    return {"bound": "tensor", "kernel": "matmul strict 3xTF32 (split_lo x2 + gemm_tf32_2sm_kernel<256,1,0,0>, cluster pairs)",
             "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
             "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
             "tensor_pipe_frac": round(3 * achieved / tf32_peak, 4), "traffic": None,

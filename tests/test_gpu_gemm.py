@@ -144,10 +144,11 @@ def test_dispatch_matmul_metal_signature(cuda_ctx):
     np.testing.assert_array_equal(O.read().reshape(2, 4), oracle_mm(x, w))
 
 
-def test_two_sm_pair_kernel_opt_in():
-    """The cta_group::2 (cluster pair) form, enabled with
-    TYSOR_CUDA_GEMM_2SM=1, against the oracle for both operand layouts; run
-    in a child process because the switch is read at load time."""
+def test_one_sm_kernel_when_the_pair_form_is_off():
+    """The 1-SM (cta_group::1) form, selected with TYSOR_CUDA_GEMM_2SM=0
+    (the cluster-pair form is the default for 256-column tiles), against the
+    oracle for both operand layouts; run in a child process because the
+    switch is read at load time."""
     import os
     import subprocess
     import sys
@@ -175,6 +176,6 @@ for (m, n, k, ta, tb) in [(512, 512, 256, False, False), (640, 768, 96, False, T
 print("ok")
 '''
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, TYSOR_CUDA_GEMM_2SM="1")
+    env = dict(os.environ, TYSOR_CUDA_GEMM_2SM="0")
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr

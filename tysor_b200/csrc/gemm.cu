@@ -224,6 +224,68 @@ __device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, fl
                : "memory");
 }
 
+// Epilogue of one CTA's 128 x BN tile, run by the 8 accumulator warps
+// (thread = row quad*32 + lane, columns half*BN/2 ...): alpha, bias, relu,
+// then the tile goes through shared memory.  The stage ring is idle once the
+// last chunk has been read (every MMA has completed), so the tile is staged
+// there; TMA then writes it in 32-column boxes (full 128-byte rows rather
+// than one 16-byte piece per row per store; `accumulate` becomes a tile
+// reduce-add), or, where C's strides rule TMA out, all 256 threads copy it
+// out row-contiguously.
+template <int BN>
+__device__ __forceinline__ void tile_epilogue(float (&acc)[BN / 2], bool have, uint8_t* smem,
+                                              const CUtensorMap* map_c, int c_tma, const GemmOutput& out,
+                                              const GemmEpilogue& ep, int M, int N, int m0, int n0, int bz,
+                                              int quad, int half, int lane, int tid) {
+  constexpr int kHalf = BN / 2;
+  const int col0 = n0 + half * kHalf;
+  const uint32_t sbase = smem_u32(smem);
+  if (have) {
+#pragma unroll
+    for (int i = 0; i < kHalf; ++i) {
+      float r = acc[i] * ep.alpha;
+      if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
+      if (ep.relu) r = fmaxf(r, 0.0f);
+      acc[i] = r;
+    }
+    const int r_local = quad * 32 + lane;
+#pragma unroll
+    for (int b = 0; b < kHalf / 32; ++b)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        st_shared_f4(c_stage_addr(sbase, half * (kHalf / 32) + b, r_local, j), acc[b * 32 + 4 * j],
+                     acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kAccWarps) : "memory");
+  if (c_tma) {
+    if (tid == 64) {
+#pragma unroll 1
+      for (int b = 0; b < BN / 32; ++b)
+        if (n0 + 32 * b < N) tma_store_3d(map_c, sbase + (uint32_t)b * (BM * 128), n0 + 32 * b, m0, bz, ep.accumulate);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+  } else {
+    const int t = tid - 64;
+    float* cbase = out.ptr + (int64_t)bz * out.batch_stride;
+#pragma unroll 1
+    for (int idx = t; idx < BM * (BN / 4); idx += 32 * kAccWarps) {
+      const int r = idx / (BN / 4), c4 = idx % (BN / 4);
+      const int grow = m0 + r, gcol = n0 + 4 * c4;
+      if (grow >= M || gcol >= N) continue;
+      float v[4];
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                   : "r"(c_stage_addr(sbase, c4 >> 3, r, c4 & 7)));
+      float* dst = cbase + (int64_t)grow * out.ld + gcol;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (gcol + q < N) dst[q] = ep.accumulate ? dst[q] + v[q] : v[q];
+    }
+  }
+}
+
 template <int BN, bool kStrict, bool kAmn, bool kBmn>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -399,59 +461,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[buf]));
     }
 
-    // Epilogue: alpha, bias, relu, then the tile goes through shared memory.
-    // The stage ring is idle once the last chunk has been read (every MMA
-    // has completed), so the 128 x BN tile is staged there; TMA then writes
-    // it in 32-column boxes (full 128-byte rows rather than one 16-byte piece
-    // per row per store), or, where C's strides rule TMA out, all 256
-    // threads copy it out row-contiguously.
-    const int col0 = n0 + half * kHalf;
-    const uint32_t sbase = smem_u32(smem);
-    if (have) {
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        float r = acc[i] * ep.alpha;
-        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
-        if (ep.relu) r = fmaxf(r, 0.0f);
-        acc[i] = r;
-      }
-      const int r_local = quad * 32 + lane;
-#pragma unroll
-      for (int b = 0; b < kHalf / 32; ++b)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_shared_f4(c_stage_addr(sbase, half * (kHalf / 32) + b, r_local, j), acc[b * 32 + 4 * j],
-                       acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kAccWarps) : "memory");
-    if (c_tma) {
-      if (warp == 2 && lane == 0) {
-#pragma unroll 1
-        for (int b = 0; b < BN / 32; ++b)
-          if (n0 + 32 * b < N)
-            tma_store_3d(&map_c, sbase + (uint32_t)b * (BM * 128), n0 + 32 * b, m0, bz, ep.accumulate);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-      }
-    } else {
-      const int t = tid - 64;
-      float* cbase = out.ptr + (int64_t)bz * out.batch_stride;
-#pragma unroll 1
-      for (int idx = t; idx < BM * (BN / 4); idx += 32 * kAccWarps) {
-        const int r = idx / (BN / 4), c4 = idx % (BN / 4);
-        const int grow = m0 + r, gcol = n0 + 4 * c4;
-        if (grow >= M || gcol >= N) continue;
-        float v[4];
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
-                     : "r"(c_stage_addr(sbase, c4 >> 3, r, c4 & 7)));
-        float* dst = cbase + (int64_t)grow * out.ld + gcol;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (gcol + q < N) dst[q] = ep.accumulate ? dst[q] + v[q] : v[q];
-      }
-    }
+    tile_epilogue<BN>(acc, have, smem, &map_c, c_tma, out, ep, M, N, m0, n0, bz, quad, half, lane, tid);
   }
 
   tc_fence_before();
@@ -540,9 +550,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     gemm_tf32_2sm_kernel(const __grid_constant__ CUtensorMap map_a,
                          const __grid_constant__ CUtensorMap map_alo,
                          const __grid_constant__ CUtensorMap map_b,
-                         const __grid_constant__ CUtensorMap map_blo, GemmOutput out,
-                         GemmEpilogue ep, int M, int N, int K, int* err) {
+                         const __grid_constant__ CUtensorMap map_blo,
+                         const __grid_constant__ CUtensorMap map_c, GemmOutput out,
+                         GemmEpilogue ep, int M, int N, int K, int c_tma, int* err) {
   using Cfg = PipeCfg2<BN, kStrict>;
+  static_assert(Cfg::kStages * Cfg::kStageBytes >= BM * BN * 4, "output staging must fit the stage ring");
   constexpr int kA = Cfg::kA;
   constexpr int kB = Cfg::kB;
   constexpr int kStages = Cfg::kStages;
@@ -569,13 +581,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   const int lane = tid & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  // Pair index -> (row pair, column tile), column tiles fastest: consecutive
-  // pairs share their A rows, so A streams from HBM once while the (smaller)
-  // B panel stays in L2.
+  // Pair index -> (row pair, column tile) in groups of kGroupM / 2 row pairs
+  // walked column by column (the 1-SM kernel's grouped raster).
   const int n_tiles = (N + BN - 1) / BN;
+  const int pair_rows = (M + 255) / 256;
+  constexpr int kGroupP = kGroupM / 2;
   const int pair = blockIdx.x >> 1;
-  const int m0 = (pair / n_tiles) * 256 + (int)rank * BM;  // this CTA's rows
-  const int n0 = (pair % n_tiles) * BN;
+  const int per_group = kGroupP * n_tiles;
+  const int first_p = (pair / per_group) * kGroupP;
+  const int gsize = min(pair_rows - first_p, kGroupP);
+  const int in_group = pair % per_group;
+  const int m0 = (first_p + in_group % gsize) * 256 + (int)rank * BM;  // this CTA's rows
+  const int n0 = (in_group / gsize) * BN;
   const int nb0 = n0 + (int)rank * kBH;  // this CTA's half of B
   const int bz = blockIdx.z;
   const int num_kb = (K + BK - 1) / BK;
@@ -689,51 +706,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
       const uint32_t taddr =
           tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
 #pragma unroll
-      for (int c = 0; c < kHalf; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      for (int c = 0; c < kHalf; c += 16) {
+        float r[16];
+        tmem_ld16(taddr + c, r);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[c + i] = acc[c + i] + __uint_as_float(r[i]);
+        for (int i = 0; i < 16; ++i) acc[c + i] = acc[c + i] + r[i];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[buf]), 0));
     }
-
-    const int row = m0 + quad * 32 + lane;
-    const int col0 = n0 + half * kHalf;
-    if (have && row < M && col0 < N) {
-      float* crow = out.ptr + (int64_t)bz * out.batch_stride + (int64_t)row * out.ld + col0;
-      const bool vec_ok = ((out.ld & 3) == 0) && ((((uintptr_t)out.ptr) & 15) == 0) &&
-                          ((out.batch_stride & 3) == 0) && (col0 + kHalf <= N);
-#pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        float r = acc[i] * ep.alpha;
-        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
-        if (ep.relu) r = fmaxf(r, 0.0f);
-        acc[i] = r;
-      }
-      if (vec_ok) {
-        float4* dst = (float4*)crow;
-#pragma unroll
-        for (int q = 0; q < kHalf / 4; ++q) {
-          float4 w = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-          if (ep.accumulate) {
-            const float4 o = dst[q];
-            w.x = o.x + w.x;
-            w.y = o.y + w.y;
-            w.z = o.z + w.z;
-            w.w = o.w + w.w;
-          }
-          dst[q] = w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i)
-          if (col0 + i < N) crow[i] = ep.accumulate ? crow[i] + acc[i] : acc[i];
-      }
-    }
+    tile_epilogue<BN>(acc, have, smem, &map_c, c_tma, out, ep, M, N, m0, n0, bz, quad, half, lane, tid);
   }
 
   // Neither CTA may leave (releasing its shared memory and tensor memory)
@@ -900,8 +883,8 @@ void launch_tc(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
 
 template <int BN, bool S, bool AMN, bool BMN>
 void launch_tc2(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
-                const CUtensorMap& mblo, const GemmOutput& C, const GemmEpilogue& ep, int batch,
-                int M, int N, int K, int* d_err, cudaStream_t st) {
+                const CUtensorMap& mblo, const CUtensorMap& mc, int c_tma, const GemmOutput& C,
+                const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfg2<BN, S>::kSmem;
   auto kern = gemm_tf32_2sm_kernel<BN, S, AMN, BMN>;
   static bool configured = false;
@@ -910,22 +893,22 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMa
     configured = true;
   }
   dim3 grid((unsigned)(2 * ceil_div(M, 256) * ceil_div(N, BN)), 1u, (unsigned)batch);
-  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, C, ep, M, N, K, d_err);
+  kern<<<grid, kThreadsTC, smem, st>>>(ma, malo, mb, mblo, mc, C, ep, M, N, K, c_tma, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 template <int BN, bool S>
 void dispatch_layout2(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
-                      const CUtensorMap& mb, const CUtensorMap& mblo, const GemmOutput& C,
-                      const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
-                      cudaStream_t st) {
+                      const CUtensorMap& mb, const CUtensorMap& mblo, const CUtensorMap& mc, int c_tma,
+                      const GemmOutput& C, const GemmEpilogue& ep, int batch, int M, int N, int K,
+                      int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_tc2<BN, S, true, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else launch_tc2<BN, S, true, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_tc2<BN, S, true, true>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc2<BN, S, true, false>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
   } else {
-    if (bmn) launch_tc2<BN, S, false, true>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else launch_tc2<BN, S, false, false>(ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_tc2<BN, S, false, true>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    else launch_tc2<BN, S, false, false>(ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
   }
 }
 
@@ -945,14 +928,13 @@ void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMa
 
 }  // namespace
 
-// The 2-SM (cluster pair) kernel is opt-in (TYSOR_CUDA_GEMM_2SM=1).  It
-// relieves shared-memory bandwidth, which only binds when an operand is
-// M/N-major; the executor hands the GEMM K-major operands, for which the
-// 1-SM kernel already runs at the 3xTF32 tensor-core ceiling, and the pair
-// form showed step-to-step variance in the block benchmark.
+// The 2-SM (cluster pair) kernel is the default for tiles of 256 columns
+// and at least 256 rows: it halves each SM's B-operand traffic through
+// shared memory, which binds the 1-SM 128 x 256 tile (3-6% faster on every
+// measured shape).  TYSOR_CUDA_GEMM_2SM=0 selects the 1-SM kernel.
 bool g_two_sm_enabled = [] {
   const char* v = getenv("TYSOR_CUDA_GEMM_2SM");
-  return v && v[0] == '1';
+  return !(v && v[0] == '0');
 }();
 
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st) {
@@ -1038,15 +1020,15 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     malo = make_map(alo, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
     mblo = make_map(blo, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
   }
+  // The tile-store epilogue needs C's rows and batches on 16-byte strides.
+  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
+  const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
+  CUtensorMap mc = ma;
+  if (c_tma) mc = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (two_sm) {
-    if (strict) dispatch_layout2<256, true>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
-    else dispatch_layout2<256, false>(amn, bmn, ma, malo, mb, mblo, C, ep, batch, M, N, K, d_err, st);
+    if (strict) dispatch_layout2<256, true>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
+    else dispatch_layout2<256, false>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
   } else {
-    // The tile-store epilogue needs C's rows and batches on 16-byte strides.
-    const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
-    const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
-    CUtensorMap mc = ma;
-    if (c_tma) mc = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (BN == 128) {
       if (strict) dispatch_layout<128, true>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
       else dispatch_layout<128, false>(amn, bmn, ma, malo, mb, mblo, mc, c_tma, C, ep, batch, M, N, K, d_err, st);
