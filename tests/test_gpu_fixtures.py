@@ -65,3 +65,35 @@ def test_train_fixture(cuda_ctx, fx):
     for name, t in want_params.items():
         close(got_params[name], t.data, 1e-5)
     ex.close()
+
+
+def test_cli_paths_dump_full_precision_results(cuda_ctx, tmp_path, monkeypatch, capsys):
+    """run/backward/train_cuda_module print the reference's text and, with
+    TYSOR_DUMP_DIR set, write the same results as raw f32 files that match
+    the oracle at full precision (the text keeps 4 decimals)."""
+    from tysor_b200.runtime import (DUMP_ENV, backward_cuda_module, read_dump, run_cuda_module,
+                                    train_cuda_module)
+    monkeypatch.setenv(DUMP_ENV, str(tmp_path))
+    run_fx = cases("run")[0]
+    g = run_fx.build()
+    run_cuda_module(cuda_ctx, g, run_fx.shapes)
+    want, _ = L.run_forward(g, run_fx.shapes)
+    got = read_dump("output", str(tmp_path))
+    assert got.shape == want.shape
+    close(got.data, want.data, 1e-5)
+    assert "--- Execution Output ---" in capsys.readouterr().out
+
+    bw = cases("backward")[0]
+    g = bw.build()
+    backward_cuda_module(cuda_ctx, g, bw.shapes)
+    for name, wt in L.backward_report(g, bw.shapes):
+        close(read_dump(f"{name}_grad", str(tmp_path)).data, wt.data, 1e-5)
+
+    tr = cases("train")[0]
+    g = tr.build()
+    train_cuda_module(cuda_ctx, g, tr.shapes)
+    want_losses, want_params = L.train(g, tr.shapes)
+    close(read_dump("losses", str(tmp_path)).data, want_losses, 1e-4)
+    for name, t in want_params.items():
+        close(read_dump(f"param_{name}", str(tmp_path)).data, t.data, 1e-5)
+    assert "backend=cuda" in capsys.readouterr().out

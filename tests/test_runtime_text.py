@@ -32,3 +32,21 @@ def test_rounding_matches_the_oracle_on_random_values():
     got, want = _both([len(vals)], vals, "float16")
     assert got == want
     assert got.startswith(f"shape=[{len(vals)}] dtype=float16\n")
+
+
+def test_binary_dump_round_trips_bit_exactly(tmp_path):
+    """The TYSOR_DUMP_DIR side channel keeps every bit of the values."""
+    from tysor_b200.runtime import dump_tensor, read_dump
+    vals = np.random.default_rng(3).standard_normal(37).astype(np.float32)
+    vals[[0, 5]] = [np.nan, -0.0]
+    path = dump_tensor("w/eird name", HostTensor([37], vals, "float16"), str(tmp_path))
+    assert path.endswith("w_eird_name.f32")
+    back = read_dump("w/eird name", str(tmp_path))
+    assert back.shape == [37] and back.dtype == "float16"
+    np.testing.assert_array_equal(back.data.view(np.uint32), vals.view(np.uint32))
+
+
+def test_no_dump_without_a_directory(monkeypatch):
+    from tysor_b200.runtime import DUMP_ENV, dump_tensor
+    monkeypatch.delenv(DUMP_ENV, raising=False)
+    assert dump_tensor("x", HostTensor([1], np.zeros(1, np.float32))) is None

@@ -15,6 +15,9 @@ operation runs in libtysor_cuda on an sm_100 device.
 from __future__ import annotations
 
 import ctypes
+import json
+import os
+import re
 import weakref
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -275,12 +278,43 @@ class CudaGraphExecutor:
 
 # ---- reference-shaped entry points --------------------------------------------------
 
+DUMP_ENV = "TYSOR_DUMP_DIR"
+
+
+def dump_tensor(name: str, t: HostTensor, directory: Optional[str] = None) -> Optional[str]:
+    """Binary side channel next to the text output: when `directory` (or the
+    TYSOR_DUMP_DIR environment variable) is set, writes `<name>.f32` (the
+    values, little-endian f32, row-major) and `<name>.json` (shape, dtype)
+    there, so results can be compared at full precision instead of through
+    the 4-decimal text of print_tensor.  Returns the .f32 path, or None."""
+    d = directory or os.environ.get(DUMP_ENV)
+    if not d:
+        return None
+    os.makedirs(d, exist_ok=True)
+    safe = re.sub(r"[^A-Za-z0-9_.-]", "_", name)
+    path = os.path.join(d, safe + ".f32")
+    np.ascontiguousarray(np.asarray(t.data, dtype=np.float32).reshape(-1)).astype("<f4").tofile(path)
+    with open(os.path.join(d, safe + ".json"), "w") as f:
+        json.dump({"name": name, "shape": [int(x) for x in t.shape], "dtype": t.dtype}, f)
+    return path
+
+
+def read_dump(name: str, directory: str) -> HostTensor:
+    """Reads back a tensor written by dump_tensor."""
+    safe = re.sub(r"[^A-Za-z0-9_.-]", "_", name)
+    with open(os.path.join(directory, safe + ".json")) as f:
+        meta = json.load(f)
+    data = np.fromfile(os.path.join(directory, safe + ".f32"), dtype="<f4").astype(np.float32)
+    return HostTensor(list(meta["shape"]), data, meta["dtype"])
+
+
 def run_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, echo: bool = True) -> HostTensor:
     ex = CudaGraphExecutor(ctx, graph, shapes, inputs)
     try:
         out = ex.run()
     finally:
         ex.close()
+    dump_tensor("output", out)
     if echo:
         print("\n--- Execution Output ---")
         print(format_tensor(out))
@@ -294,6 +328,8 @@ def backward_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, ec
         grads = ex.backward()
     finally:
         ex.close()
+    for name, t in grads:
+        dump_tensor(f"{name}_grad", t)
     if echo:
         print("\n--- Gradient Output ---")
         for name, t in grads:
@@ -311,6 +347,10 @@ def train_cuda_module(ctx: CudaContext, graph: Graph, shapes, inputs=None, param
         params = ex.parameters()
     finally:
         ex.close()
+    dump_tensor("losses", HostTensor([len(losses)], np.asarray(losses, np.float32)))
+    for name, t in params.items():
+        flat = np.asarray(t, np.float32).reshape(-1)
+        dump_tensor(f"param_{name}", HostTensor([int(flat.size)], flat))
     if echo:
         print("\n--- Training Output ---")
         print("backend=cuda")
