@@ -230,6 +230,9 @@ bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losse
  * *n_items the item count.  A profiling aid: the step is not captured. */
 bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int capacity,
                                    int* n_items);
+/* Extension: label of traced item `item` ("fwd <op> #<value>", "bwd ...",
+ * "update ..."), valid until the next traced step; NULL if out of range. */
+const char* tysor_cuda_graph_trace_label(void* graph, int item);
 /* Shape and value of any tensor value by id after a run. */
 int tysor_cuda_graph_value_rank(void* graph, int value_id);
 bool tysor_cuda_graph_value_shape(void* graph, int value_id, int64_t* dims);

@@ -126,3 +126,50 @@ def test_block_medium_uses_transposed_operand_copies(cuda_ctx):
         assert np.isfinite(got).all(), name
         assert frob(got, gt.data) < 1e-4, name
     ex.close()
+
+
+def test_traced_step_reports_every_item_and_matches_a_plain_step(cuda_ctx):
+    """tysor_cuda_graph_train_traced runs the same step op by op: every item
+    has a forward/backward/update label and a device time, and the gradients
+    it leaves equal the oracle's."""
+    from tysor_b200.runtime import CudaGraphExecutor
+    g = llama_block(**CFG)
+    T = CFG["batch"] * CFG["seq"]
+    shapes = {"x": [T, CFG["d_model"]]}
+    x = np.random.default_rng(1).standard_normal((T, CFG["d_model"])).astype(np.float32)
+    params = params_for(g)
+    oparams = {k: L.Tensor(list(v.shape), v.reshape(-1).copy()) for k, v in params.items()}
+    _, grads, _ = L.train_step_grads(g, shapes, inputs={"x": x}, parameters=oparams)
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs={"x": x}, parameters=params)
+    items = ex.train_traced(0.0)
+    assert len(items) > 20
+    assert all(lab.split(" ")[0] in ("fwd", "bwd", "update") for lab, _ in items), items[:5]
+    assert all(ms >= 0.0 for _, ms in items)
+    assert any(lab.startswith("fwd apply linear") for lab, _ in items)
+    for name, gt in grads.items():
+        assert frob(ex.parameter_grad(name), gt.data) < 1e-4, name
+    ex.close()
+
+
+def test_fused_causal_attention_refuses_rows_whose_masked_entries_keep_probability(cuda_ctx):
+    """The causal GEMM skipping treats masked probabilities as exact zeros,
+    which holds unless a row's scores are all below about -9896 (then
+    exp(-1e4 - max) is not zero).  Such inputs are reported as an error, not
+    computed wrongly."""
+    from tysor_b200 import native
+    from tysor_b200.graph import GraphBuilder
+    from tysor_b200.runtime import CudaGraphExecutor
+    b = GraphBuilder()
+    q, k, v = b.param("q"), b.param("k"), b.param("v")
+    s = b.call("scale", b.call("matmul", q, b.call("transpose", k, 2, 3)), 0.17)
+    p = b.apply(b.ctor("Softmax"), b.call("causal_mask", s))
+    b.ret(b.let("out", b.call("matmul", p, v)))
+    b.train(objective="out", lr=0.0)
+    g = b.build()
+    shape = [1, 1, 256, 32]
+    ins = {"q": np.full(shape, -100.0, np.float32), "k": np.full(shape, 100.0, np.float32),
+           "v": np.ones(shape, np.float32)}
+    ex = CudaGraphExecutor(cuda_ctx, g, {n: shape for n in ins}, inputs=ins)
+    with pytest.raises(native.NativeError, match="fused causal attention"):
+        ex.train(1, 0.0)
+    ex.close()

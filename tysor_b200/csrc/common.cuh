@@ -22,6 +22,7 @@ enum DeviceError : int {
   kErrIndexRange = 1,      // embedding / label index outside [0, n)
   kErrBarrierTimeout = 2,  // an mbarrier wait ran past its time limit
   kErrTmemAlloc = 3,
+  kErrCausalSkip = 4,      // a fused causal softmax row gave a masked entry a nonzero probability
 };
 
 struct CudaError : std::runtime_error {
@@ -69,6 +70,12 @@ struct GemmEpilogue {
   float alpha;        // multiplies the product (1.0f for plain matmul)
   int accumulate;     // 1: C = C_old + result
   int relu;           // 1: result = max(result, 0)
+  // Causal structure of a batched attention GEMM (tensor-core kernels only;
+  // every skipped term is an exact zero or an output nobody reads):
+  // 0 none; 1 skip output tiles whose columns all exceed their rows;
+  // 2 contract only k < end of the tile's rows; 3 only k >= start of the
+  // tile's rows; 4 only k >= start of the tile's columns.
+  int tri = 0;
 };
 
 enum GemmMode : int {

@@ -87,6 +87,26 @@ struct Param {
 
 using StepFn = std::function<void(cudaStream_t)>;
 
+// A step list whose items carry the label of the graph node being planned
+// when they were added (for the traced step's per-op report).
+struct StepList {
+  std::vector<StepFn> fns;
+  std::vector<std::string> labels;
+  const std::string* cur = nullptr;
+  void push_back(StepFn f) {
+    fns.push_back(std::move(f));
+    labels.push_back(cur ? *cur : std::string());
+  }
+  void clear() {
+    fns.clear();
+    labels.clear();
+  }
+  size_t size() const { return fns.size(); }
+  bool empty() const { return fns.empty(); }
+  std::vector<StepFn>::const_iterator begin() const { return fns.begin(); }
+  std::vector<StepFn>::const_iterator end() const { return fns.end(); }
+};
+
 int64_t numel(const std::vector<int64_t>& s) {
   int64_t n = 1;
   for (auto d : s) n *= d;
@@ -121,9 +141,10 @@ struct Executor {
   std::vector<StepFn> setup;      // once per plan: constant weights, parameter init
   std::vector<std::pair<std::string, StepFn>> upload;  // once per call: graph inputs
   std::set<std::string> device_inputs;  // inputs last written by upload_input
-  std::vector<StepFn> forward;    // every step
-  std::vector<StepFn> backward;   // every step
-  std::vector<StepFn> update;     // every train step
+  std::string cur_label;         // node being planned (labels step items)
+  StepList forward{{}, {}, &cur_label};   // every step
+  StepList backward{{}, {}, &cur_label};  // every step
+  StepList update{{}, {}, &cur_label};    // every train step
   std::map<int, Slot*> vgrad;
   std::map<std::string, Param> params;
   std::vector<std::string> param_order;
@@ -139,6 +160,7 @@ struct Executor {
   cudaGraphExec_t exec = nullptr;
   int64_t last_launches = 0;
   int64_t step_launches = 0;   // kernels of one train step (forward, backward, update)
+  std::vector<std::string> trace_labels;  // item labels of the last traced step
   float* loss_hist = nullptr;  // per-step losses of one train call (device)
   int loss_hist_cap = 0;
 
@@ -171,6 +193,8 @@ struct Executor {
     deferred_matmul.clear();
     folded_scale.clear();
     masked_input.clear();
+    causal_scores.clear();
+    causal_probs.clear();
     grad_alias.clear();
     loss = grad_block = scratch = nullptr;
     scratch_floats = 0;
@@ -369,7 +393,7 @@ struct Executor {
   // both operands K-major (its fastest form).  Values are immutable within
   // a step once produced, so one preparation serves every later GEMM that
   // reads the same operand the same way.
-  Prepared prepare(std::vector<StepFn>& out, Slot* x, bool is_a, bool trans, int64_t ld, int64_t bs,
+  Prepared prepare(StepList& out, Slot* x, bool is_a, bool trans, int64_t ld, int64_t bs,
                    int batch, int64_t M, int64_t N, int64_t K) {
     const int64_t R = is_a ? (trans ? K : M) : (trans ? N : K);
     const int64_t C = is_a ? (trans ? M : K) : (trans ? K : N);
@@ -417,9 +441,10 @@ struct Executor {
     return p;
   }
 
-  void gemm_step(std::vector<StepFn>& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
+  void gemm_step(StepList& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
-                 Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu) {
+                 Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu,
+                 int tri = 0) {
     Prepared pa, pb;
     pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
     pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
@@ -435,7 +460,7 @@ struct Executor {
       GemmOperand A{pa.hi->p, pa.trans, pa.ld, pa.bs};
       GemmOperand B{pb.hi->p, pb.trans, pb.ld, pb.bs};
       GemmOutput O{c->p, ldc, sc};
-      GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0};
+      GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0, tri};
       GemmScratch s{nullptr, nullptr, 0, 0, 1};
       if (pa.lo && pb.lo) {
         s.a_lo = pa.lo->p;
@@ -450,8 +475,8 @@ struct Executor {
   // C = alpha * lhs . rhs for rank 2, or batched over equal leading dims.
   // shape_only: check and return the result's shape without planning work
   // (the value is produced later, folded into its consumer).
-  HVal plan_matmul(const HVal& l, const HVal& r, std::vector<StepFn>& out, bool shape_only = false,
-                   float alpha = 1.0f) {
+  HVal plan_matmul(const HVal& l, const HVal& r, StepList& out, bool shape_only = false,
+                   float alpha = 1.0f, int tri = 0) {
     if (l.shape.size() < 2 || r.shape.size() < 2) fail("matmul currently requires rank-2 tensors");
     if (l.shape.size() != r.shape.size()) fail("matmul currently requires rank-2 tensors");
     for (size_t i = 0; i + 2 < l.shape.size(); ++i)
@@ -472,8 +497,27 @@ struct Executor {
     }
     HVal o = new_tensor(os);
     gemm_step(out, batch, m, n, k, l.slot, false, k, m * k, r.slot, false, n, k * n, o.slot, n, m * n,
-              nullptr, alpha, false, false);
+              nullptr, alpha, false, false, tri);
     return o;
+  }
+
+  // True if `vid`'s only consumer is a causal_mask that the executor fuses
+  // with the Softmax consuming it (train and run modes).
+  bool feeds_fused_mask(int vid) const {
+    if (mode == kModeBackward) return false;
+    const GNode* c = sole_consumer(vid);
+    if (!c || c->kind != kNCall || c->op != "causal_mask") return false;
+    const GNode* p = sole_consumer(c->output);
+    return p && is_softmax_apply_of(*p, c->output);
+  }
+
+  // True if some consumer of `vid` is a matmul taking it as the left operand.
+  bool is_matmul_lhs(int vid) const {
+    for (int ci : consumers[vid]) {
+      const GNode& c = nodes[ci];
+      if (c.kind == kNPrimitive && c.op == "matmul" && !c.inputs.empty() && c.inputs[0] == vid) return true;
+    }
+    return false;
   }
 
   // The scale node of a folded matmul: one GEMM with alpha = the constant.
@@ -482,7 +526,14 @@ struct Executor {
     float f = 1.0f;
     scales_by_const(node, m, &f);
     const auto& ops = deferred_matmul.at(m);
-    return plan_matmul(val(ops.first), val(ops.second), forward, false, f);
+    // Attention scores read only through a fused causal mask: tiles wholly
+    // above the diagonal are never read, so they are not computed.
+    int tri = 0;
+    if (feeds_fused_mask(node.output) && val(ops.first).shape.size() >= 2) {
+      causal_scores.insert(m);
+      tri = 1;
+    }
+    return plan_matmul(val(ops.first), val(ops.second), forward, false, f, tri);
   }
 
   // ---- forward planning --------------------------------------------------------
@@ -518,7 +569,25 @@ struct Executor {
       }
       hv[v.id] = h;
     }
-    for (const GNode& node : nodes) hv[node.output] = plan_node(node);
+    for (const GNode& node : nodes) {
+      cur_label = "fwd " + node_label(node);
+      hv[node.output] = plan_node(node);
+    }
+    cur_label.clear();
+  }
+
+  std::string node_label(const GNode& node) const {
+    std::string what;
+    switch (node.kind) {
+      case kNBinary: what = std::string("binary ") + node.binop; break;
+      case kNApply: {
+        const GNode* c = node.inputs.empty() ? nullptr : producer_node(node.inputs[0]);
+        what = "apply " + (c ? c->op : std::string("?"));
+        break;
+      }
+      default: what = node.op; break;
+    }
+    return what + " #" + std::to_string(node.output);
   }
 
   HVal plan_node(const GNode& node) {
@@ -606,6 +675,10 @@ struct Executor {
   std::map<int, std::pair<int, int>> deferred_matmul;  // matmul out -> (lhs, rhs)
   std::map<int, int> folded_scale;          // scale node out -> matmul out
   std::map<int, int> masked_input;          // causal_mask out -> its input
+  // Fused causal attention: score matmuls (output ids) whose scaled output
+  // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
+  std::set<int> causal_scores;
+  std::set<int> causal_probs;
   std::map<int, std::pair<Slot*, float>> grad_alias;   // value -> (grad slot, factor)
 
   void build_uses() {
@@ -663,7 +736,9 @@ struct Executor {
         folded_scale[s->output] = node.output;
         return o;
       }
-      return plan_matmul(l, r, forward);
+      // Probabilities of a fused causal softmax are exact zeros above the
+      // diagonal: contract each row tile only over the keys it can see.
+      return plan_matmul(l, r, forward, false, 1.0f, causal_probs.count(node.inputs[0]) ? 2 : 0);
     }
     if (node.op == "relu") {
       const HVal& x = tensor(node.inputs.at(0), "relu");
@@ -964,7 +1039,10 @@ struct Executor {
             Slot* src = val(mi->second).slot;
             const int64_t q = x.shape[x.shape.size() - 2];
             const int64_t outer = n / (q * w);
-            forward.push_back([=](cudaStream_t st) { launch_masked_softmax(src->p, c->p, outer, q, w, st); });
+            causal_probs.insert(node.output);
+            // The guard is armed when a matmul will skip the masked entries.
+            int* err = is_matmul_lhs(node.output) ? ctx->d_err : nullptr;
+            forward.push_back([=](cudaStream_t st) { launch_masked_softmax(src->p, c->p, outer, q, w, err, st); });
           } else {
             forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
           }
@@ -1030,23 +1108,24 @@ struct Executor {
   // d(lhs) of lhs.rhs: g . rhs^T ; d(rhs): lhs^T . g  (layers.rs:521-527)
   // `alpha` scales the incoming gradient (a folded scale-by-constant).
   void emit_matmul_grads(Slot* g, const HVal& l, const HVal& r, int lid, int rid, bool want_l,
-                         bool want_r, float alpha = 1.0f) {
+                         bool want_r, float alpha = 1.0f, int tri_l = 0, int tri_r = 0) {
     const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
     std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
     const int batch = (int)numel(lead);
     if (want_l) {
       auto [d, acc] = contrib(lid);
       gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr,
-                alpha, acc, false);
+                alpha, acc, false, tri_l);
     }
     if (want_r) {
       auto [d, acc] = contrib(rid);
       gemm_step(backward, batch, k, n, m, l.slot, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr,
-                alpha, acc, false);
+                alpha, acc, false, tri_r);
     }
   }
 
   void plan_backward() {
+    cur_label = "bwd objective seed";
     const int oid = objective;
     if (oid < 0) fail("Graph does not have a return value");
     const HVal& obj = val(oid);
@@ -1060,6 +1139,7 @@ struct Executor {
     const bool train = mode == kModeTrain;
     for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
       const GNode& node = *it;
+      cur_label = "bwd " + node_label(node);
       Slot* g = nullptr;
       float galpha = 1.0f;
       auto gi = vgrad.find(node.output);
@@ -1123,7 +1203,19 @@ struct Executor {
           if (node.op == "matmul") {
             const HVal& l = val(node.inputs[0]);
             const HVal& r = val(node.inputs[1]);
-            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true, galpha);
+            // Causal attention: the score gradient is an exact zero above the
+            // diagonal (dQ contracts keys <= query, d(K^T) queries >= key); the
+            // probability gradient is read only below it, and dV contracts
+            // queries >= key.
+            int tri_l = 0, tri_r = 0;
+            if (causal_scores.count(node.output)) {
+              tri_l = 2;
+              tri_r = 4;
+            } else if (causal_probs.count(node.inputs[0])) {
+              tri_l = 1;
+              tri_r = 3;
+            }
+            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true, galpha, tri_l, tri_r);
           } else if (node.op == "relu") {
             auto [d, acc] = contrib(node.inputs[0]);
             Slot* y = out.slot;
@@ -1332,6 +1424,7 @@ struct Executor {
 
   // ---- update planning (train) ------------------------------------------------------
   void plan_update() {
+    cur_label = "update (loss, all-reduce, sgd)";
     // The loss (sum of the objective) is computed before the update, from
     // the forward values of this step (executor.rs:803-811).
     const HVal& obj = val(objective);
@@ -1417,17 +1510,18 @@ struct Executor {
     plan_forward();
     if (mode != kModeRun) plan_backward();
     if (mode == kModeTrain) plan_update();
+    cur_label.clear();
     layout();
     dirty = false;
   }
 
-  void run_list(const std::vector<StepFn>& list) {
+  void run_list(const StepList& list) {
     for (const StepFn& f : list) f(ctx->stream);
   }
 
   void ensure_setup() {
     if (setup_done) return;
-    run_list(setup);
+    for (const StepFn& f : setup) f(ctx->stream);
     setup_done = true;
   }
 };
@@ -1641,8 +1735,12 @@ bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int c
     e->run_uploads();
     cudaStream_t st = e->ctx->stream;
     std::vector<const StepFn*> items;
+    e->trace_labels.clear();
     for (const auto* list : {&e->forward, &e->backward, &e->update})
-      for (const StepFn& f : *list) items.push_back(&f);
+      for (size_t i = 0; i < list->size(); ++i) {
+        items.push_back(&list->fns[i]);
+        e->trace_labels.push_back(list->labels[i]);
+      }
     std::vector<cudaEvent_t> ev(items.size() + 1, nullptr);
     try {
       for (auto& x : ev) TYSOR_CUDA(cudaEventCreate(&x));
@@ -1666,6 +1764,16 @@ bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int c
     }
     for (auto& x : ev) cudaEventDestroy(x);
   });
+}
+
+const char* tysor_cuda_graph_trace_label(void* graph, int item) {
+  const char* out = nullptr;
+  guarded_g([&] {
+    Executor* e = E(graph);
+    if (item < 0 || item >= (int)e->trace_labels.size()) throw CudaError("no such traced item");
+    out = e->trace_labels[(size_t)item].c_str();
+  });
+  return out;
 }
 
 int tysor_cuda_graph_value_rank(void* graph, int value_id) {

@@ -194,6 +194,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+// Causal attention GEMMs (GemmEpilogue::tri): for a tile of rows
+// [r0, r0 + rows) and columns from c0, narrows the k-block range to the
+// terms that can be nonzero, or returns true when the whole output tile is
+// above the diagonal and nobody reads it (mode 1).
+__device__ __forceinline__ bool causal_range(int tri, int r0, int rows, int c0, int* kb_begin, int* kb_end) {
+  switch (tri) {
+    case 1: return c0 >= r0 + rows;
+    case 2: {
+      const int e = (r0 + rows + BK - 1) / BK;
+      if (e < *kb_end) *kb_end = e;
+      return false;
+    }
+    case 3: *kb_begin = r0 / BK; return false;
+    case 4: *kb_begin = c0 / BK; return false;
+    default: return false;
+  }
+}
+
 // Tile stores from shared memory (bulk async proxy).  `add` reduces into
 // global memory (C = C + tile, round-to-nearest), which is the accumulate
 // epilogue's `existing + new`.
@@ -333,7 +351,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int m0 = (first_m + in_group % gsize) * BM;
   const int n0 = (in_group / gsize) * BN;
   const int bz = blockIdx.z;
-  const int num_kb = (K + BK - 1) / BK;
+  int kb_begin = 0, kb_end = (K + BK - 1) / BK;
+  if (ep.tri != 0 && causal_range(ep.tri, m0, BM, n0, &kb_begin, &kb_end)) return;  // tile not needed
+  const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
   const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
 
   if (tid == 0) {
@@ -368,7 +388,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t fb = smem_u32(&full_bar[s]);
       mbar_expect_tx(fb, kTxBytes);
       const uint32_t base = smem_u32(smem + s * kStageBytes);
-      const int k0 = kb * BK;
+      const int k0 = (kb_begin + kb) * BK;
       const int nmaps = kStrict ? 2 : 1;
       for (int h = 0; h < nmaps; ++h) {
         const CUtensorMap* ma = h ? &map_alo : &map_a;
@@ -595,7 +615,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   const int n0 = (in_group / gsize) * BN;
   const int nb0 = n0 + (int)rank * kBH;  // this CTA's half of B
   const int bz = blockIdx.z;
-  const int num_kb = (K + BK - 1) / BK;
+  int kb_begin = 0, kb_end = (K + BK - 1) / BK;
+  // Decided on the pair's 256 rows, so both CTAs agree (and leave together,
+  // before any cluster barrier, when the tile is not needed).
+  if (ep.tri != 0 && causal_range(ep.tri, m0 - (int)rank * BM, 2 * BM, n0, &kb_begin, &kb_end)) return;
+  const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
   const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
 
   if (tid == 0) {
@@ -630,7 +654,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
       const uint32_t fb = smem_u32(&full_bar[s]);
       if (leader) mbar_expect_tx(fb, kTxBytes);
       const uint32_t base = smem_u32(smem + s * kStageBytes);
-      const int k0 = kb * BK;
+      const int k0 = (kb_begin + kb) * BK;
       const int nmaps = kStrict ? 2 : 1;
       for (int h = 0; h < nmaps; ++h) {
         const CUtensorMap* ma = h ? &map_alo : &map_a;

@@ -425,7 +425,7 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
 template <int VPT>
 __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restrict__ x,
                                                           float* __restrict__ out, int64_t rows,
-                                                          int q, int masked) {
+                                                          int q, int masked, int* err) {
   __shared__ float red[33];
   constexpr int kWidth = 1024 * VPT;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -447,6 +447,10 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
       m = fmaxf(fmaxf(fmaxf(m, t.x), fmaxf(t.y, t.z)), t.w);
     }
     m = block_max(m, red);
+    // With `err`, later GEMMs skip the masked entries as exact zeros; flag the
+    // (scores below about -9896) rows where exp(-1e4 - max) is not zero.
+    if (err != nullptr && threadIdx.x == 0 && qi < kWidth - 1 && expf(-1.0e4f - m) != 0.0f)
+      atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -476,7 +480,7 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
 // Row r of [outer*q] rows of width k; row index within its q x k block is
 // r % q.  Values with col > row read as -1e4.
 __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                      int64_t rows, int q, int width) {
+                                      int64_t rows, int q, int width, int* err) {
   __shared__ float red[33];
   const bool vec = (width & 3) == 0 && aligned16(x) && aligned16(out);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -497,6 +501,8 @@ __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __rest
       for (int j = threadIdx.x; j < width; j += blockDim.x) m = fmaxf(m, j > qi ? -1.0e4f : xr[j]);
     }
     m = block_max(m, red);
+    if (err != nullptr && threadIdx.x == 0 && qi < width - 1 && expf(-1.0e4f - m) != 0.0f)
+      atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
     if (vec) {
       for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
@@ -1236,24 +1242,24 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
 
 // Launches the register-resident form when the width allows; false if not.
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 cudaStream_t st);
+                 int* err, cudaStream_t st);
 
 void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st) {
   if (rows <= 0) return;
-  if (softmax_reg(x, out, rows, width, 1, 0, st)) return;
+  if (softmax_reg(x, out, rows, width, 1, 0, nullptr, st)) return;
   softmax_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(x, out, rows, (int)width);
   check_launch();
 }
 
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 cudaStream_t st) {
+                 int* err, cudaStream_t st) {
   if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out)) return false;
   const int blocks = row_blocks(rows);
   switch (width / 1024) {
-    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
-    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
-    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
-    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked); break;
+    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
+    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
+    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
+    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
     default: return false;
   }
   check_launch();
@@ -1261,11 +1267,11 @@ bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_
 }
 
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           cudaStream_t st) {
+                           int* err, cudaStream_t st) {
   const int64_t rows = outer * q;
   if (rows <= 0) return;
-  if (softmax_reg(x, out, rows, k, q, 1, st)) return;
-  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k);
+  if (softmax_reg(x, out, rows, k, q, 1, err, st)) return;
+  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k, err);
   check_launch();
 }
 

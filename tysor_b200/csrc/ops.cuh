@@ -64,8 +64,11 @@ void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cud
 // Softmax of causal_mask(x) over [outer][q][k] in one pass: entries with
 // col > row take the mask's -1e4 (layers.rs:217-236), then the row softmax
 // (tensor.rs:235-260) — the same arithmetic as the two ops in sequence.
+// With `err`, a row whose masked entries would get a nonzero probability
+// (possible only when its scores are all below about -9896) records
+// kErrCausalSkip: GEMMs that treat those entries as zeros would be wrong.
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           cudaStream_t st);
+                           int* err, cudaStream_t st);
 // Backward of Softmax(causal_mask(x)) with the reference rules: the
 // diagonal softmax term y(1-y)g (layers.rs:350-364), then the mask zeroes
 // col > row (layers.rs:418-436): dx (+)= col > row ? 0 : y(1-y)g.

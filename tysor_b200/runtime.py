@@ -202,16 +202,17 @@ class CudaGraphExecutor:
         check(self._lib.tysor_cuda_graph_train(self.handle, it, rate, fptr(losses)), "train")
         return [float(x) for x in losses[:it]]
 
-    def train_traced(self, lr: Optional[float] = None) -> np.ndarray:
-        """One train step launched op by op; returns each planned step
-        item's device milliseconds (forward, backward, update order)."""
+    def train_traced(self, lr: Optional[float] = None) -> List[Tuple[str, float]]:
+        """One train step launched op by op; returns (label, device ms) for
+        each planned step item, in forward, backward, update order."""
         rate = self.graph.lr if lr is None else float(lr)
         n = ctypes.c_int(0)
         check(self._lib.tysor_cuda_graph_train_traced(self.handle, rate, None, 0, ctypes.byref(n)), "train_traced")
         ms = np.zeros(max(n.value, 1), dtype=np.float32)
         check(self._lib.tysor_cuda_graph_train_traced(self.handle, rate, fptr(ms), ms.size, ctypes.byref(n)),
               "train_traced")
-        return ms[:n.value]
+        labels = [(self._lib.tysor_cuda_graph_trace_label(self.handle, i) or b"").decode() for i in range(n.value)]
+        return list(zip(labels, [float(v) for v in ms[:n.value]]))
 
     # --- results -------------------------------------------------------------
     def shape(self, value_id: int) -> List[int]:
