@@ -179,3 +179,21 @@ print("ok")
     env = dict(os.environ, TYSOR_CUDA_GEMM_2SM="0")
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (False, False)])
+def test_persistent_pair_kernel_many_tiles_per_cluster(cuda_ctx, ta, tb):
+    """Shapes with several 256-row tiles per resident cluster (the persistent
+    schedule), both B tile widths (N > 128 and N <= 128), batched, with the
+    accumulate / alpha / bias epilogue."""
+    rng = np.random.default_rng(11)
+    for (bt, m, n, k) in [(3, 1024, 1000, 200), (2, 2048, 128, 336)]:
+        a = rng.uniform(-1, 1, (bt, m, k)).astype(np.float32)
+        b = rng.uniform(-1, 1, (bt, k, n)).astype(np.float32)
+        c0 = rng.uniform(-1, 1, (bt, m, n)).astype(np.float32)
+        a_st = np.ascontiguousarray(a.transpose(0, 2, 1)) if ta else a
+        b_st = np.ascontiguousarray(b.transpose(0, 2, 1)) if tb else b
+        got = run_ex(cuda_ctx, a_st, ta, b_st, tb, m, n, k, batch=bt, alpha=0.75, acc=c0)
+        for i in range(bt):
+            want = c0[i] + oracle_mm(a[i], b[i]) * np.float32(0.75)
+            assert frob(got[i], want) < 1e-5, (bt, m, n, k, i)

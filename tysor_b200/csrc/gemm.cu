@@ -752,6 +752,277 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent cluster-pair form.  One cluster of two CTAs per pair of SMs
+// stays resident and walks output tiles (256 x BN, BN = 256 or 128) in the
+// grouped raster order, tile t, t + clusters, ...  The TMA / MMA stage ring
+// and the two tensor-memory chunk buffers keep running counters across
+// tiles, so the producer loads and the MMAs of the next tile proceed while
+// the accumulator warps finish the previous one: each warp writes its 32 x
+// BN/2 part of the tile through two 4 KB shared-memory boxes (32 rows x 32
+// columns, 128-byte swizzle) with TMA tile stores (reduce-adds for
+// `accumulate`), so no tile waits for another's epilogue.  Per tile the
+// protocol is the 2-SM kernel's; tiles that a causal mode skips are skipped
+// by every role alike.
+// ---------------------------------------------------------------------------
+
+template <int BN, bool kStrict>
+struct PipeCfgP {
+  static constexpr int kA = BM * BK * 4;        // this CTA's 128 rows of A
+  static constexpr int kB = (BN / 2) * BK * 4;  // this CTA's half of B
+  static constexpr int kStageBytes = kStrict ? 2 * (kA + kB) : (kA + kB);
+  static constexpr int kEpiBytes = kAccWarps * 2 * 4096;  // two 32x32 boxes per accumulator warp
+  static constexpr int kStagesRaw = (160 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024 + 256;
+};
+
+// Tile t of the persistent schedule: batch item, this CTA's first row, the
+// tile's first column; false if the causal mode skips it.  kb range in
+// [*kb_begin, *kb_end).
+template <int BN>
+__device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_rows, int n_tiles, int rank,
+                                        int tri, int K, int* bz, int* m0, int* n0, int* kb_begin, int* kb_end) {
+  constexpr int kGroupP = kGroupM / 2;
+  *bz = t / tiles_per_batch;
+  const int pair = t - *bz * tiles_per_batch;
+  const int per_group = kGroupP * n_tiles;
+  const int first_p = (pair / per_group) * kGroupP;
+  const int gsize = min(pair_rows - first_p, kGroupP);
+  const int in_group = pair % per_group;
+  const int pr0 = (first_p + in_group % gsize) * 256;
+  *n0 = (in_group / gsize) * BN;
+  *m0 = pr0 + rank * BM;
+  *kb_begin = 0;
+  *kb_end = (K + BK - 1) / BK;
+  if (tri != 0 && causal_range(tri, pr0, 2 * BM, *n0, kb_begin, kb_end)) return false;
+  if (*kb_end < *kb_begin) *kb_end = *kb_begin;
+  return true;
+}
+
+template <int BN, bool kStrict, bool kAmn, bool kBmn>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
+    gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_alo,
+                        const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_blo,
+                        const __grid_constant__ CUtensorMap map_c32, GemmEpilogue ep, int M, int N, int K,
+                        int batch, int* err) {
+  using Cfg = PipeCfgP<BN, kStrict>;
+  constexpr int kA = Cfg::kA;
+  constexpr int kB = Cfg::kB;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kStageBytes = Cfg::kStageBytes;
+  constexpr uint32_t kTxBytes = 2 * kStageBytes;  // both CTAs' loads
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr int kHalf = BN / 2;  // columns per accumulator warp
+  constexpr int kBH = BN / 2;    // rows (K-major) or columns (MN-major) of B per CTA
+  constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kAmn ? 1u : 0u) << 15) |
+                              ((kBmn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(256 >> 4) << 24);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* epi = smem + kStages * kStageBytes;  // 1 KiB aligned: kStageBytes is a multiple of 1 KiB
+  uint64_t* bars = (uint64_t*)(epi + Cfg::kEpiBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* tfull_bar = bars + 2 * kStages;
+  uint64_t* tempty_bar = bars + 2 * kStages + 2;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kStages + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int rank = (int)cluster_ctarank();
+  const bool leader = rank == 0;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int pair_rows = (M + 255) / 256;
+  const int tiles_per_batch = n_tiles * pair_rows;
+  const int total = tiles_per_batch * batch;
+  const int cluster = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull_bar[b]), 1);
+      mbar_init(smem_u32(&tempty_bar[b]), 2 * kAccWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    // TMA producer (both CTAs), stage ring counter across tiles.
+    uint32_t it = 0;
+    for (int t = cluster; t < total && ok; t += clusters) {
+      int bz, m0, n0, kb0, kb1;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+        continue;
+      const int nb0 = n0 + rank * kBH;
+      for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
+        const int s = (int)(it % kStages);
+        if (it >= (uint32_t)kStages) ok = mbar_wait(smem_u32(&empty_bar[s]), ((it / kStages) - 1) & 1, err);
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&full_bar[s]);
+        if (leader) mbar_expect_tx(fb, kTxBytes);
+        const uint32_t base = smem_u32(smem + s * kStageBytes);
+        const int k0 = kb * BK;
+        const int nmaps = kStrict ? 2 : 1;
+        for (int h = 0; h < nmaps; ++h) {
+          const CUtensorMap* ma = h ? &map_alo : &map_a;
+          const CUtensorMap* mb = h ? &map_blo : &map_b;
+          const uint32_t ta = base + h * kA;
+          const uint32_t tb = base + nmaps * kA + h * kB;
+          if (kAmn) {
+#pragma unroll
+            for (int i = 0; i < BM / 32; ++i) tma_load_3d_pair(ta + i * 2048, ma, fb, m0 + 32 * i, k0, bz);
+          } else {
+            tma_load_3d_pair(ta, ma, fb, k0, m0, bz);
+          }
+          if (kBmn) {
+#pragma unroll
+            for (int i = 0; i < kBH / 32; ++i) tma_load_3d_pair(tb + i * 2048, mb, fb, nb0 + 32 * i, k0, bz);
+          } else {
+            tma_load_3d_pair(tb, mb, fb, k0, nb0, bz);
+          }
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // MMA issuer (even CTA): stage counter and chunk counter across tiles.
+    uint32_t it = 0, ch = 0;
+    for (int t = cluster; t < total && ok; t += clusters) {
+      int bz, m0, n0, kb0, kb1;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+        continue;
+      const int nkb = kb1 - kb0;
+      for (int j = 0; j < nkb && ok; ++j, ++it) {
+        const int s = (int)(it % kStages);
+        const uint32_t gch = ch + (uint32_t)(j / kChunkKb);
+        const int buf = (int)(gch & 1);
+        const bool first = (j % kChunkKb) == 0;
+        const bool last = (j % kChunkKb) == kChunkKb - 1 || j == nkb - 1;
+        if (first && gch >= 2) {
+          ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((gch >> 1) - 1) & 1, err);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        ok = mbar_wait(smem_u32(&full_bar[s]), (it / kStages) & 1, err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        const uint32_t base = smem_u32(smem + s * kStageBytes);
+        const int nmaps = kStrict ? 2 : 1;
+        const uint32_t ta = base, talo = base + kA;
+        const uint32_t tb = base + nmaps * kA, tblo = tb + kB;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t da = operand_desc(ta, kAmn, kk);
+          const uint64_t db = operand_desc(tb, kBmn, kk);
+          const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+          if (kStrict) {
+            umma_tf32_pair(d, operand_desc(talo, kAmn, kk), db, kIdesc, acc);
+            umma_tf32_pair(d, da, operand_desc(tblo, kBmn, kk), kIdesc, 1u);
+            umma_tf32_pair(d, da, db, kIdesc, 1u);
+          } else {
+            umma_tf32_pair(d, da, db, kIdesc, acc);
+          }
+        }
+        umma_commit_pair(smem_u32(&empty_bar[s]));
+        if (last) umma_commit_pair(smem_u32(&tfull_bar[buf]));
+      }
+      ch += (uint32_t)((nkb + kChunkKb - 1) / kChunkKb);
+    }
+  } else if (warp >= 2) {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t ebox0 = smem_u32(epi) + (uint32_t)(warp - 2) * 8192u;
+    uint32_t ch = 0;
+    bool have = true;
+    for (int t = cluster; t < total && have; t += clusters) {
+      int bz, m0, n0, kb0, kb1;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+        continue;
+      const int nch = (kb1 - kb0 + kChunkKb - 1) / kChunkKb;
+      float acc[kHalf];
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t gch = ch + (uint32_t)c;
+        const int buf = (int)(gch & 1);
+        have = mbar_wait(smem_u32(&tfull_bar[buf]), (gch >> 1) & 1, err);
+        if (!have) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
+#pragma unroll
+        for (int cc = 0; cc < kHalf; cc += 16) {
+          float r[16];
+          tmem_ld16(taddr + cc, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[cc + i] = acc[cc + i] + r[i];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[buf]), 0));
+      }
+      ch += (uint32_t)nch;
+      if (!have) break;
+      // Epilogue of this warp's 32 rows x kHalf columns.
+      const int col0 = n0 + half * kHalf;
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
+        float r = acc[i] * ep.alpha;
+        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
+        if (ep.relu) r = fmaxf(r, 0.0f);
+        acc[i] = r;
+      }
+#pragma unroll
+      for (int b = 0; b < kHalf / 32; ++b) {
+        const uint32_t box = ebox0 + (uint32_t)(b & 1) * 4096u;
+        // The box is reused two stores later: wait until at most one store
+        // is still reading this warp's boxes.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_shared_f4(box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4), acc[b * 32 + 4 * j],
+                       acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          if (col0 + 32 * b < N) tma_store_3d(&map_c32, box, col0 + 32 * b, m0 + quad * 32, bz, ep.accumulate);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  __syncwarp();
+
+  // Neither CTA may leave (releasing its shared memory and tensor memory)
+  // while the pair's MMAs can still read or write them.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // lo(x) = x - tf32_trunc(x), elementwise over a contiguous span.
 __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n >> 2;
@@ -922,6 +1193,50 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMa
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  TYSOR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (counts[dev] == 0) TYSOR_CUDA(cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev));
+  return counts[dev];
+}
+
+template <int BN, bool S, bool AMN, bool BMN>
+void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
+               const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
+               cudaStream_t st) {
+  constexpr int smem = PipeCfgP<BN, S>::kSmem;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN>;
+  static bool configured = false;
+  if (!configured) {
+    TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  const int64_t tiles = (int64_t)ceil_div(M, 256) * ceil_div(N, BN) * batch;
+  if (tiles > INT32_MAX) throw CudaError("matmul has too many tiles");
+  int64_t clusters = sm_count() / 2;
+  if (clusters > tiles) clusters = tiles;
+  if (clusters < 1) clusters = 1;
+  kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), kThreadsTC, smem, st>>>(ma, malo, mb, mblo, mc32, ep, M, N, K,
+                                                                          batch, d_err);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <int BN, bool S>
+void dispatch_pp(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
+                 const CUtensorMap& mblo, const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M,
+                 int N, int K, int* d_err, cudaStream_t st) {
+  if (amn) {
+    if (bmn) launch_pp<BN, S, true, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    else launch_pp<BN, S, true, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+  } else {
+    if (bmn) launch_pp<BN, S, false, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    else launch_pp<BN, S, false, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+  }
+}
+
 template <int BN, bool S>
 void dispatch_layout2(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo,
                       const CUtensorMap& mb, const CUtensorMap& mblo, const CUtensorMap& mc, int c_tma,
@@ -958,6 +1273,13 @@ void dispatch_layout(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMa
 // measured shape).  TYSOR_CUDA_GEMM_2SM=0 selects the 1-SM kernel.
 bool g_two_sm_enabled = [] {
   const char* v = getenv("TYSOR_CUDA_GEMM_2SM");
+  return !(v && v[0] == '0');
+}();
+
+// Cluster pairs run the persistent kernel (tiles of 256 x 256, or 256 x 128
+// when N <= 128) unless TYSOR_CUDA_GEMM_PERSISTENT=0.
+bool g_persistent_enabled = [] {
+  const char* v = getenv("TYSOR_CUDA_GEMM_PERSISTENT");
   return !(v && v[0] == '0');
 }();
 
@@ -1026,8 +1348,12 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     blo = scratch.b_lo;
   }
   const int BN = N <= 128 ? 128 : 256;
-  // The 2-SM form needs a full 256-row pair tile to be worth its cluster.
-  const bool two_sm = g_two_sm_enabled && BN == 256 && M >= 256;
+  // The pair forms need a full 256-row pair tile to be worth their cluster;
+  // the persistent one also needs C on 16-byte strides (its TMA stores).
+  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
+  const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
+  const bool persistent = g_two_sm_enabled && g_persistent_enabled && M >= 256 && c_tma;
+  const bool two_sm = persistent || (g_two_sm_enabled && BN == 256 && M >= 256);
   const bool amn = A.trans, bmn = !B.trans;
   // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
   const uint64_t a_in = amn ? M : K, a_out = amn ? K : M;
@@ -1044,9 +1370,18 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     malo = make_map(alo, a_in, a_out, batch, A.ld, A.batch_stride, a_box_in, a_box_out, a_sw);
     mblo = make_map(blo, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
   }
+  if (persistent) {
+    const CUtensorMap mc32 = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (BN == 128) {
+      if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+      else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    } else {
+      if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+      else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    }
+    return 1;
+  }
   // The tile-store epilogue needs C's rows and batches on 16-byte strides.
-  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
-  const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
   CUtensorMap mc = ma;
   if (c_tma) mc = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (two_sm) {
