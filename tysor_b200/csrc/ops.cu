@@ -449,11 +449,18 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
     m = block_max(m, red);
     // With `err`, later GEMMs skip the masked entries as exact zeros; flag the
     // (scores below about -9896) rows where exp(-1e4 - max) is not zero.
-    if (err != nullptr && threadIdx.x == 0 && qi < kWidth - 1 && expf(-1.0e4f - m) != 0.0f)
+    const bool masked_zero = expf(-1.0e4f - m) == 0.0f;  // the row's masked entries underflow to 0
+    if (err != nullptr && threadIdx.x == 0 && qi < kWidth - 1 && !masked_zero)
       atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
+      // Wholly masked groups are exact zeros when exp(-1e4 - max) underflows:
+      // their exp, sum terms (+0) and divisions are skipped.
+      if (masked_zero && 4 * (threadIdx.x + i * 256) > qi) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
       v[i].x = expf(v[i].x - m);
       v[i].y = expf(v[i].y - m);
       v[i].z = expf(v[i].z - m);
@@ -468,10 +475,12 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       float4 t = v[i];
-      t.x = t.x / d;
-      t.y = t.y / d;
-      t.z = t.z / d;
-      t.w = t.w / d;
+      if (!(masked_zero && 4 * (threadIdx.x + i * 256) > qi)) {
+        t.x = t.x / d;
+        t.y = t.y / d;
+        t.z = t.z / d;
+        t.w = t.w / d;
+      }
       yr[threadIdx.x + i * 256] = t;
     }
   }
@@ -662,6 +671,10 @@ __global__ void __launch_bounds__(512, 2) cross_entropy_kernel(const float* __re
     const float* tr = target + r * width;
     float m, d;
     row_stats(xr, width, vec, red, &m, &d);
+    // ln(max(p, 1e-6)) with ln p = (x - m) - ln d: one subtraction per
+    // element instead of exp, divide and log (ln is monotonic, so the clamp
+    // moves to the log side).
+    const float logd = logf(d), lclamp = logf(1e-6f);
     float acc = 0.0f;
     if (vec) {
       const int n4 = width >> 2;
@@ -675,22 +688,22 @@ __global__ void __launch_bounds__(512, 2) cross_entropy_kernel(const float* __re
         }
 #pragma unroll
         for (int u = 0; u < kCeUnroll; ++u) {
-          acc += t[u].x * logf(fmaxf(expf(x[u].x - m) / d, 1e-6f));
-          acc += t[u].y * logf(fmaxf(expf(x[u].y - m) / d, 1e-6f));
-          acc += t[u].z * logf(fmaxf(expf(x[u].z - m) / d, 1e-6f));
-          acc += t[u].w * logf(fmaxf(expf(x[u].w - m) / d, 1e-6f));
+          acc += t[u].x * fmaxf((x[u].x - m) - logd, lclamp);
+          acc += t[u].y * fmaxf((x[u].y - m) - logd, lclamp);
+          acc += t[u].z * fmaxf((x[u].z - m) - logd, lclamp);
+          acc += t[u].w * fmaxf((x[u].w - m) - logd, lclamp);
         }
       }
       for (; j < n4; j += blockDim.x) {
         const float4 x = ((const float4*)xr)[j], t = ((const float4*)tr)[j];
-        acc += t.x * logf(fmaxf(expf(x.x - m) / d, 1e-6f));
-        acc += t.y * logf(fmaxf(expf(x.y - m) / d, 1e-6f));
-        acc += t.z * logf(fmaxf(expf(x.z - m) / d, 1e-6f));
-        acc += t.w * logf(fmaxf(expf(x.w - m) / d, 1e-6f));
+        acc += t.x * fmaxf((x.x - m) - logd, lclamp);
+        acc += t.y * fmaxf((x.y - m) - logd, lclamp);
+        acc += t.z * fmaxf((x.z - m) - logd, lclamp);
+        acc += t.w * fmaxf((x.w - m) - logd, lclamp);
       }
     } else {
       for (int j = threadIdx.x; j < width; j += blockDim.x)
-        acc += tr[j] * logf(fmaxf(expf(xr[j] - m) / d, 1e-6f));
+        acc += tr[j] * fmaxf((xr[j] - m) - logd, lclamp);
     }
     acc = block_sum(acc, red);
     if (threadIdx.x == 0) loss[r] = 0.0f - acc;
@@ -701,9 +714,11 @@ __global__ void __launch_bounds__(512, 2) cross_entropy_kernel(const float* __re
 // target row or, with labels, the one-hot row of label `lab`.  The row was
 // just read by row_stats, so x comes from L2 here; kCeUnroll float4 per
 // thread are loaded ahead of their use.
-__device__ __forceinline__ float4 ce_grad4(float4 x, float4 t, float m, float d) {
-  return make_float4(expf(x.x - m) / d - t.x, expf(x.y - m) / d - t.y, expf(x.z - m) / d - t.z,
-                     expf(x.w - m) / d - t.w);
+// softmax - target with the row's 1/d precomputed (within one rounding of
+// exp(x - m) / d).
+__device__ __forceinline__ float4 ce_grad4(float4 x, float4 t, float m, float inv_d) {
+  return make_float4(expf(x.x - m) * inv_d - t.x, expf(x.y - m) * inv_d - t.y, expf(x.z - m) * inv_d - t.z,
+                     expf(x.w - m) * inv_d - t.w);
 }
 
 __device__ __forceinline__ float4 onehot4(int c, long long lab) {
@@ -714,6 +729,7 @@ __device__ __forceinline__ float4 onehot4(int c, long long lab) {
 __device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const float* __restrict__ tr,
                                             long long lab, float* __restrict__ gr, int width, bool vec,
                                             float m, float d, int accumulate) {
+  const float inv_d = 1.0f / d;
   if (vec) {
     const int n4 = width >> 2;
     const float4* x4 = (const float4*)xr;
@@ -731,13 +747,13 @@ __device__ __forceinline__ void ce_grad_row(const float* __restrict__ xr, const 
       }
 #pragma unroll
       for (int u = 0; u < kCeGradUnroll; ++u) {
-        float4 v = ce_grad4(x[u], t[u], m, d);
+        float4 v = ce_grad4(x[u], t[u], m, inv_d);
         if (accumulate) v = make_float4(o[u].x + v.x, o[u].y + v.y, o[u].z + v.z, o[u].w + v.w);
         g4[j + u * blockDim.x] = v;
       }
     }
     for (; j < n4; j += blockDim.x) {
-      float4 v = ce_grad4(x4[j], tr ? t4[j] : onehot4(4 * j, lab), m, d);
+      float4 v = ce_grad4(x4[j], tr ? t4[j] : onehot4(4 * j, lab), m, inv_d);
       if (accumulate) {
         const float4 o = g4[j];
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
