@@ -195,6 +195,7 @@ struct Executor {
     masked_input.clear();
     causal_scores.clear();
     causal_probs.clear();
+    folded_transpose.clear();
     grad_alias.clear();
     loss = grad_block = scratch = nullptr;
     scratch_floats = 0;
@@ -476,7 +477,7 @@ struct Executor {
   // shape_only: check and return the result's shape without planning work
   // (the value is produced later, folded into its consumer).
   HVal plan_matmul(const HVal& l, const HVal& r, StepList& out, bool shape_only = false,
-                   float alpha = 1.0f, int tri = 0) {
+                   float alpha = 1.0f, int tri = 0, int lid = -1, int rid = -1) {
     if (l.shape.size() < 2 || r.shape.size() < 2) fail("matmul currently requires rank-2 tensors");
     if (l.shape.size() != r.shape.size()) fail("matmul currently requires rank-2 tensors");
     for (size_t i = 0; i + 2 < l.shape.size(); ++i)
@@ -496,8 +497,23 @@ struct Executor {
       return o;
     }
     HVal o = new_tensor(os);
-    gemm_step(out, batch, m, n, k, l.slot, false, k, m * k, r.slot, false, n, k * n, o.slot, n, m * n,
-              nullptr, alpha, false, false, tri);
+    // A folded transpose operand is read from its source with trans set:
+    // lhs x^T with x stored [k, m], rhs y^T with y stored [n, k].
+    Slot *as = l.slot, *bs = r.slot;
+    bool ta = false, tb = false;
+    int64_t lda = k, ldb = n;
+    if (auto f = folded_transpose.find(lid); f != folded_transpose.end()) {
+      as = val(f->second).slot;
+      ta = true;
+      lda = m;
+    }
+    if (auto f = folded_transpose.find(rid); f != folded_transpose.end()) {
+      bs = val(f->second).slot;
+      tb = true;
+      ldb = k;
+    }
+    gemm_step(out, batch, m, n, k, as, ta, lda, m * k, bs, tb, ldb, k * n, o.slot, n, m * n, nullptr, alpha, false,
+              false, tri);
     return o;
   }
 
@@ -533,7 +549,7 @@ struct Executor {
       causal_scores.insert(m);
       tri = 1;
     }
-    return plan_matmul(val(ops.first), val(ops.second), forward, false, f, tri);
+    return plan_matmul(val(ops.first), val(ops.second), forward, false, f, tri, ops.first, ops.second);
   }
 
   // ---- forward planning --------------------------------------------------------
@@ -679,6 +695,9 @@ struct Executor {
   // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
   std::set<int> causal_scores;
   std::set<int> causal_probs;
+  // transpose(x, -2, -1) outputs read only by one matmul: the GEMM reads x
+  // with its trans flag flipped and the copy is never made (value -> x).
+  std::map<int, int> folded_transpose;
   std::map<int, std::pair<Slot*, float>> grad_alias;   // value -> (grad slot, factor)
 
   void build_uses() {
@@ -738,7 +757,8 @@ struct Executor {
       }
       // Probabilities of a fused causal softmax are exact zeros above the
       // diagonal: contract each row tile only over the keys it can see.
-      return plan_matmul(l, r, forward, false, 1.0f, causal_probs.count(node.inputs[0]) ? 2 : 0);
+      return plan_matmul(l, r, forward, false, 1.0f, causal_probs.count(node.inputs[0]) ? 2 : 0, node.inputs[0],
+                         node.inputs[1]);
     }
     if (node.op == "relu") {
       const HVal& x = tensor(node.inputs.at(0), "relu");
@@ -895,6 +915,17 @@ struct Executor {
       if (a > b) std::swap(a, b);
       std::vector<int64_t> s = x.shape;
       std::swap(s[a], s[b]);
+      // Folded into its only consumer, a matmul, when it swaps the last two
+      // axes (train and run modes; --backward reports every value's grad).
+      const GNode* c = sole_consumer(node.output);
+      if (mode != kModeBackward && rank >= 2 && a == rank - 2 && b == rank - 1 && c && c->kind == kNPrimitive &&
+          c->op == "matmul" && x.slot) {
+        folded_transpose[node.output] = node.inputs[0];
+        HVal o;
+        o.t = HVal::Tensor;
+        o.shape = s;
+        return o;
+      }
       HVal o = new_tensor(s);
       std::vector<int64_t> dims = x.shape;
       Slot *src = x.slot, *dst = o.slot;
@@ -1112,15 +1143,49 @@ struct Executor {
     const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
     std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
     const int batch = (int)numel(lead);
+    // Folded transpose operands: l = x^T (x stored [k, m]) or r = y^T (y
+    // stored [n, k]); their gradient goes straight to x or y, transposed by
+    // swapping the GEMM's operands (the transpose node has none to pass on).
+    const auto fl = folded_transpose.find(lid), fr = folded_transpose.find(rid);
+    const bool fold_l = fl != folded_transpose.end(), fold_r = fr != folded_transpose.end();
+    Slot* lp = fold_l ? val(fl->second).slot : l.slot;  // physical lhs
+    Slot* rp = fold_r ? val(fr->second).slot : r.slot;  // physical rhs
     if (want_l) {
-      auto [d, acc] = contrib(lid);
-      gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr,
-                alpha, acc, false, tri_l);
+      if (!fold_l) {
+        // d(l) [m, k] = g . r^T
+        auto [d, acc] = contrib(lid);
+        if (fold_r) gemm_step(backward, batch, m, k, n, g, false, n, m * n, rp, false, k, n * k, d, k, m * k, nullptr,
+                              alpha, acc, false, tri_l);
+        else gemm_step(backward, batch, m, k, n, g, false, n, m * n, rp, true, n, k * n, d, k, m * k, nullptr, alpha,
+                       acc, false, tri_l);
+      } else {
+        // d(x) [k, m] = (g . r^T)^T = r . g^T
+        auto [d, acc] = contrib(fl->second);
+        if (fold_r) gemm_step(backward, batch, k, m, n, rp, true, k, n * k, g, true, n, m * n, d, m, k * m, nullptr,
+                              alpha, acc, false, 0);
+        else gemm_step(backward, batch, k, m, n, rp, false, n, k * n, g, true, n, m * n, d, m, k * m, nullptr, alpha,
+                       acc, false, 0);
+      }
     }
     if (want_r) {
-      auto [d, acc] = contrib(rid);
-      gemm_step(backward, batch, k, n, m, l.slot, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr,
-                alpha, acc, false, tri_r);
+      if (!fold_r) {
+        // d(r) [k, n] = l^T . g
+        auto [d, acc] = contrib(rid);
+        if (fold_l) gemm_step(backward, batch, k, n, m, lp, false, m, k * m, g, false, n, m * n, d, n, k * n, nullptr,
+                              alpha, acc, false, tri_r);
+        else gemm_step(backward, batch, k, n, m, lp, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr, alpha,
+                       acc, false, tri_r);
+      } else {
+        // d(y) [n, k] = (l^T . g)^T = g^T . l.  A causal contraction that
+        // started at the output's first column (keys) now starts at its first
+        // row.
+        auto [d, acc] = contrib(fr->second);
+        const int tri = tri_r == 4 ? 3 : 0;
+        if (fold_l) gemm_step(backward, batch, n, k, m, g, true, n, m * n, lp, true, m, k * m, d, k, n * k, nullptr,
+                              alpha, acc, false, tri);
+        else gemm_step(backward, batch, n, k, m, g, true, n, m * n, lp, false, k, m * k, d, k, n * k, nullptr, alpha,
+                       acc, false, tri);
+      }
     }
   }
 
@@ -1547,6 +1612,8 @@ bool guarded_g(F&& f) {
 Slot* value_slot(Executor* e, int id, std::vector<int64_t>* shape) {
   if (id < 0 || id >= (int)e->hv.size()) throw CudaError("value id out of range");
   const HVal& h = e->hv[id];
+  if (h.t == HVal::Tensor && !h.slot && (e->folded_transpose.count(id) || e->masked_input.count(id)))
+    throw CudaError("value " + std::to_string(id) + " is not materialised: it was fused into its consumer");
   if (h.t != HVal::Tensor || !h.slot) throw CudaError("value " + std::to_string(id) + " is not a tensor");
   if (shape) *shape = h.shape;
   return h.slot;
