@@ -1072,8 +1072,21 @@ struct Executor {
             const int64_t outer = n / (q * w);
             causal_probs.insert(node.output);
             // The guard is armed when a matmul will skip the masked entries.
-            int* err = is_matmul_lhs(node.output) ? ctx->d_err : nullptr;
-            forward.push_back([=](cudaStream_t st) { launch_masked_softmax(src->p, c->p, outer, q, w, err, st); });
+            const bool lhs = is_matmul_lhs(node.output);
+            int* err = lhs ? ctx->d_err : nullptr;
+            // A strict GEMM reading the probabilities as its left operand gets
+            // their low part from this kernel (registered where the GEMM's
+            // operand preparation looks it up) instead of a split pass.  The
+            // probabilities are a fresh, zero-filled buffer written only here,
+            // so the wholly masked (exact zero) groups are not stored.
+            Slot* lo = nullptr;
+            if (lhs && plan_matmul_mode == kGemmStrict && w % 4 == 0) {
+              lo = alloc((size_t)n);
+              prep_cache[std::make_tuple(c, false, q, w, w, q * w, outer)] = {c, lo};
+            }
+            forward.push_back([=](cudaStream_t st) {
+              launch_masked_softmax(src->p, c->p, outer, q, w, err, lo ? lo->p : nullptr, 1, st);
+            });
           } else {
             forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
           }
@@ -1462,8 +1475,17 @@ struct Executor {
           Slot* ys = out.slot;
           const int64_t q = out.shape[out.shape.size() - 2], k = out.shape.back();
           const int64_t outer = n / (q * k);
+          // As in the forward: when the scores come from a (folded-scale)
+          // matmul, its strict backward GEMMs read this gradient's low part
+          // from here; a fresh zero-filled gradient skips its masked zeros.
+          Slot* lo = nullptr;
+          if (!acc && folded_scale.count(mi->second) && plan_matmul_mode == kGemmStrict && k % 4 == 0) {
+            lo = alloc((size_t)n);
+            prep_cache[std::make_tuple(d, false, q, k, k, q * k, outer)] = {d, lo};
+          }
+          const int skip = acc ? 0 : 1;
           backward.push_back([=](cudaStream_t st) {
-            launch_masked_softmax_backward(ys->p, g->p, d->p, outer, q, k, acc, st);
+            launch_masked_softmax_backward(ys->p, g->p, d->p, outer, q, k, acc, lo ? lo->p : nullptr, skip, st);
           });
           return;
         }

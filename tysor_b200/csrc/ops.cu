@@ -15,6 +15,12 @@ constexpr int kThreads = 256;
 
 __device__ __forceinline__ bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 
+// x - tf32(x): the low part a strict 3xTF32 GEMM multiplies separately.
+__device__ __forceinline__ float lo_part(float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ float4 lo_part4(float4 v) {
+  return make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+}
+
 // f32 -> i64 with Rust `as` semantics (truncation, saturation, NaN -> 0).
 __device__ __forceinline__ long long rust_f32_to_i64(float v) {
   if (isnan(v)) return 0;
@@ -425,7 +431,8 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
 template <int VPT>
 __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restrict__ x,
                                                           float* __restrict__ out, int64_t rows,
-                                                          int q, int masked, int* err) {
+                                                          int q, int masked, int* err,
+                                                          float* __restrict__ lo, int skip_zero) {
   __shared__ float red[33];
   constexpr int kWidth = 1024 * VPT;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -472,16 +479,24 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
     }
     const float d = fmaxf(block_sum(s, red), 1.1920928955078125e-7f);
     float4* yr = (float4*)(out + r * kWidth);
+    float4* lr = lo ? (float4*)(lo + r * kWidth) : nullptr;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       float4 t = v[i];
-      if (!(masked_zero && 4 * (threadIdx.x + i * 256) > qi)) {
-        t.x = t.x / d;
-        t.y = t.y / d;
-        t.z = t.z / d;
-        t.w = t.w / d;
+      if (masked_zero && 4 * (threadIdx.x + i * 256) > qi) {
+        // Exact zeros: not stored at all into buffers that hold zeros there.
+        if (!skip_zero) {
+          yr[threadIdx.x + i * 256] = t;
+          if (lr) lr[threadIdx.x + i * 256] = t;
+        }
+        continue;
       }
+      t.x = t.x / d;
+      t.y = t.y / d;
+      t.z = t.z / d;
+      t.w = t.w / d;
       yr[threadIdx.x + i * 256] = t;
+      if (lr) lr[threadIdx.x + i * 256] = lo_part4(t);
     }
   }
 }
@@ -489,7 +504,7 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
 // Row r of [outer*q] rows of width k; row index within its q x k block is
 // r % q.  Values with col > row read as -1e4.
 __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                      int64_t rows, int q, int width, int* err) {
+                                      int64_t rows, int q, int width, int* err, float* __restrict__ lo) {
   __shared__ float red[33];
   const bool vec = (width & 3) == 0 && aligned16(x) && aligned16(out);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -536,17 +551,22 @@ __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __rest
         o.z = expf((c + 2 > qi ? -1.0e4f : v.z) - m) / d;
         o.w = expf((c + 3 > qi ? -1.0e4f : v.w) - m) / d;
         ((float4*)yr)[j] = o;
+        if (lo) ((float4*)(lo + r * width))[j] = lo_part4(o);
       }
     } else {
-      for (int j = threadIdx.x; j < width; j += blockDim.x) yr[j] = expf((j > qi ? -1.0e4f : xr[j]) - m) / d;
+      for (int j = threadIdx.x; j < width; j += blockDim.x) {
+        const float p = expf((j > qi ? -1.0e4f : xr[j]) - m) / d;
+        yr[j] = p;
+        if (lo) lo[r * width + j] = lo_part(p);
+      }
     }
   }
 }
 
 __global__ void masked_softmax_backward_kernel(const float* __restrict__ y, const float* __restrict__ g,
                                                float* __restrict__ dx, int64_t n, int64_t q, int64_t k,
-                                               int accumulate) {
-  const bool vec = (k & 3) == 0 && aligned16(y) && aligned16(g) && aligned16(dx);
+                                               int accumulate, float* __restrict__ lo, int skip_zero) {
+  const bool vec = (k & 3) == 0 && aligned16(y) && aligned16(g) && aligned16(dx) && (lo == nullptr || aligned16(lo));
   if (vec) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n >> 2);
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -559,19 +579,24 @@ __global__ void masked_softmax_backward_kernel(const float* __restrict__ y, cons
         v.y = col + 1 > row ? 0.0f : (yv.y * (1.0f - yv.y)) * gv.y;
         v.z = col + 2 > row ? 0.0f : (yv.z * (1.0f - yv.z)) * gv.z;
         v.w = col + 3 > row ? 0.0f : (yv.w * (1.0f - yv.w)) * gv.w;
+      } else if (skip_zero || (accumulate && lo == nullptr)) {
+        continue;  // the buffers already hold zero there, or this adds zero
       }
       if (accumulate) {
         const float4 o = ((float4*)dx)[i];
         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
       }
       ((float4*)dx)[i] = v;
+      if (lo) ((float4*)lo)[i] = lo_part4(v);
     }
   } else {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t col = i % k, row = (i / k) % q;
       const float v = col > row ? 0.0f : (y[i] * (1.0f - y[i])) * g[i];
-      dx[i] = accumulate ? dx[i] + v : v;
+      const float r = accumulate ? dx[i] + v : v;
+      dx[i] = r;
+      if (lo) lo[i] = lo_part(r);
     }
   }
 }
@@ -1258,24 +1283,24 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
 
 // Launches the register-resident form when the width allows; false if not.
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 int* err, cudaStream_t st);
+                 int* err, float* lo, int skip_zero, cudaStream_t st);
 
 void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st) {
   if (rows <= 0) return;
-  if (softmax_reg(x, out, rows, width, 1, 0, nullptr, st)) return;
+  if (softmax_reg(x, out, rows, width, 1, 0, nullptr, nullptr, 0, st)) return;
   softmax_kernel<<<row_blocks(rows), row_threads(width), 0, st>>>(x, out, rows, (int)width);
   check_launch();
 }
 
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 int* err, cudaStream_t st) {
-  if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out)) return false;
+                 int* err, float* lo, int skip_zero, cudaStream_t st) {
+  if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out) || (lo && !aligned16_host(lo))) return false;
   const int blocks = row_blocks(rows);
   switch (width / 1024) {
-    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
-    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
-    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
-    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err); break;
+    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
+    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
+    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
+    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
     default: return false;
   }
   check_launch();
@@ -1283,20 +1308,21 @@ bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_
 }
 
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           int* err, cudaStream_t st) {
+                           int* err, float* lo, int skip_zero, cudaStream_t st) {
   const int64_t rows = outer * q;
   if (rows <= 0) return;
-  if (softmax_reg(x, out, rows, k, q, 1, err, st)) return;
-  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k, err);
+  if (softmax_reg(x, out, rows, k, q, 1, err, lo, skip_zero, st)) return;
+  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k, err, lo);
   check_launch();
 }
 
 void launch_masked_softmax_backward(const float* y, const float* g, float* dx, int64_t outer,
-                                    int64_t q, int64_t k, int accumulate, cudaStream_t st) {
+                                    int64_t q, int64_t k, int accumulate, float* lo, int skip_zero,
+                                    cudaStream_t st) {
   const int64_t n = outer * q * k;
   if (n <= 0) return;
   masked_softmax_backward_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
-      y, g, dx, n, q, k, accumulate);
+      y, g, dx, n, q, k, accumulate, lo, skip_zero);
   check_launch();
 }
 

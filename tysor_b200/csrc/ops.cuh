@@ -67,13 +67,18 @@ void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cud
 // With `err`, a row whose masked entries would get a nonzero probability
 // (possible only when its scores are all below about -9896) records
 // kErrCausalSkip: GEMMs that treat those entries as zeros would be wrong.
+// With `lo`, also writes each probability's low part x - tf32(x) (the
+// operand split a strict GEMM consuming them needs).  With `skip_zero`,
+// wholly masked groups (exact zeros) are not stored: for buffers known to
+// hold zeros there already.
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           int* err, cudaStream_t st);
+                           int* err, float* lo, int skip_zero, cudaStream_t st);
 // Backward of Softmax(causal_mask(x)) with the reference rules: the
 // diagonal softmax term y(1-y)g (layers.rs:350-364), then the mask zeroes
 // col > row (layers.rs:418-436): dx (+)= col > row ? 0 : y(1-y)g.
 void launch_masked_softmax_backward(const float* y, const float* g, float* dx, int64_t outer,
-                                    int64_t q, int64_t k, int accumulate, cudaStream_t st);
+                                    int64_t q, int64_t k, int accumulate, float* lo, int skip_zero,
+                                    cudaStream_t st);
 void launch_cross_entropy(const float* logits, const float* target, float* loss, int64_t rows,
                           int64_t width, cudaStream_t st);
 void launch_cross_entropy_backward(const float* logits, const float* target, float* grad,
