@@ -93,7 +93,16 @@ struct GemmScratch {
   int64_t a_elems;
   int64_t b_elems;
   int presplit = 0;
+  // Optional workspace for split-K partial sums (16-byte aligned): a GEMM
+  // whose output tiles cannot fill the GPU may split its K range into up to
+  // 4 parts, written here and summed in a fixed order (deterministic).
+  float* ws = nullptr;
+  int64_t ws_elems = 0;
 };
+
+// Workspace elements a split-K launch of this GEMM would need (0: it would
+// not split).
+int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c);
 
 // Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
 extern bool g_two_sm_enabled;

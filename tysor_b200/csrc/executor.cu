@@ -457,6 +457,11 @@ struct Executor {
     }
     Context* cx = ctx;
     const int mode_now = plan_matmul_mode;
+    // Split-K workspace (the shared scratch slot) for GEMMs whose output
+    // tiles cannot fill the GPU.
+    const int64_t ws_elems = tc && tri == 0 ? gemm_splitk_ws_elems(batch, M, N, K, mode_now, ldc, sc) : 0;
+    if (ws_elems > 0) need_scratch((size_t)ws_elems);
+    Slot** scr = &scratch;
     out.push_back([=](cudaStream_t st) {
       GemmOperand A{pa.hi->p, pa.trans, pa.ld, pa.bs};
       GemmOperand B{pb.hi->p, pb.trans, pb.ld, pb.bs};
@@ -468,6 +473,10 @@ struct Executor {
         s.b_lo = pb.lo->p;
         s.a_elems = (int64_t)pa.lo->n;
         s.b_elems = (int64_t)pb.lo->n;
+      }
+      if (ws_elems > 0) {
+        s.ws = (*scr)->p;
+        s.ws_elems = ws_elems;
       }
       gemm_launch(batch, M, N, K, A, B, O, ep, mode_now, s, cx->d_err, st);
     });

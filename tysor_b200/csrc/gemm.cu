@@ -782,8 +782,17 @@ struct PipeCfgP {
 // [*kb_begin, *kb_end).
 template <int BN>
 __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_rows, int n_tiles, int rank,
-                                        int tri, int K, int* bz, int* m0, int* n0, int* kb_begin, int* kb_end) {
+                                        int tri, int K, int* bz, int* m0, int* n0, int* kb_begin, int* kb_end,
+                                        int splits = 1, int total_tiles = 0, int* ks = nullptr) {
   constexpr int kGroupP = kGroupM / 2;
+  // Split-K: tile t covers part t / total_tiles of the K range of output
+  // tile t % total_tiles.
+  int part = 0;
+  if (splits > 1) {
+    part = t / total_tiles;
+    t -= part * total_tiles;
+  }
+  if (ks) *ks = part;
   *bz = t / tiles_per_batch;
   const int pair = t - *bz * tiles_per_batch;
   const int per_group = kGroupP * n_tiles;
@@ -797,6 +806,13 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   *kb_end = (K + BK - 1) / BK;
   if (tri != 0 && causal_range(tri, pr0, 2 * BM, *n0, kb_begin, kb_end)) return false;
   if (*kb_end < *kb_begin) *kb_end = *kb_begin;
+  if (splits > 1) {
+    const int per = (*kb_end - *kb_begin + splits - 1) / splits;
+    const int b = *kb_begin + part * per;
+    const int e = min(*kb_end, b + per);
+    *kb_begin = b;
+    *kb_end = e > b ? e : b;
+  }
   return true;
 }
 
@@ -807,7 +823,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
                         const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_blo,
                         const __grid_constant__ CUtensorMap map_c32, GemmEpilogue ep, int M, int N, int K,
-                        int batch, int* err) {
+                        int batch, int splits, int* err) {
+  // splits > 1: map_c32 addresses the split-K workspace ([splits * batch][M]
+  // [N] raw sums); alpha, bias, relu and accumulate are left to the
+  // reduction that sums the parts.
   using Cfg = PipeCfgP<BN, kStrict>;
   constexpr int kA = Cfg::kA;
   constexpr int kB = Cfg::kB;
@@ -839,7 +858,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   const int n_tiles = (N + BN - 1) / BN;
   const int pair_rows = (M + 255) / 256;
   const int tiles_per_batch = n_tiles * pair_rows;
-  const int total = tiles_per_batch * batch;
+  const int out_tiles = tiles_per_batch * batch;
+  const int total = out_tiles * splits;
   const int cluster = blockIdx.x >> 1;
   const int clusters = gridDim.x >> 1;
 
@@ -870,8 +890,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     // TMA producer (both CTAs), stage ring counter across tiles.
     uint32_t it = 0;
     for (int t = cluster; t < total && ok; t += clusters) {
-      int bz, m0, n0, kb0, kb1;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+      int bz, m0, n0, kb0, kb1, ks;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
         continue;
       const int nb0 = n0 + rank * kBH;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
@@ -907,8 +927,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     // MMA issuer (even CTA): stage counter and chunk counter across tiles.
     uint32_t it = 0, ch = 0;
     for (int t = cluster; t < total && ok; t += clusters) {
-      int bz, m0, n0, kb0, kb1;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+      int bz, m0, n0, kb0, kb1, ks;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
         continue;
       const int nkb = kb1 - kb0;
       for (int j = 0; j < nkb && ok; ++j, ++it) {
@@ -955,8 +975,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     uint32_t ch = 0;
     bool have = true;
     for (int t = cluster; t < total && have; t += clusters) {
-      int bz, m0, n0, kb0, kb1;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1))
+      int bz, m0, n0, kb0, kb1, ks;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
         continue;
       const int nch = (kb1 - kb0 + kChunkKb - 1) / kChunkKb;
       float acc[kHalf];
@@ -984,13 +1004,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
       if (!have) break;
       // Epilogue of this warp's 32 rows x kHalf columns.
       const int col0 = n0 + half * kHalf;
+      if (splits == 1) {
 #pragma unroll
-      for (int i = 0; i < kHalf; ++i) {
-        float r = acc[i] * ep.alpha;
-        if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
-        if (ep.relu) r = fmaxf(r, 0.0f);
-        acc[i] = r;
+        for (int i = 0; i < kHalf; ++i) {
+          float r = acc[i] * ep.alpha;
+          if (ep.bias != nullptr && col0 + i < N) r = r + ep.bias[col0 + i];
+          if (ep.relu) r = fmaxf(r, 0.0f);
+          acc[i] = r;
+        }
       }
+      const int zc = splits == 1 ? bz : ks * batch + bz;  // output (or workspace) batch index
+      const int red = splits == 1 ? ep.accumulate : 0;
 #pragma unroll
       for (int b = 0; b < kHalf / 32; ++b) {
         const uint32_t box = ebox0 + (uint32_t)(b & 1) * 4096u;
@@ -1005,7 +1029,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          if (col0 + 32 * b < N) tma_store_3d(&map_c32, box, col0 + 32 * b, m0 + quad * 32, bz, ep.accumulate);
+          if (col0 + 32 * b < N) tma_store_3d(&map_c32, box, col0 + 32 * b, m0 + quad * 32, zc, red);
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
       }
@@ -1020,6 +1044,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   cluster_sync();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// Split-K reduction: C (+)= epilogue(sum over parts of ws[part]), parts
+// added in order 0, 1, ... (deterministic).  ws is [splits * batch][M][ldw].
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int batch, int M, int N,
+                                     int64_t ldw, GemmOutput out, GemmEpilogue ep) {
+  const int64_t per_batch = (int64_t)M * N;
+  const int64_t total = per_batch * batch;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(e / per_batch);
+    const int64_t rem = e - (int64_t)b * per_batch;
+    const int row = (int)(rem / N), col = (int)(rem % N);
+    float v = 0.0f;
+    for (int p = 0; p < splits; ++p) v = v + ws[((int64_t)(p * batch + b) * M + row) * ldw + col];
+    float r = v * ep.alpha;
+    if (ep.bias != nullptr) r = r + ep.bias[col];
+    if (ep.relu) r = fmaxf(r, 0.0f);
+    float* dst = out.ptr + (int64_t)b * out.batch_stride + (int64_t)row * out.ld + col;
+    *dst = ep.accumulate ? *dst + r : r;
   }
 }
 
@@ -1204,8 +1249,8 @@ int sm_count() {
 
 template <int BN, bool S, bool AMN, bool BMN>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
-               const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int* d_err,
-               cudaStream_t st) {
+               const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int splits,
+               int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfgP<BN, S>::kSmem;
   auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN>;
   static bool configured = false;
@@ -1213,13 +1258,13 @@ void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const int64_t tiles = (int64_t)ceil_div(M, 256) * ceil_div(N, BN) * batch;
+  const int64_t tiles = (int64_t)ceil_div(M, 256) * ceil_div(N, BN) * batch * splits;
   if (tiles > INT32_MAX) throw CudaError("matmul has too many tiles");
   int64_t clusters = sm_count() / 2;
   if (clusters > tiles) clusters = tiles;
   if (clusters < 1) clusters = 1;
   kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), kThreadsTC, smem, st>>>(ma, malo, mb, mblo, mc32, ep, M, N, K,
-                                                                          batch, d_err);
+                                                                          batch, splits, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
@@ -1227,14 +1272,36 @@ void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
 template <int BN, bool S>
 void dispatch_pp(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
                  const CUtensorMap& mblo, const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M,
-                 int N, int K, int* d_err, cudaStream_t st) {
+                 int N, int K, int splits, int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_pp<BN, S, true, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
-    else launch_pp<BN, S, true, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_pp<BN, S, true, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, true, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   } else {
-    if (bmn) launch_pp<BN, S, false, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
-    else launch_pp<BN, S, false, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+    if (bmn) launch_pp<BN, S, false, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, false, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   }
+}
+
+// Split-K for the persistent kernel: when the output tiles leave the
+// resident clusters idle (a weight gradient with few output tiles and a
+// long K), K is cut into up to 4 parts of at least 1024 elements, choosing
+// the fewest parts that minimise whole rounds of tiles per cluster.
+int splitk_parts(int batch, int64_t M, int64_t N, int64_t K) {
+  const int64_t BN = N <= 128 ? 128 : 256;
+  const int64_t tiles = ceil_div(M, 256) * ceil_div(N, BN) * batch;
+  const int64_t clusters = sm_count() / 2;
+  if (clusters < 1) return 1;
+  int best = 1;
+  double best_cost = (double)ceil_div(tiles, clusters);
+  for (int parts = 2; parts <= 4; ++parts) {
+    if (K / parts < 1024) break;
+    const double cost = (double)ceil_div(tiles * parts, clusters) / parts;
+    if (cost < 0.9 * best_cost) {
+      best = parts;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 template <int BN, bool S>
@@ -1282,6 +1349,15 @@ bool g_persistent_enabled = [] {
   const char* v = getenv("TYSOR_CUDA_GEMM_PERSISTENT");
   return !(v && v[0] == '0');
 }();
+
+int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c) {
+  if (mode == kGemmExact || !g_two_sm_enabled || !g_persistent_enabled || M < 256 || (ldc & 3) != 0 ||
+      (batch > 1 && (stride_c & 3) != 0) || M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
+    return 0;
+  const int parts = splitk_parts(batch, M, N, K);
+  if (parts <= 1) return 0;
+  return (int64_t)parts * batch * M * ((N + 3) & ~(int64_t)3);
+}
 
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st) {
   if (n <= 0) return;
@@ -1371,13 +1447,29 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     mblo = make_map(blo, b_in, b_out, batch, B.ld, B.batch_stride, b_box_in, b_box_out, b_sw);
   }
   if (persistent) {
-    const CUtensorMap mc32 = make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    // Split-K into the caller's workspace when it has one and it pays.
+    int splits = 1;
+    const int64_t ldw = (N + 3) & ~(int64_t)3;
+    if (ep.tri == 0 && scratch.ws != nullptr && (((uintptr_t)scratch.ws) & 15) == 0) {
+      splits = splitk_parts(batch, M, N, K);
+      if ((int64_t)splits * batch * M * ldw > scratch.ws_elems) splits = 1;
+    }
+    const CUtensorMap mc32 =
+        splits > 1 ? make_map(scratch.ws, N, M, (uint64_t)splits * batch, ldw, M * ldw, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)
+                   : make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    const int im = (int)M, in = (int)N, ik = (int)K;
     if (BN == 128) {
-      if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
-      else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+      if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
     } else {
-      if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
-      else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, M, N, K, d_err, st);
+      if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+    }
+    if (splits > 1) {
+      splitk_reduce_kernel<<<elementwise_blocks((int64_t)batch * M * N, 256), 256, 0, st>>>(scratch.ws, splits, batch, im,
+                                                                                            in, ldw, C, ep);
+      TYSOR_CUDA(cudaGetLastError());
+      g_launches.fetch_add(1, std::memory_order_relaxed);
     }
     return 1;
   }
