@@ -68,13 +68,14 @@ def test_block_forward_backward_and_sgd(cuda_ctx):
     ex.close()
 
 
-@pytest.mark.parametrize("shape", [[2, 3, 64, 32], [1, 2, 1024, 32]])
+@pytest.mark.parametrize("shape", [[2, 3, 64, 32], [1, 2, 1024, 32], [1, 2, 2048, 32]])
 def test_attention_core_with_fused_scale_and_masked_softmax(cuda_ctx, shape):
     """softmax(causal_mask(scale(q . k^T, c))) . v, training semantics: the
     executor folds the scale into the GEMM's alpha and runs mask+softmax as
     one kernel (forward and backward); values and the gradients reaching q,
     k and v must match the op-by-op oracle.  Row widths that are multiples
-    of 1024 take the register-resident softmax."""
+    of 1024 take the register-resident softmax (one or two warps per row
+    at widths 1024 and 2048)."""
     from tysor_b200.graph import GraphBuilder
     from tysor_b200.runtime import CudaGraphExecutor
     b = GraphBuilder()

@@ -195,7 +195,7 @@ def test_activation_backwards(dev):
     np.testing.assert_array_equal(D.read(), L.softmax_backward(T([x.size], sm), T([g.size], g)).data)
 
 
-@pytest.mark.parametrize("rows,width", [(5, 3), (33, 257), (300, 2048), (65536, 4096)])
+@pytest.mark.parametrize("rows,width", [(5, 3), (33, 257), (300, 1024), (300, 2048), (65536, 4096)])
 def test_rms_norm_softmax_silu_sweep(dev, rows, width):
     """rms_norm (reference semantics and the gain/eps extension), softmax and
     SiLU at x ~ N(0,1); the largest case is the [65536, 4096] sweep shape."""

@@ -532,8 +532,21 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
   return r;
 }
 
+// Arrival on a barrier of this CTA or of the peer (an address from
+// map_to_rank), with the default release semantics at CTA scope.  A release
+// at cluster scope measured over 1,000 cycles per arrival here, enough to
+// bound a pipeline that arrives once per stage.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // Loads into this CTA's shared memory; the transaction bytes complete on the
@@ -764,7 +777,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
 // `accumulate`), so no tile waits for another's epilogue.  Per tile the
 // protocol is the 2-SM kernel's; tiles that a causal mode skips are skipped
 // by every role alike.
+//
+// kConvA (strict mode): the low part of A is made in shared memory instead
+// of being loaded.  Each CTA's A tile lands on a barrier of its own
+// ("A full"); two converter warps per CTA write lo = a - tf32_trunc(a) beside
+// it, in the same swizzled positions, and arrive on the even CTA's
+// "converted" barrier, which the MMA issuer waits for besides "full".  For
+// the GEMMs that stream a large A past a narrow B (attention probabilities
+// times values, N <= 128) this halves the bytes read from HBM: the kernel
+// is bound by the A stream, not by the tensor core.
 // ---------------------------------------------------------------------------
+
+template <bool kConvA>
+constexpr int pp_threads() {
+  return kThreadsTC + (kConvA ? 64 : 0);
+}
 
 template <int BN, bool kStrict>
 struct PipeCfgP {
@@ -816,8 +843,8 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   return true;
 }
 
-template <int BN, bool kStrict, bool kAmn, bool kBmn>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
+template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>(), 1)
     gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_alo,
                         const __grid_constant__ CUtensorMap map_b,
@@ -832,7 +859,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   constexpr int kB = Cfg::kB;
   constexpr int kStages = Cfg::kStages;
   constexpr int kStageBytes = Cfg::kStageBytes;
-  constexpr uint32_t kTxBytes = 2 * kStageBytes;  // both CTAs' loads
+  static_assert(!kConvA || kStrict, "A's low part is only used in strict mode");
+  static_assert(!kConvA || (4 * kStages + 4) * 8 + 4 <= 256, "barriers exceed their reserve");
+  static_assert(kA % (16 * 64) == 0, "converter warps cover the A tile in float4 rounds");
+  // Both CTAs' loads on the even CTA's "full" barrier (with kConvA: B only).
+  constexpr uint32_t kTxBytes = kConvA ? 2 * (kStageBytes - 2 * kA) : 2 * kStageBytes;
   constexpr uint32_t kTmemCols = 2 * BN;
   constexpr int kHalf = BN / 2;  // columns per accumulator warp
   constexpr int kBH = BN / 2;    // rows (K-major) or columns (MN-major) of B per CTA
@@ -848,7 +879,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   uint64_t* empty_bar = bars + kStages;
   uint64_t* tfull_bar = bars + 2 * kStages;
   uint64_t* tempty_bar = bars + 2 * kStages + 2;
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kStages + 4);
+  uint64_t* afull_bar = bars + 2 * kStages + 4;  // kConvA: this CTA's A tile landed
+  uint64_t* conv_bar = bars + 3 * kStages + 4;   // kConvA: both CTAs' low parts written
+  uint32_t* tmem_slot = (uint32_t*)(bars + (kConvA ? 4 * kStages + 4 : 2 * kStages + 4));
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -871,6 +904,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull_bar[b]), 1);
       mbar_init(smem_u32(&tempty_bar[b]), 2 * kAccWarps);
+    }
+    if (kConvA) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(smem_u32(&afull_bar[s]), 1);
+        mbar_init(smem_u32(&conv_bar[s]), 4);  // two converter warps in each CTA
+      }
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -900,6 +939,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
         if (!ok) break;
         const uint32_t fb = smem_u32(&full_bar[s]);
         if (leader) mbar_expect_tx(fb, kTxBytes);
+        const uint32_t afb = smem_u32(&afull_bar[s]);
+        if (kConvA) mbar_expect_tx(afb, kA);
         const uint32_t base = smem_u32(smem + s * kStageBytes);
         const int k0 = kb * BK;
         const int nmaps = kStrict ? 2 : 1;
@@ -908,7 +949,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
           const CUtensorMap* mb = h ? &map_blo : &map_b;
           const uint32_t ta = base + h * kA;
           const uint32_t tb = base + nmaps * kA + h * kB;
-          if (kAmn) {
+          if (kConvA) {
+            // The high part only, completing on this CTA's own barrier.
+            if (h == 0) {
+              if (kAmn) {
+#pragma unroll
+                for (int i = 0; i < BM / 32; ++i) tma_load_3d(ta + i * 2048, ma, afb, m0 + 32 * i, k0, bz);
+              } else {
+                tma_load_3d(ta, ma, afb, k0, m0, bz);
+              }
+            }
+          } else if (kAmn) {
 #pragma unroll
             for (int i = 0; i < BM / 32; ++i) tma_load_3d_pair(ta + i * 2048, ma, fb, m0 + 32 * i, k0, bz);
           } else {
@@ -943,6 +994,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
           tc_fence_after();
         }
         ok = mbar_wait(smem_u32(&full_bar[s]), (it / kStages) & 1, err);
+        if (ok && kConvA) ok = mbar_wait(smem_u32(&conv_bar[s]), (it / kStages) & 1, err);
         if (!ok) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * BN);
@@ -968,7 +1020,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
       }
       ch += (uint32_t)((nkb + kChunkKb - 1) / kChunkKb);
     }
-  } else if (warp >= 2) {
+  } else if (kConvA && warp >= 2 + kAccWarps) {
+    // Converter warps (both CTAs): the low part of each landed A tile,
+    // elementwise, so it keeps the tile's swizzled layout at offset kA.
+    const int ct = tid - 32 * (2 + kAccWarps);  // 0 .. 63
+    uint32_t it = 0;
+    for (int t = cluster; t < total && ok; t += clusters) {
+      int bz, m0, n0, kb0, kb1, ks;
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
+        continue;
+      for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
+        const int s = (int)(it % kStages);
+        ok = mbar_wait(smem_u32(&afull_bar[s]), (it / kStages) & 1, err);
+        if (!ok) break;
+        const uint32_t hi = smem_u32(smem + s * kStageBytes);
+        constexpr int kPer = kA / (16 * 64);  // float4 per converter thread
+        float4 v[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) v[i] = ld_shared_f4(hi + (uint32_t)(ct + 64 * i) * 16u);
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          st_shared_f4(hi + (uint32_t)kA + (uint32_t)(ct + 64 * i) * 16u,
+                       v[i].x - __uint_as_float(__float_as_uint(v[i].x) & 0xFFFFE000u),
+                       v[i].y - __uint_as_float(__float_as_uint(v[i].y) & 0xFFFFE000u),
+                       v[i].z - __uint_as_float(__float_as_uint(v[i].z) & 0xFFFFE000u),
+                       v[i].w - __uint_as_float(__float_as_uint(v[i].w) & 0xFFFFE000u));
+        // Generic-proxy writes made visible to the tensor core's reads.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&conv_bar[s]), 0));
+      }
+    }
+  } else if (warp >= 2 && warp < 2 + kAccWarps) {
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t ebox0 = smem_u32(epi) + (uint32_t)(warp - 2) * 8192u;
@@ -1247,12 +1330,12 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int BN, bool S, bool AMN, bool BMN>
+template <int BN, bool S, bool AMN, bool BMN, bool CONV>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
                const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int splits,
                int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfgP<BN, S>::kSmem;
-  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN>;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV>;
   static bool configured = false;
   if (!configured) {
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1263,22 +1346,22 @@ void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
   int64_t clusters = sm_count() / 2;
   if (clusters > tiles) clusters = tiles;
   if (clusters < 1) clusters = 1;
-  kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), kThreadsTC, smem, st>>>(ma, malo, mb, mblo, mc32, ep, M, N, K,
-                                                                          batch, splits, d_err);
+  kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), pp_threads<CONV>(), smem, st>>>(ma, malo, mb, mblo, mc32, ep, M,
+                                                                                  N, K, batch, splits, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
-template <int BN, bool S>
+template <int BN, bool S, bool CONV = false>
 void dispatch_pp(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
                  const CUtensorMap& mblo, const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M,
                  int N, int K, int splits, int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_pp<BN, S, true, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, true, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, true, true, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, true, false, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   } else {
-    if (bmn) launch_pp<BN, S, false, true>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, false, false>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, false, true, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, false, false, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   }
 }
 
@@ -1350,6 +1433,13 @@ bool g_persistent_enabled = [] {
   return !(v && v[0] == '0');
 }();
 
+// Strict persistent GEMMs with N <= 128 make A's low part in shared memory
+// (kConvA) unless TYSOR_CUDA_GEMM_CONV_A=0.
+bool g_conv_a_enabled = [] {
+  const char* v = getenv("TYSOR_CUDA_GEMM_CONV_A");
+  return !(v && v[0] == '0');
+}();
+
 int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c) {
   if (mode == kGemmExact || !g_two_sm_enabled || !g_persistent_enabled || M < 256 || (ldc & 3) != 0 ||
       (batch > 1 && (stride_c & 3) != 0) || M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
@@ -1404,6 +1494,13 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     return 0;
   }
   const bool strict = mode == kGemmStrict;
+  const int BN = N <= 128 ? 128 : 256;
+  // The pair forms need a full 256-row pair tile to be worth their cluster;
+  // the persistent one also needs C on 16-byte strides (its TMA stores).
+  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
+  const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
+  const bool persistent = g_two_sm_enabled && g_persistent_enabled && M >= 256 && c_tma;
+  const bool conv_a = strict && persistent && BN == 128 && g_conv_a_enabled;
   const float* alo = A.ptr;
   const float* blo = B.ptr;
   if (strict) {
@@ -1417,18 +1514,12 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
                       (scratch.a_lo ? "" : " (none)") + ", B needs " + std::to_string(nb) + " has " +
                       std::to_string(scratch.b_elems) + (scratch.b_lo ? "" : " (none)") + ")");
     if (!scratch.presplit) {
-      launch_split_lo(A.ptr, scratch.a_lo, na, st);
+      if (!conv_a) launch_split_lo(A.ptr, scratch.a_lo, na, st);
       launch_split_lo(B.ptr, scratch.b_lo, nb, st);
     }
     alo = scratch.a_lo;
     blo = scratch.b_lo;
   }
-  const int BN = N <= 128 ? 128 : 256;
-  // The pair forms need a full 256-row pair tile to be worth their cluster;
-  // the persistent one also needs C on 16-byte strides (its TMA stores).
-  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
-  const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
-  const bool persistent = g_two_sm_enabled && g_persistent_enabled && M >= 256 && c_tma;
   const bool two_sm = persistent || (g_two_sm_enabled && BN == 256 && M >= 256);
   const bool amn = A.trans, bmn = !B.trans;
   // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
@@ -1459,7 +1550,8 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
                    : make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const int im = (int)M, in = (int)N, ik = (int)K;
     if (BN == 128) {
-      if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      if (conv_a) dispatch_pp<128, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
       else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
     } else {
       if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);

@@ -501,6 +501,98 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
   }
 }
 
+// WPR warps per row for rows of 128 * NPL * WPR values (NPL float4 per
+// lane): the row stays in registers and both reductions are warp shuffles,
+// joined across the row's warps through shared memory under a named barrier
+// of the row's 32 * WPR threads (no block-wide barrier).  A block of 8 warps
+// has 8 / WPR rows in flight.  Same arithmetic and options as
+// softmax_reg_kernel.
+template <int NPL, int WPR>
+__global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                           int64_t rows, int q, int masked, int* err,
+                                                           float* __restrict__ lo, int skip_zero) {
+  constexpr int kWidth = 128 * NPL * WPR;
+  constexpr int kRowsPerBlock = 8 / WPR;
+  __shared__ float red[kRowsPerBlock][2][WPR];
+  const int lane = threadIdx.x & 31;
+  const int grp = (threadIdx.x >> 5) / WPR;  // the row slot of this warp
+  const int wr = (threadIdx.x >> 5) % WPR;   // this warp's part of the row
+  const int t = 32 * wr + lane;              // thread index within the row
+  for (int64_t r = (int64_t)blockIdx.x * kRowsPerBlock + grp; r < rows; r += (int64_t)gridDim.x * kRowsPerBlock) {
+    const int qi = masked ? (int)(r % q) : kWidth;
+    const float4* xr = (const float4*)(x + r * kWidth);
+    float4 v[NPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      const int c = 4 * (t + 32 * WPR * i);
+      float4 u = c > qi ? make_float4(-1.0e4f, -1.0e4f, -1.0e4f, -1.0e4f) : xr[t + 32 * WPR * i];
+      if (c + 1 > qi) u.y = -1.0e4f;
+      if (c + 2 > qi) u.z = -1.0e4f;
+      if (c + 3 > qi) u.w = -1.0e4f;
+      v[i] = u;
+      m = fmaxf(fmaxf(fmaxf(m, u.x), fmaxf(u.y, u.z)), u.w);
+    }
+    m = warp_max(m);
+    if constexpr (WPR > 1) {
+      if (lane == 0) red[grp][0][wr] = m;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * WPR) : "memory");
+      m = red[grp][0][0];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) m = fmaxf(m, red[grp][0][w]);
+    }
+    const bool masked_zero = expf(-1.0e4f - m) == 0.0f;
+    if (err != nullptr && t == 0 && qi < kWidth - 1 && !masked_zero) atomicCAS(err, 0, (int)kErrCausalSkip);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      if (masked_zero && 4 * (t + 32 * WPR * i) > qi) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      v[i].x = expf(v[i].x - m);
+      v[i].y = expf(v[i].y - m);
+      v[i].z = expf(v[i].z - m);
+      v[i].w = expf(v[i].w - m);
+      s += v[i].x;
+      s += v[i].y;
+      s += v[i].z;
+      s += v[i].w;
+    }
+    s = warp_sum(s);
+    if constexpr (WPR > 1) {
+      // Slot 1 is free: every thread of the row read slot 1 of the previous
+      // row before it arrived at this row's first barrier.
+      if (lane == 0) red[grp][1][wr] = s;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * WPR) : "memory");
+      s = red[grp][1][0];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) s += red[grp][1][w];
+    }
+    const float d = fmaxf(s, 1.1920928955078125e-7f);
+    float4* yr = (float4*)(out + r * kWidth);
+    float4* lr = lo ? (float4*)(lo + r * kWidth) : nullptr;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      const int j = t + 32 * WPR * i;
+      float4 u = v[i];
+      if (masked_zero && 4 * j > qi) {
+        if (!skip_zero) {
+          yr[j] = u;
+          if (lr) lr[j] = u;
+        }
+        continue;
+      }
+      u.x = u.x / d;
+      u.y = u.y / d;
+      u.z = u.z / d;
+      u.w = u.w / d;
+      yr[j] = u;
+      if (lr) lr[j] = lo_part4(u);
+    }
+  }
+}
+
 // Row r of [outer*q] rows of width k; row index within its q x k block is
 // r % q.  Values with col > row read as -1e4.
 __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __restrict__ out,
@@ -558,6 +650,53 @@ __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __rest
         const float p = expf((j > qi ? -1.0e4f : xr[j]) - m) / d;
         yr[j] = p;
         if (lo) lo[r * width + j] = lo_part(p);
+      }
+    }
+  }
+}
+
+// Row-wise form of masked_softmax_backward_kernel for k % 4 == 0 and 16-byte
+// aligned buffers: one warp per row (grid-stride over rows), so the causal
+// bound qi = r % q is computed once per row and the lanes walk only the
+// float4 groups that hold data (col <= qi), plus the zero groups above the
+// diagonal when they must be stored.  Same arithmetic per element.
+__global__ void __launch_bounds__(256) masked_softmax_backward_rows_kernel(
+    const float4* __restrict__ y, const float4* __restrict__ g, float4* __restrict__ dx, int64_t rows,
+    int64_t q, int k4, int accumulate, float4* __restrict__ lo, int skip_zero) {
+  const int lane = threadIdx.x & 31;
+  const bool store_zero = !(skip_zero || (accumulate && lo == nullptr));
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int qi = (int)(r % q);
+    const int data_end = min(k4, (qi >> 2) + 1);  // groups holding a col <= qi
+    const int end = store_zero ? k4 : data_end;
+    const int64_t base = r * k4;
+    for (int j0 = 0; j0 < end; j0 += 32 * 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + 32 * u + lane;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < data_end) {
+          const float4 yv = y[base + j], gv = g[base + j];
+          const int col = 4 * j;
+          v[u].x = (yv.x * (1.0f - yv.x)) * gv.x;
+          v[u].y = col + 1 > qi ? 0.0f : (yv.y * (1.0f - yv.y)) * gv.y;
+          v[u].z = col + 2 > qi ? 0.0f : (yv.z * (1.0f - yv.z)) * gv.z;
+          v[u].w = col + 3 > qi ? 0.0f : (yv.w * (1.0f - yv.w)) * gv.w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + 32 * u + lane;
+        if (j >= end) continue;
+        float4 t = v[u];
+        if (accumulate) {
+          const float4 o = dx[base + j];
+          t = make_float4(o.x + t.x, o.y + t.y, o.z + t.z, o.w + t.w);
+        }
+        dx[base + j] = t;
+        if (lo) lo[base + j] = lo_part4(t);
       }
     }
   }
@@ -1295,6 +1434,17 @@ void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cud
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
                  int* err, float* lo, int skip_zero, cudaStream_t st) {
   if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out) || (lo && !aligned16_host(lo))) return false;
+  if (width == 1024 || width == 2048) {
+    const int wpr = (int)(width / 1024);
+    const int64_t want = (rows * wpr + 7) / 8;
+    const int wblocks = (int)(want < 148 * 16 ? want : 148 * 16);
+    // Two warps per 2048-wide row measured faster than one warp holding 16
+    // float4 per lane (128 registers, half the resident warps) or four warps.
+    if (width == 1024) softmax_warp_kernel<8, 1><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero);
+    else softmax_warp_kernel<8, 2><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero);
+    check_launch();
+    return true;
+  }
   const int blocks = row_blocks(rows);
   switch (width / 1024) {
     case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
@@ -1321,6 +1471,17 @@ void launch_masked_softmax_backward(const float* y, const float* g, float* dx, i
                                     cudaStream_t st) {
   const int64_t n = outer * q * k;
   if (n <= 0) return;
+  if (k % 4 == 0 && k / 4 <= INT32_MAX && aligned16_host(y) && aligned16_host(g) && aligned16_host(dx) &&
+      (lo == nullptr || aligned16_host(lo))) {
+    const int64_t rows = outer * q;
+    const int64_t want = (rows + 7) / 8;
+    const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+    masked_softmax_backward_rows_kernel<<<blocks, 256, 0, st>>>(
+        (const float4*)y, (const float4*)g, (float4*)dx, rows, q, (int)(k / 4), accumulate, (float4*)lo,
+        skip_zero);
+    check_launch();
+    return;
+  }
   masked_softmax_backward_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
       y, g, dx, n, q, k, accumulate, lo, skip_zero);
   check_launch();
