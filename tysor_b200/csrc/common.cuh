@@ -85,8 +85,9 @@ enum GemmMode : int {
 };
 
 // Scratch the strict-mode GEMM needs: one "lo" copy of each operand, laid
-// out like the operand.  With `presplit` set the copies already hold
-// lo(A), lo(B) and the launcher does not recompute them.
+// out like the operand (no a_lo when gemm_converts_a).  With `presplit` set
+// the copies already hold lo(A), lo(B) and the launcher does not recompute
+// them.
 struct GemmScratch {
   float* a_lo;
   float* b_lo;
@@ -103,6 +104,11 @@ struct GemmScratch {
 // Workspace elements a split-K launch of this GEMM would need (0: it would
 // not split).
 int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c);
+
+// Whether gemm_launch runs this strict GEMM (C 16-byte aligned, with these
+// strides) on the kernel form that makes A's low part in shared memory:
+// its scratch then needs no a_lo (only b_lo).
+bool gemm_converts_a(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c);
 
 // Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
 extern bool g_two_sm_enabled;

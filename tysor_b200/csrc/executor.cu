@@ -190,6 +190,7 @@ struct Executor {
     params.clear();
     param_order.clear();
     prep_cache.clear();
+    lazy_lo.clear();
     deferred_matmul.clear();
     folded_scale.clear();
     masked_input.clear();
@@ -380,8 +381,24 @@ struct Executor {
     bool trans = false;
     int64_t ld = 0, bs = 0;
   };
-  std::map<std::tuple<Slot*, bool, int64_t, int64_t, int64_t, int64_t, int64_t>, std::pair<Slot*, Slot*>>
-      prep_cache;
+  using PrepKey = std::tuple<Slot*, bool, int64_t, int64_t, int64_t, int64_t, int64_t>;
+  std::map<PrepKey, std::pair<Slot*, Slot*>> prep_cache;
+  // Low parts that the kernel producing a value can write as it goes (the
+  // fused causal softmax, forward and backward), keyed like prep_cache.  The
+  // buffer is made, and the producer told to fill it, only when a GEMM's
+  // preparation asks for it: GEMMs that make A's low part in shared memory
+  // do not.
+  struct LazyLo {
+    Slot* slot = nullptr;
+    size_t n = 0;
+  };
+  std::map<PrepKey, std::shared_ptr<LazyLo>> lazy_lo;
+  std::shared_ptr<LazyLo> offer_lo(const PrepKey& key, size_t n) {
+    auto lo = std::make_shared<LazyLo>();
+    lo->n = n;
+    lazy_lo[key] = lo;
+    return lo;
+  }
   int plan_matmul_mode = kGemmStrict;
 
   static bool tma_aligned(int64_t ld, int64_t bs, int batch) {
@@ -395,7 +412,7 @@ struct Executor {
   // a step once produced, so one preparation serves every later GEMM that
   // reads the same operand the same way.
   Prepared prepare(StepList& out, Slot* x, bool is_a, bool trans, int64_t ld, int64_t bs,
-                   int batch, int64_t M, int64_t N, int64_t K) {
+                   int batch, int64_t M, int64_t N, int64_t K, bool need_lo = true) {
     const int64_t R = is_a ? (trans ? K : M) : (trans ? N : K);
     const int64_t C = is_a ? (trans ? M : K) : (trans ? K : N);
     const bool mn_major = is_a ? trans : !trans;
@@ -408,15 +425,21 @@ struct Executor {
     p.trans = trans;
     p.ld = ld;
     p.bs = bs;
-    if (!transpose && !strict) return p;
+    if (!transpose && !(strict && need_lo)) return p;
     // The cache holds memory objects (a copy of the stored [R][C] matrix,
     // transposed or not, and its low part); how a GEMM reads them (its
     // trans flag) is rebuilt for each caller.
     auto key = std::make_tuple(x, transpose, R, C, ld, bs, (int64_t)batch);
     auto it = prep_cache.find(key);
     std::pair<Slot*, Slot*> mem;
+    auto lz = lazy_lo.find(key);
     if (it != prep_cache.end()) {
       mem = it->second;
+    } else if (lz != lazy_lo.end()) {
+      // The producer writes the low part: claim its buffer.
+      lz->second->slot = alloc(lz->second->n);
+      mem = {x, lz->second->slot};
+      prep_cache[key] = mem;
     } else if (transpose) {
       const int64_t n = (int64_t)batch * R * C;
       mem = {alloc((size_t)n), strict ? alloc((size_t)n) : nullptr};
@@ -452,7 +475,8 @@ struct Executor {
     const bool tc = plan_matmul_mode != kGemmExact && K > 0 && tma_aligned(lda, sa, batch) &&
                     tma_aligned(ldb, sb, batch);
     if (tc) {
-      pa = prepare(out, a, true, ta, lda, sa, batch, M, N, K);
+      const bool conv_a = gemm_converts_a(batch, M, N, K, plan_matmul_mode, ldc, sc);
+      pa = prepare(out, a, true, ta, lda, sa, batch, M, N, K, !conv_a);
       pb = prepare(out, b, false, tb, ldb, sb, batch, M, N, K);
     }
     Context* cx = ctx;
@@ -468,10 +492,12 @@ struct Executor {
       GemmOutput O{c->p, ldc, sc};
       GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0, tri};
       GemmScratch s{nullptr, nullptr, 0, 0, 1};
-      if (pa.lo && pb.lo) {
+      if (pa.lo) {
         s.a_lo = pa.lo->p;
-        s.b_lo = pb.lo->p;
         s.a_elems = (int64_t)pa.lo->n;
+      }
+      if (pb.lo) {
+        s.b_lo = pb.lo->p;
         s.b_elems = (int64_t)pb.lo->n;
       }
       if (ws_elems > 0) {
@@ -1083,18 +1109,17 @@ struct Executor {
             // The guard is armed when a matmul will skip the masked entries.
             const bool lhs = is_matmul_lhs(node.output);
             int* err = lhs ? ctx->d_err : nullptr;
-            // A strict GEMM reading the probabilities as its left operand gets
-            // their low part from this kernel (registered where the GEMM's
-            // operand preparation looks it up) instead of a split pass.  The
-            // probabilities are a fresh, zero-filled buffer written only here,
-            // so the wholly masked (exact zero) groups are not stored.
-            Slot* lo = nullptr;
-            if (lhs && plan_matmul_mode == kGemmStrict && w % 4 == 0) {
-              lo = alloc((size_t)n);
-              prep_cache[std::make_tuple(c, false, q, w, w, q * w, outer)] = {c, lo};
-            }
+            // A strict GEMM reading the probabilities as its left operand and
+            // needing their low part gets it from this kernel (offered where
+            // the GEMM's operand preparation looks it up) instead of a split
+            // pass.  The probabilities are a fresh, zero-filled buffer written
+            // only here, so the wholly masked (exact zero) groups are not
+            // stored.
+            std::shared_ptr<LazyLo> lo;
+            if (lhs && plan_matmul_mode == kGemmStrict && w % 4 == 0)
+              lo = offer_lo(std::make_tuple(c, false, q, w, w, q * w, outer), (size_t)n);
             forward.push_back([=](cudaStream_t st) {
-              launch_masked_softmax(src->p, c->p, outer, q, w, err, lo ? lo->p : nullptr, 1, st);
+              launch_masked_softmax(src->p, c->p, outer, q, w, err, lo && lo->slot ? lo->slot->p : nullptr, 1, st);
             });
           } else {
             forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
@@ -1487,14 +1512,13 @@ struct Executor {
           // As in the forward: when the scores come from a (folded-scale)
           // matmul, its strict backward GEMMs read this gradient's low part
           // from here; a fresh zero-filled gradient skips its masked zeros.
-          Slot* lo = nullptr;
-          if (!acc && folded_scale.count(mi->second) && plan_matmul_mode == kGemmStrict && k % 4 == 0) {
-            lo = alloc((size_t)n);
-            prep_cache[std::make_tuple(d, false, q, k, k, q * k, outer)] = {d, lo};
-          }
+          std::shared_ptr<LazyLo> lo;
+          if (!acc && folded_scale.count(mi->second) && plan_matmul_mode == kGemmStrict && k % 4 == 0)
+            lo = offer_lo(std::make_tuple(d, false, q, k, k, q * k, outer), (size_t)n);
           const int skip = acc ? 0 : 1;
           backward.push_back([=](cudaStream_t st) {
-            launch_masked_softmax_backward(ys->p, g->p, d->p, outer, q, k, acc, lo ? lo->p : nullptr, skip, st);
+            launch_masked_softmax_backward(ys->p, g->p, d->p, outer, q, k, acc, lo && lo->slot ? lo->slot->p : nullptr,
+                                           skip, st);
           });
           return;
         }

@@ -1440,6 +1440,12 @@ bool g_conv_a_enabled = [] {
   return !(v && v[0] == '0');
 }();
 
+bool gemm_converts_a(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c) {
+  return mode == kGemmStrict && K > 0 && g_two_sm_enabled && g_persistent_enabled && g_conv_a_enabled &&
+         M >= 256 && N <= 128 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) && M <= INT32_MAX / 2 &&
+         N <= INT32_MAX / 2 && K <= INT32_MAX / 2;
+}
+
 int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c) {
   if (mode == kGemmExact || !g_two_sm_enabled || !g_persistent_enabled || M < 256 || (ldc & 3) != 0 ||
       (batch > 1 && (stride_c & 3) != 0) || M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
@@ -1506,7 +1512,7 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
   if (strict) {
     int64_t na, nb;
     gemm_scratch_need(batch, M, N, K, A, B, mode, &na, &nb);
-    if (scratch.a_lo == nullptr || scratch.b_lo == nullptr || scratch.a_elems < na ||
+    if ((!conv_a && (scratch.a_lo == nullptr || scratch.a_elems < na)) || scratch.b_lo == nullptr ||
         scratch.b_elems < nb)
       throw CudaError("strict matmul needs scratch for the split operands (batch " + std::to_string(batch) +
                       ", M " + std::to_string(M) + ", N " + std::to_string(N) + ", K " + std::to_string(K) +
