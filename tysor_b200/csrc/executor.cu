@@ -435,6 +435,15 @@ struct Executor {
     auto lz = lazy_lo.find(key);
     if (it != prep_cache.end()) {
       mem = it->second;
+      if (strict && need_lo && mem.second == nullptr) {
+        // An earlier GEMM took this transposed copy without its low part
+        // (it made A's low part itself): split the copy now.
+        const int64_t n = (int64_t)batch * R * C;
+        Slot *hi = mem.first, *lo = alloc((size_t)n);
+        out.push_back([=](cudaStream_t st) { launch_split_lo(hi->p, lo->p, n, st); });
+        mem.second = lo;
+        it->second = mem;
+      }
     } else if (lz != lazy_lo.end()) {
       // The producer writes the low part: claim its buffer.
       lz->second->slot = alloc(lz->second->n);
@@ -442,7 +451,7 @@ struct Executor {
       prep_cache[key] = mem;
     } else if (transpose) {
       const int64_t n = (int64_t)batch * R * C;
-      mem = {alloc((size_t)n), strict ? alloc((size_t)n) : nullptr};
+      mem = {alloc((size_t)n), strict && need_lo ? alloc((size_t)n) : nullptr};
       Slot *src = x, *hi = mem.first, *lo = mem.second;
       out.push_back([=](cudaStream_t st) {
         launch_split_transpose(src->p, hi->p, lo ? lo->p : nullptr, batch, R, C, st);

@@ -782,10 +782,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
 // of being loaded.  Each CTA's A tile lands on a barrier of its own
 // ("A full"); two converter warps per CTA write lo = a - tf32_trunc(a) beside
 // it, in the same swizzled positions, and arrive on the even CTA's
-// "converted" barrier, which the MMA issuer waits for besides "full".  For
-// the GEMMs that stream a large A past a narrow B (attention probabilities
-// times values, N <= 128) this halves the bytes read from HBM: the kernel
-// is bound by the A stream, not by the tensor core.
+// "converted" barrier, which the MMA issuer waits for besides "full".  The
+// A stream read from HBM halves and no split pass over A runs; the two
+// converter warps keep up with the tensor core (about 560 cycles per stage
+// against 750 of MMAs for 256 x 256 tiles).
 // ---------------------------------------------------------------------------
 
 template <bool kConvA>
@@ -1433,8 +1433,10 @@ bool g_persistent_enabled = [] {
   return !(v && v[0] == '0');
 }();
 
-// Strict persistent GEMMs with N <= 128 make A's low part in shared memory
-// (kConvA) unless TYSOR_CUDA_GEMM_CONV_A=0.
+// Strict persistent GEMMs make A's low part in shared memory (kConvA)
+// unless TYSOR_CUDA_GEMM_CONV_A=0: the split pass over A and the reads of
+// its low part from HBM disappear, at no cost to the tensor-core rate
+// (measured 1-12% faster per GEMM, split passes included).
 bool g_conv_a_enabled = [] {
   const char* v = getenv("TYSOR_CUDA_GEMM_CONV_A");
   return !(v && v[0] == '0');
@@ -1442,7 +1444,7 @@ bool g_conv_a_enabled = [] {
 
 bool gemm_converts_a(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c) {
   return mode == kGemmStrict && K > 0 && g_two_sm_enabled && g_persistent_enabled && g_conv_a_enabled &&
-         M >= 256 && N <= 128 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) && M <= INT32_MAX / 2 &&
+         M >= 256 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) && M <= INT32_MAX / 2 &&
          N <= INT32_MAX / 2 && K <= INT32_MAX / 2;
 }
 
@@ -1506,7 +1508,7 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
   const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
   const int c_tma = tma_ok(Cview, batch) ? 1 : 0;
   const bool persistent = g_two_sm_enabled && g_persistent_enabled && M >= 256 && c_tma;
-  const bool conv_a = strict && persistent && BN == 128 && g_conv_a_enabled;
+  const bool conv_a = strict && persistent && g_conv_a_enabled;
   const float* alo = A.ptr;
   const float* blo = B.ptr;
   if (strict) {
@@ -1560,7 +1562,8 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
       else if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
       else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
     } else {
-      if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      if (conv_a) dispatch_pp<256, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
       else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
     }
     if (splits > 1) {
