@@ -1198,6 +1198,58 @@ __global__ void split_transpose_kernel(const float* __restrict__ x, float* __res
   }
 }
 
+// The same for rows % 4 == 0 and cols % 4 == 0 (16-byte aligned x, hi_t,
+// lo_t): 64 x 64 tiles moved with float4 loads and stores, so each row
+// segment read or written is 256 contiguous bytes.  Edge tiles are clipped
+// to whole float4 groups (the dimensions are multiples of 4).
+__global__ void __launch_bounds__(256) split_transpose64_kernel(const float* __restrict__ x,
+                                                                float* __restrict__ hi_t,
+                                                                float* __restrict__ lo_t, int64_t rows,
+                                                                int64_t cols) {
+  __shared__ float tile[64][65];
+  const int64_t b = blockIdx.z;
+  const float* xb = x + b * rows * cols;
+  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+  const int t = threadIdx.x;
+  const int q = t & 15;  // float4 group within a 64-wide row segment
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int lr = (t >> 4) + 16 * i;
+    const int64_t r = r0 + lr, c = c0 + 4 * q;
+    if (r < rows && c < cols) {
+      const float4 v = *(const float4*)(xb + r * cols + c);
+      tile[lr][4 * q] = v.x;
+      tile[lr][4 * q + 1] = v.y;
+      tile[lr][4 * q + 2] = v.z;
+      tile[lr][4 * q + 3] = v.w;
+    }
+  }
+  __syncthreads();
+  float* hb = hi_t + b * rows * cols;
+  float* lb = lo_t ? lo_t + b * rows * cols : nullptr;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int lc = (t >> 4) + 16 * i;  // output row = input column
+    const int64_t c = c0 + lc, r = r0 + 4 * q;
+    if (c < cols && r < rows) {
+      float4 v;
+      v.x = tile[4 * q][lc];
+      v.y = tile[4 * q + 1][lc];
+      v.z = tile[4 * q + 2][lc];
+      v.w = tile[4 * q + 3][lc];
+      *(float4*)(hb + c * rows + r) = v;
+      if (lb) {
+        float4 l;
+        l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+        l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+        l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+        l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        *(float4*)(lb + c * rows + r) = l;
+      }
+    }
+  }
+}
+
 // CUDA-core GEMM: one output per thread, 16x16 tiles staged in shared
 // memory, k walked in increasing order with separately rounded products
 // and sums.
@@ -1468,8 +1520,14 @@ void launch_split_transpose(const float* x, float* hi_t, float* lo_t, int64_t ba
                             int64_t cols, cudaStream_t st) {
   if (batch <= 0 || rows <= 0 || cols <= 0) return;
   if (batch > 65535 || ceil_div(rows, 32) > 65535) throw CudaError("split_transpose: grid too large");
-  dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32), (unsigned)batch);
-  split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi_t, lo_t, rows, cols);
+  const auto a16 = [](const void* p) { return p == nullptr || (((uintptr_t)p) & 15) == 0; };
+  if (rows % 4 == 0 && cols % 4 == 0 && a16(x) && a16(hi_t) && a16(lo_t)) {
+    dim3 grid((unsigned)ceil_div(cols, 64), (unsigned)ceil_div(rows, 64), (unsigned)batch);
+    split_transpose64_kernel<<<grid, 256, 0, st>>>(x, hi_t, lo_t, rows, cols);
+  } else {
+    dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32), (unsigned)batch);
+    split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi_t, lo_t, rows, cols);
+  }
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }

@@ -1,8 +1,9 @@
 """Summaries of ncu output for profiles/.
 
-    python -m tysor_b200.profiling launches gpurun_out/launches.csv
+    python -m tysor_b200.profiling launches gpurun_out/launches.csv [N]
         per-kernel launches, total device time and share of a
-        `ncu --metrics gpu__time_duration.sum --csv` launch list
+        `ncu --metrics gpu__time_duration.sum --csv` launch list (N: only
+        the N launches after the bench's pre-timing spin kernel)
     python -m tysor_b200.profiling report prof.ncu-rep
         the headline metrics of an `ncu --set full` capture
     python -m tysor_b200.profiling traffic gpurun_out/sweep_ncu.csv
@@ -19,21 +20,32 @@ import sys
 UNIT_NS = {"ns": 1.0, "nsecond": 1.0, "us": 1e3, "usecond": 1e3, "ms": 1e6, "msecond": 1e6}
 
 
-def launches(path: str, foreign: str = "at::") -> str:
+def launches(path: str, foreign: str = "at::", window: int = 0) -> str:
     """Per-kernel launches, device time and share; kernels whose name
     contains `foreign` (PyTorch's own helper kernels, e.g. the spin kernel
     the bench runs before its timed region) are listed apart and left out of
-    the shares."""
+    the shares.  window > 0: only the first `window` launches of this
+    library after the first foreign launch (the bench's timed steps)."""
     text = open(path).read().splitlines()
     start = next(i for i, line in enumerate(text) if line.startswith('"ID"'))
     rows = list(csv.reader(text[start:]))
     hdr = rows[0]
     ki, mi, ui, vi = (hdr.index(k) for k in ("Kernel Name", "Metric Name", "Metric Unit", "Metric Value"))
     agg = collections.defaultdict(lambda: [0, 0.0])
+    seen_foreign, taken = window == 0, 0
     for r in rows[1:]:
         if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
             continue
         name = r[ki].split("(")[0].replace("(anonymous namespace)::", "")
+        if window:
+            if foreign in name:
+                if seen_foreign:
+                    continue
+                seen_foreign = True
+            elif not seen_foreign or taken >= window:
+                continue
+            else:
+                taken += 1
         agg[name][0] += 1
         agg[name][1] += float(r[vi].replace(",", "")) * UNIT_NS.get(r[ui], 1.0)
     ours = {k: v for k, v in agg.items() if foreign not in k}
@@ -107,4 +119,7 @@ def traffic(path: str) -> str:
 
 if __name__ == "__main__":
     kind, path = sys.argv[1], sys.argv[2]
-    print({"launches": launches, "report": report, "traffic": traffic}[kind](path))
+    if kind == "launches" and len(sys.argv) > 3:
+        print(launches(path, window=int(sys.argv[3])))
+    else:
+        print({"launches": launches, "report": report, "traffic": traffic}[kind](path))
