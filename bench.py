@@ -455,8 +455,10 @@ def run_ours(args, rank, world, local_rank, dist):
     total_units = wl.total_units(world)
     value = total_units / (ms_per_step / 1000.0)
 
-    # end to end through the public API: every step uploads this rank's
-    # inputs from pinned host memory, runs one step and reads the loss back.
+    # end to end through the public API: every step's inputs are copied from
+    # pinned host memory (queued one step ahead on the library's copy stream,
+    # as a data loader prefetches, so the copy overlaps the previous step),
+    # then the step runs and its loss is read back.
     e2e_steps = max(5, args.steps)
     e2e_sampler = ClockSampler(gpu_index_for(local_rank)) if rank == 0 else None
     if e2e_sampler:
@@ -465,18 +467,25 @@ def run_ours(args, rank, world, local_rank, dist):
     if dist is not None:
         dist.barrier()
     ctx.synchronize()
-    t0 = time.perf_counter()
-    upload_ms, step_wall = [], []
-    for _ in range(e2e_steps):
-        t1 = time.perf_counter()
-        u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        u0.record(stream)
+    def prefetch():
         for name, arr in pinned.items():
-            native.check(lib.tysor_cuda_graph_upload_input(ex.handle, name.encode(), native.fptr(arr), arr.size))
-        u1.record(stream)
-        ex.train(1, lr)  # returns the step's loss on the host
+            native.check(lib.tysor_cuda_graph_prefetch_input(ex.handle, name.encode(), native.fptr(arr), arr.size))
+
+    # Warm the prefetch path (its copy stream and both staging buffers are
+    # made on first use) outside the timed region.
+    prefetch()
+    prefetch()
+    ex.train(2, lr)
+    ctx.synchronize()
+    t0 = time.perf_counter()
+    step_wall = []
+    prefetch()  # the first step's inputs
+    for i in range(e2e_steps):
+        t1 = time.perf_counter()
+        if i + 1 < e2e_steps:
+            prefetch()  # the next step's inputs, copied while this step computes
+        ex.train(1, lr)  # takes the oldest prefetched inputs; returns the step's loss on the host
         step_wall.append((time.perf_counter() - t1) * 1e3)
-        upload_ms.append(u0.elapsed_time(u1))
     e2e_s = (time.perf_counter() - t0) / e2e_steps
     e2e_clocks = e2e_sampler.stop() if e2e_sampler else None
     if dist is not None:
@@ -504,7 +513,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "config": cfg, "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(total_units / e2e_s, 1), "unit": wl.unit,
                     "h2d_bytes_per_step": int(sum(a.nbytes for a in inputs.values())), "d2h_bytes_per_step": 4,
-                    "h2d_ms_per_step": [round(v, 2) for v in upload_ms],
+                    "h2d": "pinned host -> device on a copy stream, one step ahead (overlaps the previous step)",
                     "wall_ms_per_step": [round(v, 2) for v in step_wall],
                     "median_wall_ms": round(float(np.median(step_wall)), 2), "clocks": e2e_clocks},
             "gpu_launches": int(launches), "clocks": clocks,

@@ -213,6 +213,17 @@ bool tysor_cuda_graph_set_input(void* graph, const char* name, const float* data
  * that its buffers are planned. */
 bool tysor_cuda_graph_upload_input(void* graph, const char* name, const float* data,
                                    size_t count);
+/* Queues `count` floats from host memory (pinned memory makes the copy
+ * asynchronous) as the next value of graph input `name`: the copy runs on
+ * a separate copy stream into one of two device staging buffers, so it
+ * overlaps kernels already queued, and the next run / backward / train call
+ * copies the oldest queued value into the input's buffer before its first
+ * step.  At most two values per input may wait.  The graph must have been
+ * run, backpropagated or trained once.  (Prefetching the next step's inputs
+ * the way a data loader does; the reference reads inputs once, at startup:
+ * tensor.rs:24-34.) */
+bool tysor_cuda_graph_prefetch_input(void* graph, const char* name, const float* data,
+                                     size_t count);
 /* Optional: initial value of a trainable parameter (e.g. "linear_5_weight")
  * instead of its pattern initialiser (layers.rs:39-75). */
 bool tysor_cuda_graph_set_parameter(void* graph, const char* name, const float* data,

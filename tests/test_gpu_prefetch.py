@@ -1,0 +1,75 @@
+"""Prefetched inputs (tysor_cuda_graph_prefetch_input): values queued from
+pinned host memory on the copy stream are taken by the following train
+calls in order, and training on them gives exactly the losses and
+parameters of uploading each value right before its step."""
+import numpy as np
+import pytest
+import torch
+
+from tysor_b200 import native
+from tysor_b200.programs import mlp_train, random_parameters
+
+pytestmark = pytest.mark.gpu
+
+ROWS, D_IN, D_H = 512, 128, 256
+
+
+def batches(n):
+    rng = np.random.default_rng(11)
+    return [{"x": rng.standard_normal((ROWS, D_IN), dtype=np.float32),
+             "target": rng.standard_normal((ROWS, D_IN), dtype=np.float32)} for _ in range(n)]
+
+
+def make(ctx, first):
+    from tysor_b200.runtime import CudaGraphExecutor
+    g = mlp_train(D_IN, D_H, D_IN, lr=0.01, iterations=1, loss_scale=1.0 / (ROWS * D_IN))
+    ex = CudaGraphExecutor(ctx, g, {"x": [ROWS, D_IN], "target": [ROWS, D_IN]}, inputs=first,
+                           parameters=random_parameters(g, 5))
+    return g, ex
+
+
+def test_prefetched_steps_match_uploaded_steps(cuda_ctx):
+    data = batches(5)
+    # Reference run: upload each batch, then step.
+    g, ex = make(cuda_ctx, data[0])
+    ex.train(1, 0.0)  # plans the buffers (lr 0: parameters unchanged)
+    want = []
+    for b in data:
+        for name, arr in b.items():
+            ex.upload_input(name, arr)
+        want += ex.train(1, 0.01)
+    names = list(random_parameters(g, 5))
+    want_p = {n: ex.parameter(n) for n in names}
+    ex.close()
+
+    # Prefetched run from pinned host memory, one step ahead.
+    g, ex = make(cuda_ctx, data[0])
+    ex.train(1, 0.0)
+    pinned = [{k: torch.from_numpy(v).pin_memory() for k, v in b.items()} for b in data]
+    got = []
+    for name, t in pinned[0].items():
+        ex.prefetch_input(name, t.numpy())
+    for i in range(len(data)):
+        if i + 1 < len(data):
+            for name, t in pinned[i + 1].items():
+                ex.prefetch_input(name, t.numpy())
+        got += ex.train(1, 0.01)
+    assert got == want
+    for n in names:
+        np.testing.assert_array_equal(ex.parameter(n), want_p[n])
+    ex.close()
+
+
+def test_prefetch_queue_holds_two_values(cuda_ctx):
+    data = batches(3)
+    g, ex = make(cuda_ctx, data[0])
+    ex.train(1, 0.0)
+    ex.prefetch_input("x", data[1]["x"])
+    ex.prefetch_input("x", data[2]["x"])
+    with pytest.raises(native.NativeError, match="two prefetched values"):
+        ex.prefetch_input("x", data[0]["x"])
+    with pytest.raises(native.NativeError, match="holds"):
+        ex.prefetch_input("target", data[0]["target"][:5])
+    ex.train(2, 0.0)  # takes one queued value (the call's first step); one stays queued
+    ex.prefetch_input("x", data[0]["x"])
+    ex.close()

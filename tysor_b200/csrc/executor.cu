@@ -164,14 +164,89 @@ struct Executor {
   float* loss_hist = nullptr;  // per-step losses of one train call (device)
   int loss_hist_cap = 0;
 
+  // Prefetched inputs: two device staging buffers per input, filled from
+  // host memory on a copy stream while earlier steps compute, and copied
+  // into the input's buffer (a kernel on the compute stream) at the start of
+  // the next run / backward / train call.
+  struct Staging {
+    float* buf = nullptr;
+    size_t n = 0;
+    cudaEvent_t copied = nullptr;    // the host-to-device copy landed
+    cudaEvent_t consumed = nullptr;  // the compute stream has copied it out
+    bool used = false;               // `consumed` has been recorded
+  };
+  struct PrefetchQueue {
+    Staging st[2];
+    int next = 0;            // buffer the next prefetch fills
+    std::deque<int> ready;   // filled buffers, oldest first
+  };
+  std::map<std::string, PrefetchQueue> prefetch;
+  cudaStream_t copy_stream = nullptr;
+
+  void prefetch_input(const std::string& name, Slot* s, const float* data, size_t count) {
+    PrefetchQueue& pq = prefetch[name];
+    if (pq.ready.size() >= 2) throw CudaError("input '" + name + "' already has two prefetched values waiting");
+    if (!copy_stream) TYSOR_CUDA(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking));
+    const int k = pq.next;
+    Staging& b = pq.st[k];
+    if (b.n != count) {
+      if (b.buf) {
+        TYSOR_CUDA(cudaStreamSynchronize(copy_stream));
+        TYSOR_CUDA(cudaStreamSynchronize(ctx->stream));
+        TYSOR_CUDA(cudaFree(b.buf));
+      }
+      b.buf = nullptr;
+      b.used = false;
+      TYSOR_CUDA(cudaMalloc(&b.buf, sizeof(float) * (count ? count : 1)));
+      b.n = count;
+    }
+    if (!b.copied) TYSOR_CUDA(cudaEventCreateWithFlags(&b.copied, cudaEventDisableTiming));
+    if (!b.consumed) TYSOR_CUDA(cudaEventCreateWithFlags(&b.consumed, cudaEventDisableTiming));
+    // The buffer's previous value must have been copied out first.
+    if (b.used) TYSOR_CUDA(cudaStreamWaitEvent(copy_stream, b.consumed, 0));
+    TYSOR_CUDA(cudaMemcpyAsync(b.buf, data, sizeof(float) * count, cudaMemcpyHostToDevice, copy_stream));
+    TYSOR_CUDA(cudaEventRecord(b.copied, copy_stream));
+    pq.ready.push_back(k);
+    pq.next = 1 - k;
+    (void)s;
+  }
+
+  // Stored inputs (pattern or set_input values) unless a device value was
+  // uploaded, then the oldest prefetched value of each input.
   void run_uploads() {
     for (auto& [name, fn] : upload)
       if (!device_inputs.count(name)) fn(ctx->stream);
+    for (auto& [name, pq] : prefetch) {
+      if (pq.ready.empty()) continue;
+      Staging& b = pq.st[pq.ready.front()];
+      pq.ready.pop_front();
+      Slot* dst = input_slot(name);
+      if (!dst || dst->n != b.n) throw CudaError("prefetched input '" + name + "' no longer matches its buffer");
+      TYSOR_CUDA(cudaStreamWaitEvent(ctx->stream, b.copied, 0));
+      launch_unary(kUnaryCopy, b.buf, dst->p, (int64_t)b.n, 0.0f, ctx->stream);
+      TYSOR_CUDA(cudaEventRecord(b.consumed, ctx->stream));
+      b.used = true;
+    }
+  }
+
+  // The device buffer of graph input `name` (null if there is none).
+  Slot* input_slot(const std::string& name) {
+    for (const GValue& v : values)
+      if (v.is_param && v.name == name) return v.id < (int)hv.size() ? hv[v.id].slot : nullptr;
+    return nullptr;
   }
 
   ~Executor() {
     release();
     if (loss_hist) cudaFree(loss_hist);
+    if (copy_stream) cudaStreamSynchronize(copy_stream);
+    for (auto& [name, pq] : prefetch)
+      for (Staging& b : pq.st) {
+        if (b.buf) cudaFree(b.buf);
+        if (b.copied) cudaEventDestroy(b.copied);
+        if (b.consumed) cudaEventDestroy(b.consumed);
+      }
+    if (copy_stream) cudaStreamDestroy(copy_stream);
   }
 
   void release() {
@@ -1751,6 +1826,22 @@ bool tysor_cuda_graph_upload_input(void* graph, const char* name, const float* d
       return;
     }
     throw CudaError(std::string("no graph input named '") + name + "'");
+  });
+}
+
+bool tysor_cuda_graph_prefetch_input(void* graph, const char* name, const float* data,
+                                     size_t count) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (e->mode < 0 || e->dirty) throw CudaError("graph buffers are not planned yet: run it once first");
+    Slot* s = e->input_slot(name);
+    if (!s) throw CudaError(std::string("no graph input named '") + name + "'");
+    if (count != s->n)
+      throw CudaError("input '" + std::string(name) + "' holds " + std::to_string(s->n) + " values, " +
+                      std::to_string(count) + " given");
+    e->prefetch_input(name, s, data, count);
+    // Later calls must not overwrite it with a stored input.
+    e->device_inputs.insert(name);
   });
 }
 

@@ -76,6 +76,7 @@ SIGNATURES = {
     "tysor_cuda_graph_set_input": (c_bool, [V, c_char_p, FP, c_size_t]),
     "tysor_cuda_graph_set_parameter": (c_bool, [V, c_char_p, FP, c_size_t]),
     "tysor_cuda_graph_upload_input": (c_bool, [V, c_char_p, FP, c_size_t]),
+    "tysor_cuda_graph_prefetch_input": (c_bool, [V, c_char_p, FP, c_size_t]),
     "tysor_cuda_graph_run": (c_bool, [V]),
     "tysor_cuda_graph_backward": (c_bool, [V]),
     "tysor_cuda_graph_train": (c_bool, [V, c_int, c_double, FP]),

@@ -14,6 +14,7 @@ operation runs in libtysor_cuda on an sm_100 device.
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import json
 import os
@@ -145,6 +146,9 @@ class CudaGraphExecutor:
         self._lib = native.lib()
         self.handle = self._lib.tysor_cuda_graph_new(ctx.handle, graph.to_text().encode())
         check(self.handle, "graph_new")
+        # host arrays of queued prefetches (at most two wait per input, one
+        # more may still be copying)
+        self._prefetched: Dict[str, collections.deque] = {}
         ctx._adopt(self)
         for name, dims in shapes.items():
             self.set_shape(name, dims)
@@ -269,6 +273,17 @@ class CudaGraphExecutor:
         host memory makes it asynchronous); the graph must have run once."""
         a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
         check(self._lib.tysor_cuda_graph_upload_input(self.handle, name.encode(), fptr(a), a.size), "upload_input")
+
+    def prefetch_input(self, name: str, arr) -> None:
+        """Queues the next value of a graph input: host -> device on the
+        library's copy stream (overlapping kernels already queued), taken by
+        the next run / backward / train call; at most two may wait.  Pinned
+        host memory makes the copy asynchronous: keep the array unchanged
+        until that call returns (this object holds a reference until then)."""
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        check(self._lib.tysor_cuda_graph_prefetch_input(self.handle, name.encode(), fptr(a), a.size),
+              "prefetch_input")
+        self._prefetched.setdefault(name, collections.deque(maxlen=3)).append(a)
 
     def __del__(self):
         try:
