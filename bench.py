@@ -475,7 +475,8 @@ def run_ours(args, rank, world, local_rank, dist):
     # made on first use) outside the timed region.
     prefetch()
     prefetch()
-    ex.train(2, lr)
+    ex.train(1, lr)  # each call takes one queued value
+    ex.train(1, lr)
     ctx.synchronize()
     t0 = time.perf_counter()
     step_wall = []
