@@ -269,6 +269,7 @@ struct Executor {
     deferred_matmul.clear();
     folded_scale.clear();
     masked_input.clear();
+    fused_silu.clear();
     causal_scores.clear();
     causal_probs.clear();
     folded_transpose.clear();
@@ -762,6 +763,22 @@ struct Executor {
 
   HVal plan_binary(const GNode& node) {
     if (folded_scale.count(node.output)) return plan_folded_scale(node);
+    for (int side = 0; side < 2; ++side) {
+      auto fs = fused_silu.find(node.inputs[side]);
+      if (fs == fused_silu.end()) continue;
+      const HVal& sv = val(node.inputs[side]);
+      const HVal& other = val(node.inputs[1 - side]);
+      if (node.binop == '*' && other.t == HVal::Tensor) {
+        if (sv.shape != other.shape) fail("tensor shape mismatch");
+        HVal o = new_tensor(sv.shape);
+        Slot *x = val(fs->second).slot, *u = other.slot, *c = o.slot;
+        const int64_t n = numel(sv.shape);
+        forward.push_back([=](cudaStream_t st) { launch_silu_mul(x->p, u->p, c->p, n, st); });
+        return o;
+      }
+      materialize_silu(node.inputs[side]);
+      break;
+    }
     const HVal& l = val(node.inputs[0]);
     const HVal& r = val(node.inputs[1]);
     const int op = binop_code(node.binop);
@@ -810,6 +827,7 @@ struct Executor {
   std::map<int, std::pair<int, int>> deferred_matmul;  // matmul out -> (lhs, rhs)
   std::map<int, int> folded_scale;          // scale node out -> matmul out
   std::map<int, int> masked_input;          // causal_mask out -> its input
+  std::map<int, int> fused_silu;            // SiLU out -> its input, computed inside the '*' reading it
   // Fused causal attention: score matmuls (output ids) whose scaled output
   // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
   std::set<int> causal_scores;
@@ -831,6 +849,33 @@ struct Executor {
   const GNode* sole_consumer(int id) const {
     if (external_uses[id] != 0 || consumers[id].size() != 1) return nullptr;
     return &nodes[consumers[id][0]];
+  }
+
+  // SiLU(x) whose output feeds only one tensor '*' (SwiGLU's product) and
+  // whose input feeds only it: the product runs as one pass (silu_mul) and
+  // its backward as another, and the activation is never stored.  --backward
+  // reports every value's gradient, so the fusion is for --run and --train.
+  bool silu_fuses_into_mul(const GNode& node) const {
+    if (mode == kModeBackward) return false;
+    const GNode* c = sole_consumer(node.output);
+    if (!c || c->kind != kNBinary || c->binop != '*' || c->inputs.size() != 2 || c->inputs[0] == c->inputs[1])
+      return false;
+    const int other = c->inputs[0] == node.output ? c->inputs[1] : c->inputs[0];
+    if (fused_silu.count(other)) return false;  // one fused operand per product
+    const GNode* xp = sole_consumer(node.inputs.at(1));
+    return xp && xp->output == node.output;
+  }
+
+  // Gives a fused SiLU output its own buffer after all (its '*' turned out
+  // not to be a tensor product).
+  void materialize_silu(int vid) {
+    const int xi = fused_silu.at(vid);
+    fused_silu.erase(vid);
+    HVal& h = hv.at(vid);
+    h.slot = alloc((size_t)numel(h.shape));
+    Slot *a = val(xi).slot, *c = h.slot;
+    const int64_t n = numel(h.shape);
+    forward.push_back([=](cudaStream_t st) { launch_unary(kUnarySilu, a->p, c->p, n, 0.0f, st); });
   }
 
   const GNode* producer_node(int id) const {
@@ -1175,6 +1220,13 @@ struct Executor {
         return o;
       }
       case HVal::Act: {
+        if (cl.act == "SiLU" && x.slot && silu_fuses_into_mul(node)) {
+          fused_silu[node.output] = node.inputs.at(1);
+          HVal o;
+          o.t = HVal::Tensor;
+          o.shape = x.shape;
+          return o;
+        }
         HVal o = new_tensor(x.shape);
         Slot *a = x.slot, *c = o.slot;
         const int64_t n = numel(x.shape);
@@ -1369,7 +1421,24 @@ struct Executor {
             switch (node.binop) {
               case '+': emit_copy(g, li, n); emit_copy(g, ri, n); break;
               case '-': emit_copy(g, li, n); emit_neg(g, ri, n); break;
-              case '*': emit_tt(kMul, g, r.slot, li, n); emit_tt(kMul, g, l.slot, ri, n); break;
+              case '*': {
+                const bool fl = fused_silu.count(li) != 0, fr = fused_silu.count(ri) != 0;
+                if (fl || fr) {
+                  // h = silu(x) * u: both gradients in one pass; the SiLU
+                  // node adds nothing later (its input feeds only it).
+                  const int xi = fused_silu.at(fl ? li : ri), ui = fl ? ri : li;
+                  Slot *xs = val(xi).slot, *us = val(ui).slot;
+                  auto [dx, accx] = contrib(xi);
+                  auto [du, accu] = contrib(ui);
+                  backward.push_back([=](cudaStream_t st) {
+                    launch_silu_mul_backward(xs->p, us->p, g->p, dx->p, du->p, n, accx, accu, st);
+                  });
+                  break;
+                }
+                emit_tt(kMul, g, r.slot, li, n);
+                emit_tt(kMul, g, l.slot, ri, n);
+                break;
+              }
               case '/': {
                 emit_tt(kDiv, g, r.slot, li, n);
                 if (!train) {
@@ -1585,6 +1654,7 @@ struct Executor {
         return;
       }
       case HVal::Act: {
+        if (fused_silu.count(node.output)) return;  // done by its '*' (silu_mul_backward)
         auto mi = masked_input.find(xi);
         if (cl.act == "Softmax" && mi != masked_input.end()) {
           // Softmax(causal_mask(x)): both backward rules in one pass, straight
@@ -1751,7 +1821,8 @@ bool guarded_g(F&& f) {
 Slot* value_slot(Executor* e, int id, std::vector<int64_t>* shape) {
   if (id < 0 || id >= (int)e->hv.size()) throw CudaError("value id out of range");
   const HVal& h = e->hv[id];
-  if (h.t == HVal::Tensor && !h.slot && (e->folded_transpose.count(id) || e->masked_input.count(id)))
+  if (h.t == HVal::Tensor && !h.slot &&
+      (e->folded_transpose.count(id) || e->masked_input.count(id) || e->fused_silu.count(id)))
     throw CudaError("value " + std::to_string(id) + " is not materialised: it was fused into its consumer");
   if (h.t != HVal::Tensor || !h.slot) throw CudaError("value " + std::to_string(id) + " is not a tensor");
   if (shape) *shape = h.shape;

@@ -234,6 +234,90 @@ __global__ void silu_backward_kernel(const float* x, const float* g, float* dx, 
   });
 }
 
+// h = silu(x) * u in one pass (SwiGLU's product): silu as unary_kernel
+// computes it, then the product, so h is bit-identical to the two-kernel
+// form; silu(x) is never stored.
+__global__ void silu_mul_kernel(const float* x, const float* u, float* h, int64_t n) {
+  ew_run<2>(In<2>{{x, u}}, h, n, 0, [=](const float (&a)[2]) {
+    const float s = apply_unary(kUnarySilu, a[0], 0.0f);
+    return s * a[1];
+  });
+}
+
+// Backward of h = silu(x) * u from dh: du (+)= dh * silu(x) and
+// dx (+)= silu_backward(x, dh * u), each element computed exactly as the
+// '*' backward and silu_backward_kernel compute it; inputs read once, the
+// activation's gradient never stored.
+__device__ __forceinline__ void silu_mul_grad(float x, float u, float dh, float* dx, float* du) {
+  const float s = apply_unary(kUnarySilu, x, 0.0f);
+  *du = dh * s;
+  const float ds = dh * u;
+  const float sg = 1.0f / (1.0f + expf(-x));
+  float t = x * sg;
+  t = t * (1.0f - sg);
+  *dx = ds * (sg + t);
+}
+
+__global__ void silu_mul_backward_kernel(const float* __restrict__ x, const float* __restrict__ u,
+                                         const float* __restrict__ dh, float* __restrict__ dx,
+                                         float* __restrict__ du, int64_t n, int acc_x, int acc_u) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  int64_t done = 0;
+  if (aligned16(x) && aligned16(u) && aligned16(dh) && aligned16(dx) && aligned16(du)) {
+    const int64_t n4 = n >> 2;
+    int64_t i = t0;
+    for (; i + stride < n4; i += 2 * stride) {
+      float4 a[2], b[2], c[2], ox[2], ou[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        a[k] = ((const float4*)x)[i + k * stride];
+        b[k] = ((const float4*)u)[i + k * stride];
+        c[k] = ((const float4*)dh)[i + k * stride];
+        ox[k] = acc_x ? ((const float4*)dx)[i + k * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ou[k] = acc_u ? ((const float4*)du)[i + k * stride] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float4 rx, ru;
+        silu_mul_grad(a[k].x, b[k].x, c[k].x, &rx.x, &ru.x);
+        silu_mul_grad(a[k].y, b[k].y, c[k].y, &rx.y, &ru.y);
+        silu_mul_grad(a[k].z, b[k].z, c[k].z, &rx.z, &ru.z);
+        silu_mul_grad(a[k].w, b[k].w, c[k].w, &rx.w, &ru.w);
+        if (acc_x) rx = make_float4(ox[k].x + rx.x, ox[k].y + rx.y, ox[k].z + rx.z, ox[k].w + rx.w);
+        if (acc_u) ru = make_float4(ou[k].x + ru.x, ou[k].y + ru.y, ou[k].z + ru.z, ou[k].w + ru.w);
+        ((float4*)dx)[i + k * stride] = rx;
+        ((float4*)du)[i + k * stride] = ru;
+      }
+    }
+    for (; i < n4; i += stride) {
+      const float4 a = ((const float4*)x)[i], b = ((const float4*)u)[i], c = ((const float4*)dh)[i];
+      float4 rx, ru;
+      silu_mul_grad(a.x, b.x, c.x, &rx.x, &ru.x);
+      silu_mul_grad(a.y, b.y, c.y, &rx.y, &ru.y);
+      silu_mul_grad(a.z, b.z, c.z, &rx.z, &ru.z);
+      silu_mul_grad(a.w, b.w, c.w, &rx.w, &ru.w);
+      if (acc_x) {
+        const float4 o = ((const float4*)dx)[i];
+        rx = make_float4(o.x + rx.x, o.y + rx.y, o.z + rx.z, o.w + rx.w);
+      }
+      if (acc_u) {
+        const float4 o = ((const float4*)du)[i];
+        ru = make_float4(o.x + ru.x, o.y + ru.y, o.z + ru.z, o.w + ru.w);
+      }
+      ((float4*)dx)[i] = rx;
+      ((float4*)du)[i] = ru;
+    }
+    done = n4 << 2;
+  }
+  for (int64_t e = done + t0; e < n; e += stride) {
+    float rx, ru;
+    silu_mul_grad(x[e], u[e], dh[e], &rx, &ru);
+    dx[e] = acc_x ? dx[e] + rx : rx;
+    du[e] = acc_u ? du[e] + ru : ru;
+  }
+}
+
 __global__ void softmax_backward_kernel(const float* y, const float* g, float* dx, int64_t n,
                                         int acc) {
   ew_run<2>(In<2>{{y, g}}, dx, n, acc, [=](const float (&a)[2]) {
@@ -1354,6 +1438,19 @@ void launch_relu_backward(const float* y, const float* g, float* dx, int64_t n, 
                           cudaStream_t st) {
   if (n <= 0) return;
   relu_backward_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(y, g, dx, n, acc);
+  check_launch();
+}
+
+void launch_silu_mul(const float* x, const float* u, float* h, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  silu_mul_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(x, u, h, n);
+  check_launch();
+}
+
+void launch_silu_mul_backward(const float* x, const float* u, const float* dh, float* dx, float* du, int64_t n,
+                              int acc_x, int acc_u, cudaStream_t st) {
+  if (n <= 0) return;
+  silu_mul_backward_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(x, u, dh, dx, du, n, acc_x, acc_u);
   check_launch();
 }
 

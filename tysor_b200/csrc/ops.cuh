@@ -44,6 +44,12 @@ void launch_div_rhs_grad(const float* g, const float* lhs, const float* rhs, flo
 // Backward helpers.  `accumulate` adds the result into dx instead of storing.
 void launch_relu_backward(const float* out_act, const float* grad, float* dx, int64_t n,
                           int accumulate, cudaStream_t st);
+// h = silu(x) * u (SwiGLU's product, bit-identical to silu then '*').
+void launch_silu_mul(const float* x, const float* u, float* h, int64_t n, cudaStream_t st);
+// Its backward from dh: du (+)= dh * silu(x), dx (+)= silu'(x) rule of
+// launch_silu_backward applied to dh * u.
+void launch_silu_mul_backward(const float* x, const float* u, const float* dh, float* dx, float* du, int64_t n,
+                              int acc_x, int acc_u, cudaStream_t st);
 void launch_silu_backward(const float* x, const float* grad, float* dx, int64_t n, int accumulate,
                           cudaStream_t st);
 void launch_softmax_backward(const float* y, const float* grad, float* dx, int64_t n,
