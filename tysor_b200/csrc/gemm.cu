@@ -786,6 +786,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
 // A stream read from HBM halves and no split pass over A runs; the two
 // converter warps keep up with the tensor core (about 560 cycles per stage
 // against 750 of MMAs for 256 x 256 tiles).
+//
+// kStackB (strict, BN = 128, i.e. N <= 128): B's high and low parts are
+// stacked along N, so each k-slice takes two MMAs instead of three: a_hi x
+// [b_hi | b_lo] (one 256-wide instruction into 256 accumulator columns) and
+// a_lo x b_hi (128 wide, into the first 128).  In a pair MMA each CTA
+// supplies half of B's columns at the same shared-memory offset, so the
+// even CTA stages b_hi (all 128 columns) and the odd CTA b_lo in the wide
+// region, and each stages its half of b_hi in the narrow one.  The
+// accumulator warps add column c and c + 128 of each chunk.  A 128-wide
+// instruction costs nearly as much to issue as a 256-wide one, and the
+// N <= 128 GEMMs (attention with head dim 128) are bound by that.
 // ---------------------------------------------------------------------------
 
 template <bool kConvA>
@@ -793,11 +804,12 @@ constexpr int pp_threads() {
   return kThreadsTC + (kConvA ? 64 : 0);
 }
 
-template <int BN, bool kStrict>
+template <int BN, bool kStrict, bool kStackB = false>
 struct PipeCfgP {
   static constexpr int kA = BM * BK * 4;        // this CTA's 128 rows of A
   static constexpr int kB = (BN / 2) * BK * 4;  // this CTA's half of B
-  static constexpr int kStageBytes = kStrict ? 2 * (kA + kB) : (kA + kB);
+  // kStackB: a 2*BN-wide stacked B region (2 kB) and a BN-wide one (kB).
+  static constexpr int kStageBytes = kStackB ? 2 * kA + 3 * kB : kStrict ? 2 * (kA + kB) : (kA + kB);
   static constexpr int kEpiBytes = kAccWarps * 2 * 4096;  // two 32x32 boxes per accumulator warp
   static constexpr int kStagesRaw = (160 * 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
@@ -843,7 +855,7 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   return true;
 }
 
-template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA>
+template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>(), 1)
     gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_alo,
@@ -854,22 +866,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   // splits > 1: map_c32 addresses the split-K workspace ([splits * batch][M]
   // [N] raw sums); alpha, bias, relu and accumulate are left to the
   // reduction that sums the parts.
-  using Cfg = PipeCfgP<BN, kStrict>;
+  using Cfg = PipeCfgP<BN, kStrict, kStackB>;
   constexpr int kA = Cfg::kA;
   constexpr int kB = Cfg::kB;
   constexpr int kStages = Cfg::kStages;
   constexpr int kStageBytes = Cfg::kStageBytes;
   static_assert(!kConvA || kStrict, "A's low part is only used in strict mode");
+  static_assert(!kStackB || (kStrict && BN == 128), "stacked B is the strict N <= 128 form");
   static_assert(!kConvA || (4 * kStages + 4) * 8 + 4 <= 256, "barriers exceed their reserve");
   static_assert(kA % (16 * 64) == 0, "converter warps cover the A tile in float4 rounds");
   // Both CTAs' loads on the even CTA's "full" barrier (with kConvA: B only).
-  constexpr uint32_t kTxBytes = kConvA ? 2 * (kStageBytes - 2 * kA) : 2 * kStageBytes;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kATx = kConvA ? 0 : (kStrict ? 2 * kA : kA);
+  constexpr uint32_t kBTx = kStackB ? 3 * kB : (kStrict ? 2 * kB : kB);
+  constexpr uint32_t kTxBytes = 2 * (kATx + kBTx);
+  constexpr int kBufCols = kStackB ? 2 * BN : BN;  // tensor-memory columns of one chunk buffer
+  constexpr uint32_t kTmemCols = 2 * kBufCols;
   constexpr int kHalf = BN / 2;  // columns per accumulator warp
   constexpr int kBH = BN / 2;    // rows (K-major) or columns (MN-major) of B per CTA
   constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kAmn ? 1u : 0u) << 15) |
                               ((kBmn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
                               ((uint32_t)(256 >> 4) << 24);
+  constexpr uint32_t kIdescWide = (kIdesc & ~(0x3Fu << 17)) | ((uint32_t)((2 * BN) >> 3) << 17);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -965,11 +982,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
           } else {
             tma_load_3d_pair(ta, ma, fb, k0, m0, bz);
           }
+          if (kStackB) continue;  // B below
           if (kBmn) {
 #pragma unroll
             for (int i = 0; i < kBH / 32; ++i) tma_load_3d_pair(tb + i * 2048, mb, fb, nb0 + 32 * i, k0, bz);
           } else {
             tma_load_3d_pair(tb, mb, fb, k0, nb0, bz);
+          }
+        }
+        if (kStackB) {
+          // Wide region: all BN columns of b_hi (even CTA) or b_lo (odd CTA);
+          // narrow region: this CTA's half of b_hi.
+          const CUtensorMap* mw = rank ? &map_blo : &map_b;
+          const uint32_t tw = base + 2 * kA, tn = tw + 2 * kB;
+          if (kBmn) {
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i) tma_load_3d_pair(tw + i * 2048, mw, fb, n0 + 32 * i, k0, bz);
+#pragma unroll
+            for (int i = 0; i < kBH / 32; ++i) tma_load_3d_pair(tn + i * 2048, &map_b, fb, nb0 + 32 * i, k0, bz);
+          } else {
+            tma_load_3d_pair(tw, mw, fb, k0, n0, bz);
+            tma_load_3d_pair(tw + kB, mw, fb, k0, n0 + kBH, bz);
+            tma_load_3d_pair(tn, &map_b, fb, k0, nb0, bz);
           }
         }
       }
@@ -997,7 +1031,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         if (ok && kConvA) ok = mbar_wait(smem_u32(&conv_bar[s]), (it / kStages) & 1, err);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        const uint32_t d = tmem + (uint32_t)(buf * kBufCols);
         const uint32_t base = smem_u32(smem + s * kStageBytes);
         const int nmaps = kStrict ? 2 : 1;
         const uint32_t ta = base, talo = base + kA;
@@ -1007,7 +1041,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
           const uint64_t da = operand_desc(ta, kAmn, kk);
           const uint64_t db = operand_desc(tb, kBmn, kk);
           const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-          if (kStrict) {
+          if (kStackB) {
+            // tb: the wide region ([b_hi | b_lo] across the pair), tb + 2 kB:
+            // the narrow one (b_hi).
+            umma_tf32_pair(d, da, db, kIdescWide, acc);
+            umma_tf32_pair(d, operand_desc(talo, kAmn, kk), operand_desc(tb + 2 * kB, kBmn, kk), kIdesc, 1u);
+          } else if (kStrict) {
             umma_tf32_pair(d, operand_desc(talo, kAmn, kk), db, kIdesc, acc);
             umma_tf32_pair(d, da, operand_desc(tblo, kBmn, kk), kIdesc, 1u);
             umma_tf32_pair(d, da, db, kIdesc, 1u);
@@ -1071,11 +1110,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         have = mbar_wait(smem_u32(&tfull_bar[buf]), (gch >> 1) & 1, err);
         if (!have) break;
         tc_fence_after();
-        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + half * kHalf);
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kBufCols + half * kHalf);
 #pragma unroll
         for (int cc = 0; cc < kHalf; cc += 16) {
           float r[16];
           tmem_ld16(taddr + cc, r);
+          if (kStackB) {
+            // Column c + BN holds a_hi . b_lo of output column c.
+            float r2[16];
+            tmem_ld16(taddr + BN + cc, r2);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = r[i] + r2[i];
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) acc[cc + i] = acc[cc + i] + r[i];
         }
@@ -1382,12 +1428,12 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int BN, bool S, bool AMN, bool BMN, bool CONV>
+template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
                const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int splits,
                int* d_err, cudaStream_t st) {
-  constexpr int smem = PipeCfgP<BN, S>::kSmem;
-  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV>;
+  constexpr int smem = PipeCfgP<BN, S, STACK>::kSmem;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK>;
   static bool configured = false;
   if (!configured) {
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1404,16 +1450,16 @@ void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
-template <int BN, bool S, bool CONV = false>
+template <int BN, bool S, bool CONV = false, bool STACK = false>
 void dispatch_pp(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
                  const CUtensorMap& mblo, const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M,
                  int N, int K, int splits, int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_pp<BN, S, true, true, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, true, false, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, true, true, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, true, false, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   } else {
-    if (bmn) launch_pp<BN, S, false, true, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, false, false, CONV>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, false, true, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, false, false, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
   }
 }
 
@@ -1482,6 +1528,13 @@ bool g_two_sm_enabled = [] {
 // when N <= 128) unless TYSOR_CUDA_GEMM_PERSISTENT=0.
 bool g_persistent_enabled = [] {
   const char* v = getenv("TYSOR_CUDA_GEMM_PERSISTENT");
+  return !(v && v[0] == '0');
+}();
+
+// Strict persistent GEMMs with N <= 128 stack B's high and low parts
+// (kStackB) unless TYSOR_CUDA_GEMM_STACK_B=0.
+bool g_stack_b_enabled = [] {
+  const char* v = getenv("TYSOR_CUDA_GEMM_STACK_B");
   return !(v && v[0] == '0');
 }();
 
@@ -1616,7 +1669,12 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
                    : make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const int im = (int)M, in = (int)N, ik = (int)K;
     if (BN == 128) {
-      if (conv_a) dispatch_pp<128, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      const bool stack_b = strict && g_stack_b_enabled;
+      if (conv_a && stack_b)
+        dispatch_pp<128, true, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else if (conv_a) dispatch_pp<128, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      else if (stack_b)
+        dispatch_pp<128, true, false, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
       else if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
       else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
     } else {
