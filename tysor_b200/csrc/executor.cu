@@ -270,6 +270,7 @@ struct Executor {
     folded_scale.clear();
     masked_input.clear();
     fused_silu.clear();
+    seqmajor_transpose.clear();
     causal_scores.clear();
     causal_probs.clear();
     folded_transpose.clear();
@@ -828,6 +829,7 @@ struct Executor {
   std::map<int, int> folded_scale;          // scale node out -> matmul out
   std::map<int, int> masked_input;          // causal_mask out -> its input
   std::map<int, int> fused_silu;            // SiLU out -> its input, computed inside the '*' reading it
+  std::map<int, int> seqmajor_transpose;    // transpose(1, 2) out -> its input, read in place by rope / repeat_kv
   // Fused causal attention: score matmuls (output ids) whose scaled output
   // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
   std::set<int> causal_scores;
@@ -1033,8 +1035,11 @@ struct Executor {
       int64_t inner = 1;
       for (size_t i = 2; i < x.shape.size(); ++i) inner *= x.shape[i];
       const int64_t outer = x.shape[0], heads = x.shape[1];
-      Slot *a = x.slot, *c = o.slot;
-      forward.push_back([=](cudaStream_t st) { launch_repeat_kv(a->p, c->p, outer, heads, inner, rep, st); });
+      // A folded transpose(1, 2): read its [B, S, heads, hd] input in place.
+      auto sm = seqmajor_transpose.find(node.inputs.at(0));
+      Slot *a = sm != seqmajor_transpose.end() ? val(sm->second).slot : x.slot, *c = o.slot;
+      const int64_t seq = sm != seqmajor_transpose.end() ? x.shape[2] : 0;
+      forward.push_back([=](cudaStream_t st) { launch_repeat_kv(a->p, c->p, outer, heads, inner, rep, st, seq); });
       return o;
     }
     if (op == "causal_mask") {
@@ -1065,8 +1070,11 @@ struct Executor {
       rope_dims(x.shape, hd, &outer, &seq);
       HVal o = new_tensor(x.shape);
       const float2* tab = ctx->rope_table(seq, hd / 2, theta);
-      Slot *a = x.slot, *c = o.slot;
-      forward.push_back([=](cudaStream_t st) { launch_rope(a->p, c->p, tab, outer, seq, hd / 2, st); });
+      // A folded transpose(1, 2): read its [B, S, H, hd] input in place.
+      auto sm = seqmajor_transpose.find(node.inputs.at(0));
+      Slot *a = sm != seqmajor_transpose.end() ? val(sm->second).slot : x.slot, *c = o.slot;
+      const int64_t hs = sm != seqmajor_transpose.end() ? x.shape[1] : 0;
+      forward.push_back([=](cudaStream_t st) { launch_rope(a->p, c->p, tab, outer, seq, hd / 2, st, hs); });
       return o;
     }
     if (op == "transpose") {
@@ -1079,9 +1087,20 @@ struct Executor {
       if (a > b) std::swap(a, b);
       std::vector<int64_t> s = x.shape;
       std::swap(s[a], s[b]);
+      const GNode* c = sole_consumer(node.output);
+      // transpose(1, 2) of [B, S, H, hd] read only by rope or repeat_kv:
+      // those kernels read the untransposed layout in place (and write the
+      // gradient back in it).  Train and run modes.
+      if (mode != kModeBackward && rank == 4 && a == 1 && b == 2 && c && c->kind == kNCall &&
+          (c->op == "rope" || c->op == "repeat_kv") && c->inputs.at(0) == node.output && x.slot) {
+        seqmajor_transpose[node.output] = node.inputs[0];
+        HVal o;
+        o.t = HVal::Tensor;
+        o.shape = s;
+        return o;
+      }
       // Folded into its only consumer, a matmul, when it swaps the last two
       // axes (train and run modes; --backward reports every value's grad).
-      const GNode* c = sole_consumer(node.output);
       if (mode != kModeBackward && rank >= 2 && a == rank - 2 && b == rank - 1 && c && c->kind == kNPrimitive &&
           c->op == "matmul" && x.slot) {
         folded_transpose[node.output] = node.inputs[0];
@@ -1564,9 +1583,12 @@ struct Executor {
       int64_t inner = 1;
       for (size_t i = 2; i < x.shape.size(); ++i) inner *= x.shape[i];
       const int64_t outer = x.shape[0], heads = x.shape[1];
-      auto [d, acc] = contrib(xi);
+      // Through a folded transpose(1, 2): the gradient goes to its input.
+      auto sm = seqmajor_transpose.find(xi);
+      const int64_t seq = sm != seqmajor_transpose.end() ? x.shape[2] : 0;
+      auto [d, acc] = contrib(sm != seqmajor_transpose.end() ? sm->second : xi);
       backward.push_back([=](cudaStream_t st) {
-        launch_repeat_kv_backward(g->p, d->p, outer, heads, inner, rep, acc, st);
+        launch_repeat_kv_backward(g->p, d->p, outer, heads, inner, rep, acc, st, seq);
       });
     } else if (op == "causal_mask") {
       const int64_t q = out.shape[out.shape.size() - 2], k = out.shape.back();
@@ -1579,8 +1601,13 @@ struct Executor {
       int64_t outer, seq;
       rope_dims(out.shape, hd, &outer, &seq);
       const float2* tab = ctx->rope_table(seq, hd / 2, theta);
-      auto [d, acc] = contrib(xi);
-      backward.push_back([=](cudaStream_t st) { launch_rope_backward(g->p, d->p, tab, outer, seq, hd / 2, acc, st); });
+      // Through a folded transpose(1, 2): the gradient goes to its input.
+      auto sm = seqmajor_transpose.find(xi);
+      const int64_t hs = sm != seqmajor_transpose.end() ? out.shape[1] : 0;
+      auto [d, acc] = contrib(sm != seqmajor_transpose.end() ? sm->second : xi);
+      backward.push_back([=](cudaStream_t st) {
+        launch_rope_backward(g->p, d->p, tab, outer, seq, hd / 2, acc, st, hs);
+      });
     }
     // Other library calls contribute nothing in train mode (executor.rs:661-687).
   }
@@ -1822,7 +1849,8 @@ Slot* value_slot(Executor* e, int id, std::vector<int64_t>* shape) {
   if (id < 0 || id >= (int)e->hv.size()) throw CudaError("value id out of range");
   const HVal& h = e->hv[id];
   if (h.t == HVal::Tensor && !h.slot &&
-      (e->folded_transpose.count(id) || e->masked_input.count(id) || e->fused_silu.count(id)))
+      (e->folded_transpose.count(id) || e->masked_input.count(id) || e->fused_silu.count(id) ||
+       e->seqmajor_transpose.count(id)))
     throw CudaError("value " + std::to_string(id) + " is not materialised: it was fused into its consumer");
   if (h.t != HVal::Tensor || !h.slot) throw CudaError("value " + std::to_string(id) + " is not a tensor");
   if (shape) *shape = h.shape;

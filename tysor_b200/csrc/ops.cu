@@ -1171,41 +1171,77 @@ __global__ void emb_accumulate_kernel(const float* __restrict__ grad, const int*
   }
 }
 
+// out[o][h][e] = x[o][h / repeats][e] over rows of `inner` values.  seq > 0:
+// x is stored [outer][seq][heads][inner / seq] instead (the layout before a
+// transpose(1, 2), folded here), so row h of out gathers its positions from
+// x's head h / repeats.
+__device__ __forceinline__ int64_t kv_src(int64_t o, int64_t kvh, int64_t e, int64_t heads, int64_t inner,
+                                          int64_t seq) {
+  if (seq == 0) return (o * heads + kvh) * inner + e;
+  const int64_t hd = inner / seq, p = e / hd, d = e - p * hd;
+  return ((o * seq + p) * heads + kvh) * hd + d;
+}
+
 __global__ void repeat_kv_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                 int64_t outer, int64_t heads, int64_t inner, int64_t repeats) {
+                                 int64_t outer, int64_t heads, int64_t inner, int64_t repeats, int64_t seq) {
   const int64_t out_heads = heads * repeats;
   const int64_t n = outer * out_heads * inner;
-  const bool vec = (inner & 3) == 0 && aligned16(x) && aligned16(out);
+  const bool vec = (inner & 3) == 0 && (seq == 0 || ((inner / seq) & 3) == 0) && aligned16(x) && aligned16(out);
   if (vec) {
     const int64_t inner4 = inner >> 2;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n >> 2);
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t e = i % inner4, row = i / inner4;
       const int64_t o = row / out_heads, dh = row % out_heads;
-      ((float4*)out)[i] = ((const float4*)x)[(o * heads + dh / repeats) * inner4 + e];
+      ((float4*)out)[i] = *(const float4*)(x + kv_src(o, dh / repeats, 4 * e, heads, inner, seq));
     }
   } else {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t e = i % inner, row = i / inner;
       const int64_t o = row / out_heads, dh = row % out_heads;
-      out[i] = x[(o * heads + dh / repeats) * inner + e];
+      out[i] = x[kv_src(o, dh / repeats, e, heads, inner, seq)];
     }
   }
 }
 
+// dx[o][h][e] (+)= sum over r in order of g[o][h * repeats + r][e]; with
+// seq > 0, dx is stored [outer][seq][heads][inner / seq].  Four values per
+// thread when the rows allow float4 accesses.
 __global__ void repeat_kv_backward_kernel(const float* __restrict__ g, float* __restrict__ dx,
                                           int64_t outer, int64_t heads, int64_t inner,
-                                          int64_t repeats, int accumulate) {
+                                          int64_t repeats, int accumulate, int64_t seq) {
   const int64_t n = outer * heads * inner;
   const int64_t out_heads = heads * repeats;
+  const bool vec = (inner & 3) == 0 && (seq == 0 || ((inner / seq) & 3) == 0) && aligned16(g) && aligned16(dx);
+  if (vec) {
+    const int64_t inner4 = inner >> 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n >> 2);
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t e = i % inner4, row = i / inner4;
+      const int64_t o = row / heads, h = row % heads;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int64_t r = 0; r < repeats; ++r) {
+        const float4 v = ((const float4*)g)[(o * out_heads + h * repeats + r) * inner4 + e];
+        acc = make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+      }
+      float4* d = (float4*)(dx + kv_src(o, h, 4 * e, heads, inner, seq));
+      if (accumulate) {
+        const float4 p = *d;
+        acc = make_float4(p.x + acc.x, p.y + acc.y, p.z + acc.z, p.w + acc.w);
+      }
+      *d = acc;
+    }
+    return;
+  }
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i % inner, row = i / inner;
     const int64_t o = row / heads, h = row % heads;
     float acc = 0.0f;
     for (int64_t r = 0; r < repeats; ++r) acc = acc + g[(o * out_heads + h * repeats + r) * inner + e];
-    dx[i] = accumulate ? dx[i] + acc : acc;
+    float* d = dx + kv_src(o, h, e, heads, inner, seq);
+    *d = accumulate ? *d + acc : acc;
   }
 }
 
@@ -1240,36 +1276,82 @@ __global__ void causal_mask_kernel(const float* __restrict__ x, float* __restric
   (void)backward;
 }
 
+// Row `rp` (= o * seq + p, o = b * H + h) of a [B, H, seq, hd] tensor, as
+// a row of the same tensor stored [B, seq, H, hd] when hs = H (the layout
+// before transpose(1, 2)), or unchanged when hs = 0.
+__device__ __forceinline__ int64_t head_row(int64_t rp, int64_t seq, int64_t hs) {
+  if (hs == 0) return rp;
+  const int64_t o = rp / seq, p = rp - o * seq;
+  const int64_t b = o / hs, h = o - b * hs;
+  return (b * seq + p) * hs + h;
+}
+
+// RoPE over rows of hd = 2 * half (rotate-half pairs f, f + half at
+// position p = row % seq).  in_hs / out_hs: the input / output is stored
+// [B, seq, H, hd] (head_row), which folds a transpose(1, 2) beside it.  Four
+// pairs per thread with float4 accesses when half % 4 == 0 and the buffers
+// are 16-byte aligned; the same products and sums per element either way.
+__device__ __forceinline__ void rope_pair(float a, float b, float2 cs, int backward, float* y1, float* y2) {
+  if (!backward) {
+    const float t1 = a * cs.x, t2 = b * cs.y;
+    const float t3 = a * cs.y, t4 = b * cs.x;
+    *y1 = t1 - t2;
+    *y2 = t3 + t4;
+  } else {
+    const float t1 = a * cs.x, t2 = b * cs.y;
+    const float t3 = (-a) * cs.y, t4 = b * cs.x;
+    *y1 = t1 + t2;
+    *y2 = t3 + t4;
+  }
+}
+
 __global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ out,
                             const float2* __restrict__ table, int64_t outer, int64_t seq,
-                            int64_t half, int backward, int accumulate) {
-  const int64_t n = outer * seq * half;
+                            int64_t half, int backward, int accumulate, int64_t in_hs, int64_t out_hs) {
   const int64_t hd = 2 * half;
+  if ((half & 3) == 0 && aligned16(x) && aligned16(out) && aligned16(table)) {
+    const int64_t q4 = half >> 2;
+    const int64_t n = outer * seq * q4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t f = 4 * (i % q4), rp = i / q4;
+      const int64_t p = rp % seq;
+      const float4 c01 = *(const float4*)(table + p * half + f);
+      const float4 c23 = *(const float4*)(table + p * half + f + 2);
+      const int64_t ib = head_row(rp, seq, in_hs) * hd, ob = head_row(rp, seq, out_hs) * hd;
+      const float4 a = *(const float4*)(x + ib + f), b = *(const float4*)(x + ib + half + f);
+      float4 y1, y2;
+      rope_pair(a.x, b.x, make_float2(c01.x, c01.y), backward, &y1.x, &y2.x);
+      rope_pair(a.y, b.y, make_float2(c01.z, c01.w), backward, &y1.y, &y2.y);
+      rope_pair(a.z, b.z, make_float2(c23.x, c23.y), backward, &y1.z, &y2.z);
+      rope_pair(a.w, b.w, make_float2(c23.z, c23.w), backward, &y1.w, &y2.w);
+      float4* o1 = (float4*)(out + ob + f);
+      float4* o2 = (float4*)(out + ob + half + f);
+      if (accumulate) {
+        const float4 p1 = *o1, p2 = *o2;
+        y1 = make_float4(p1.x + y1.x, p1.y + y1.y, p1.z + y1.z, p1.w + y1.w);
+        y2 = make_float4(p2.x + y2.x, p2.y + y2.y, p2.z + y2.z, p2.w + y2.w);
+      }
+      *o1 = y1;
+      *o2 = y2;
+    }
+    return;
+  }
+  const int64_t n = outer * seq * half;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t f = i % half, rp = i / half;  // rp = o*seq + p
     const int64_t p = rp % seq;
     const float2 cs = table[p * half + f];
-    const int64_t base = rp * hd;
-    const float a = x[base + f], b = x[base + half + f];
+    const int64_t ib = head_row(rp, seq, in_hs) * hd, ob = head_row(rp, seq, out_hs) * hd;
     float y1, y2;
-    if (!backward) {
-      const float t1 = a * cs.x, t2 = b * cs.y;
-      const float t3 = a * cs.y, t4 = b * cs.x;
-      y1 = t1 - t2;
-      y2 = t3 + t4;
-    } else {
-      const float t1 = a * cs.x, t2 = b * cs.y;
-      const float t3 = (-a) * cs.y, t4 = b * cs.x;
-      y1 = t1 + t2;
-      y2 = t3 + t4;
-    }
+    rope_pair(x[ib + f], x[ib + half + f], cs, backward, &y1, &y2);
     if (accumulate) {
-      out[base + f] = out[base + f] + y1;
-      out[base + half + f] = out[base + half + f] + y2;
+      out[ob + f] = out[ob + f] + y1;
+      out[ob + half + f] = out[ob + half + f] + y2;
     } else {
-      out[base + f] = y1;
-      out[base + half + f] = y2;
+      out[ob + f] = y1;
+      out[ob + half + f] = y2;
     }
   }
 }
@@ -1658,20 +1740,20 @@ void launch_embedding_backward(const float* grad, const float* idx, float* wgrad
 }
 
 void launch_repeat_kv(const float* x, float* out, int64_t outer, int64_t heads, int64_t inner,
-                      int64_t repeats, cudaStream_t st) {
+                      int64_t repeats, cudaStream_t st, int64_t seq) {
   const int64_t n = outer * heads * repeats * inner;
   if (n <= 0) return;
   repeat_kv_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
-      x, out, outer, heads, inner, repeats);
+      x, out, outer, heads, inner, repeats, seq);
   check_launch();
 }
 
 void launch_repeat_kv_backward(const float* g, float* dx, int64_t outer, int64_t heads,
-                               int64_t inner, int64_t repeats, int accumulate, cudaStream_t st) {
+                               int64_t inner, int64_t repeats, int accumulate, cudaStream_t st, int64_t seq) {
   const int64_t n = outer * heads * inner;
   if (n <= 0) return;
-  repeat_kv_backward_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(
-      g, dx, outer, heads, inner, repeats, accumulate);
+  repeat_kv_backward_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
+      g, dx, outer, heads, inner, repeats, accumulate, seq);
   check_launch();
 }
 
@@ -1694,20 +1776,20 @@ void launch_causal_mask_backward(const float* g, float* dx, int64_t outer, int64
 }
 
 void launch_rope(const float* x, float* out, const float2* table, int64_t outer, int64_t seq,
-                 int64_t half, cudaStream_t st) {
+                 int64_t half, cudaStream_t st, int64_t in_hs) {
   const int64_t n = outer * seq * half;
   if (n <= 0) return;
   rope_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(x, out, table, outer, seq,
-                                                                    half, 0, 0);
+                                                                    half, 0, 0, in_hs, 0);
   check_launch();
 }
 
 void launch_rope_backward(const float* g, float* dx, const float2* table, int64_t outer,
-                          int64_t seq, int64_t half, int accumulate, cudaStream_t st) {
+                          int64_t seq, int64_t half, int accumulate, cudaStream_t st, int64_t out_hs) {
   const int64_t n = outer * seq * half;
   if (n <= 0) return;
   rope_kernel<<<elementwise_blocks(n, kThreads), kThreads, 0, st>>>(g, dx, table, outer, seq, half,
-                                                                    1, accumulate);
+                                                                    1, accumulate, 0, out_hs);
   check_launch();
 }
 

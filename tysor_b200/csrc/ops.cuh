@@ -105,19 +105,25 @@ void launch_embedding_backward(const float* grad, const float* idx, float* wgrad
                                int64_t num, int64_t dim, void* work, int accumulate,
                                cudaStream_t st);
 
+// seq > 0: x (forward) / dx (backward) is stored [outer][seq][heads][inner /
+// seq], the layout before transpose(1, 2) (the transpose is folded here).
 void launch_repeat_kv(const float* x, float* out, int64_t outer, int64_t heads, int64_t inner,
-                      int64_t repeats, cudaStream_t st);
+                      int64_t repeats, cudaStream_t st, int64_t seq = 0);
 void launch_repeat_kv_backward(const float* grad, float* dx, int64_t outer, int64_t heads,
-                               int64_t inner, int64_t repeats, int accumulate, cudaStream_t st);
+                               int64_t inner, int64_t repeats, int accumulate, cudaStream_t st,
+                               int64_t seq = 0);
 void launch_causal_mask(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
                         cudaStream_t st);
 void launch_causal_mask_backward(const float* grad, float* dx, int64_t outer, int64_t q, int64_t k,
                                  int accumulate, cudaStream_t st);
 // `table` holds seq x half (cos, sin) pairs computed on the host.
+// in_hs / out_hs = H > 0: the input (forward) / output (backward) is stored
+// [B][seq][H][hd] while rows run over [B][H][seq] (a transpose(1, 2) folded
+// here).
 void launch_rope(const float* x, float* out, const float2* table, int64_t outer, int64_t seq,
-                 int64_t half, cudaStream_t st);
+                 int64_t half, cudaStream_t st, int64_t in_hs = 0);
 void launch_rope_backward(const float* grad, float* dx, const float2* table, int64_t outer,
-                          int64_t seq, int64_t half, int accumulate, cudaStream_t st);
+                          int64_t seq, int64_t half, int accumulate, cudaStream_t st, int64_t out_hs = 0);
 // Exchange axes a < b of a row-major tensor of rank <= 8.
 void launch_transpose(const float* x, float* out, const int64_t* dims, int rank, int a, int b,
                       int accumulate, cudaStream_t st);
