@@ -340,8 +340,8 @@ def measured_peaks():
 def roofline(ctx, lib, stream, m, n, k):
     """The dominant strict matmul, timed alone with events on the library's
     stream, in the layout the executor hands the kernel (A [m,k] and B
-    [n,k], both K-major); the split kernels that make the operands' low
-    parts run inside each call."""
+    [n,k], both K-major); the split kernel that makes B's low part runs
+    inside each call (A's is made inside the GEMM)."""
     import torch
     from tysor_b200 import native
     from tysor_b200.runtime import DeviceBuffer
@@ -371,10 +371,16 @@ def roofline(ctx, lib, stream, m, n, k):
     achieved = 2.0 * m * n * k / (call_ms / 1000.0) / 1e12
     for buf in (A, Bw, C):
         buf.free()
-    return {"bound": "tensor", "kernel": "matmul strict 3xTF32 (split_lo x2 + gemm_tf32_2sm_kernel<256,1,0,0>, cluster pairs)",
+    # DRAM bytes (read + write) of one launch of this kernel on this shape,
+    # from the ncu capture summarised in profiles/gemm_tf32_16384x5632x2048.md.
+    traffic = 1155622000 + 350200832 if (m, n, k) == (16384, 5632, 2048) else None
+    return {"bound": "tensor",
+            "kernel": "matmul strict 3xTF32 (split_lo of B + gemm_tf32_pp_kernel<256,1,0,0,1,0>: persistent "
+                      "cluster pairs, A's low part made in shared memory)",
             "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
             "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
-            "tensor_pipe_frac": round(3 * achieved / tf32_peak, 4), "traffic": None,
+            "tensor_pipe_frac": round(3 * achieved / tf32_peak, 4), "traffic": traffic,
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "ms_per_launch": round(call_ms, 4),
             "peak_source": f"{src}: bf16_tflops {peaks['bf16_tflops']} x 0.5 (tf32 rate is half of bf16)",
             "note": "strict 3xTF32 issues 3 tensor-core MMAs per product: frac is capped at 0.333; "
