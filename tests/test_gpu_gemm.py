@@ -184,10 +184,11 @@ print("ok")
 @pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (False, False)])
 def test_persistent_pair_kernel_many_tiles_per_cluster(cuda_ctx, ta, tb):
     """Shapes with several 256-row tiles per resident cluster (the persistent
-    schedule), both B tile widths (N > 128 and N <= 128), batched, with the
+    schedule), both B tile widths (N > 128 and N <= 128, the latter with B's
+    parts stacked, including N not a multiple of 32), batched, with the
     accumulate / alpha / bias epilogue."""
     rng = np.random.default_rng(11)
-    for (bt, m, n, k) in [(3, 1024, 1000, 200), (2, 2048, 128, 336)]:
+    for (bt, m, n, k) in [(3, 1024, 1000, 200), (2, 2048, 128, 336), (1, 520, 100, 88), (2, 768, 40, 64)]:
         a = rng.uniform(-1, 1, (bt, m, k)).astype(np.float32)
         b = rng.uniform(-1, 1, (bt, k, n)).astype(np.float32)
         c0 = rng.uniform(-1, 1, (bt, m, n)).astype(np.float32)
@@ -197,3 +198,41 @@ def test_persistent_pair_kernel_many_tiles_per_cluster(cuda_ctx, ta, tb):
         for i in range(bt):
             want = c0[i] + oracle_mm(a[i], b[i]) * np.float32(0.75)
             assert frob(got[i], want) < 1e-5, (bt, m, n, k, i)
+
+
+@pytest.mark.parametrize("switch", ["TYSOR_CUDA_GEMM_CONV_A", "TYSOR_CUDA_GEMM_STACK_B", "TYSOR_CUDA_GEMM_PERSISTENT"])
+def test_gemm_form_opt_outs(switch):
+    """Each opt-out (A's low part from a split pass instead of shared memory;
+    B's parts in three MMAs instead of stacked; the non-persistent pair
+    kernel) against the oracle on N > 128 and N <= 128 shapes, in a child
+    process because the switches are read at load time."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import sys, numpy as np
+sys.path[:0] = [".", "oracle"]
+import local as L
+from tysor_b200 import native
+from tysor_b200.runtime import CudaContext, DeviceBuffer
+ctx = CudaContext(0)
+lib = native.lib()
+rng = np.random.default_rng(5)
+for (m, n, k, ta, tb) in [(1024, 512, 256, False, True), (768, 128, 320, True, False), (512, 72, 96, False, False)]:
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    A = DeviceBuffer.from_array(ctx, np.ascontiguousarray(a.T) if ta else a)
+    B = DeviceBuffer.from_array(ctx, np.ascontiguousarray(b.T) if tb else b)
+    C = DeviceBuffer.zeros(ctx, m * n)
+    native.check(lib.tysor_cuda_dispatch_matmul_ex(ctx.handle, 1, m, n, k, A.handle, ta, m if ta else k, 0,
+                 B.handle, tb, k if tb else n, 0, C.handle, n, 0, None, 1.0, False, False))
+    got = C.read().reshape(m, n).astype(np.float64)
+    want = L.matmul(L.Tensor([m, k], a.reshape(-1).copy()), L.Tensor([k, n], b.reshape(-1).copy())).data.reshape(m, n)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err < 1e-5, (m, n, k, ta, tb, err)
+print("ok")
+'''
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, **{switch: "0"})
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
