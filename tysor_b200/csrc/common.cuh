@@ -76,6 +76,12 @@ struct GemmEpilogue {
   // 2 contract only k < end of the tile's rows; 3 only k >= start of the
   // tile's rows; 4 only k >= start of the tile's columns.
   int tri = 0;
+  // Non-null: the GEMM is the probability gradient dP of a causal
+  // Softmax(causal_mask(.)) and writes, instead of dP, the mask input's
+  // gradient dS = (p * (1 - p)) * dP (the reference's diagonal softmax
+  // backward), 0 where col > row; `smx_p` holds p in C's layout.  Only
+  // where gemm_fuses_softmax_backward holds.
+  const float* smx_p = nullptr;
 };
 
 enum GemmMode : int {
@@ -109,6 +115,12 @@ int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mod
 // strides) on the kernel form that makes A's low part in shared memory:
 // its scratch then needs no a_lo (only b_lo).
 bool gemm_converts_a(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c);
+
+// Whether gemm_launch computes GemmEpilogue::smx_p's softmax backward in the
+// GEMM's epilogue for this shape and operand layout (ta / tb as in
+// GemmOperand::trans).
+bool gemm_fuses_softmax_backward(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
+                                 int64_t ldc, int64_t stride_c);
 
 // Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
 extern bool g_two_sm_enabled;

@@ -554,7 +554,7 @@ struct Executor {
   void gemm_step(StepList& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
                  Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu,
-                 int tri = 0) {
+                 int tri = 0, Slot* smx_p = nullptr) {
     Prepared pa, pb;
     pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
     pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
@@ -577,6 +577,7 @@ struct Executor {
       GemmOperand B{pb.hi->p, pb.trans, pb.ld, pb.bs};
       GemmOutput O{c->p, ldc, sc};
       GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0, tri};
+      ep.smx_p = smx_p ? smx_p->p : nullptr;
       GemmScratch s{nullptr, nullptr, 0, 0, 1};
       if (pa.lo) {
         s.a_lo = pa.lo->p;
@@ -1340,6 +1341,30 @@ struct Executor {
   }
   // d(lhs) of lhs.rhs: g . rhs^T ; d(rhs): lhs^T . g  (layers.rs:521-527)
   // `alpha` scales the incoming gradient (a folded scale-by-constant).
+  // P . V where P = Softmax(causal_mask(s)) is read by nothing else: the
+  // GEMM for dP = g . V^T writes the diagonal softmax backward's result dS
+  // straight into s's gradient (its epilogue reads P), so dP is never
+  // stored and the Softmax node has no gradient left to propagate.  False
+  // when the shapes or layouts do not allow it.
+  bool fuse_softmax_backward(const GNode& mm, Slot* g, const HVal& l, const HVal& r, float alpha) {
+    const int pid = mm.inputs[0], vid = mm.inputs[1];
+    const GNode* only = sole_consumer(pid);
+    if (!only || only->output != mm.output || folded_transpose.count(vid) || folded_transpose.count(pid)) return false;
+    const GNode* sm = producer_node(pid);
+    if (!sm || sm->kind != kNApply || sm->inputs.size() < 2) return false;
+    auto mi = masked_input.find(sm->inputs[1]);
+    if (mi == masked_input.end() || vgrad.count(mi->second) || !l.slot || !r.slot) return false;
+    const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
+    std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
+    const int batch = (int)numel(lead);
+    if (!tma_aligned(n, m * n, batch) || !tma_aligned(n, k * n, batch)) return false;
+    if (!gemm_fuses_softmax_backward(batch, m, k, n, false, true, plan_matmul_mode, k, m * k)) return false;
+    auto [d, acc] = contrib(mi->second);
+    gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr, alpha, acc,
+              false, 1, l.slot);
+    return true;
+  }
+
   void emit_matmul_grads(Slot* g, const HVal& l, const HVal& r, int lid, int rid, bool want_l,
                          bool want_r, float alpha = 1.0f, int tri_l = 0, int tri_r = 0) {
     const int64_t m = l.shape[l.shape.size() - 2], k = l.shape.back(), n = r.shape.back();
@@ -1499,7 +1524,9 @@ struct Executor {
               tri_l = 1;
               tri_r = 3;
             }
-            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], true, true, galpha, tri_l, tri_r);
+            bool want_l = true;
+            if (tri_l == 1 && fuse_softmax_backward(node, g, l, r, galpha)) want_l = false;
+            emit_matmul_grads(g, l, r, node.inputs[0], node.inputs[1], want_l, true, galpha, tri_l, tri_r);
           } else if (node.op == "relu") {
             auto [d, acc] = contrib(node.inputs[0]);
             Slot* y = out.slot;

@@ -813,7 +813,7 @@ struct PipeCfgP {
   static constexpr int kEpiBytes = kAccWarps * 2 * 4096;  // two 32x32 boxes per accumulator warp
   static constexpr int kStagesRaw = (160 * 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
-  static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024 + 256;
+  static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024 + 512;
 };
 
 // Tile t of the persistent schedule: batch item, this CTA's first row, the
@@ -855,14 +855,18 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   return true;
 }
 
-template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB>
+template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB, bool kSmx>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>(), 1)
     gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_alo,
                         const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_blo,
-                        const __grid_constant__ CUtensorMap map_c32, GemmEpilogue ep, int M, int N, int K,
+                        const __grid_constant__ CUtensorMap map_c32,
+                        const __grid_constant__ CUtensorMap map_y, GemmEpilogue ep, int M, int N, int K,
                         int batch, int splits, int* err) {
+  // kSmx: map_y addresses the probabilities p (C's geometry); each
+  // accumulator warp loads its boxes of p with TMA into its epilogue boxes
+  // and rewrites them in place as dS = (p * (1 - p)) * dP before storing.
   // splits > 1: map_c32 addresses the split-K workspace ([splits * batch][M]
   // [N] raw sums); alpha, bias, relu and accumulate are left to the
   // reduction that sums the parts.
@@ -873,7 +877,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   constexpr int kStageBytes = Cfg::kStageBytes;
   static_assert(!kConvA || kStrict, "A's low part is only used in strict mode");
   static_assert(!kStackB || (kStrict && BN == 128), "stacked B is the strict N <= 128 form");
-  static_assert(!kConvA || (4 * kStages + 4) * 8 + 4 <= 256, "barriers exceed their reserve");
+  static_assert(((kConvA ? 4 : 2) * kStages + 4 + 2 * kAccWarps) * 8 + 4 <= 512, "barriers exceed their reserve");
   static_assert(kA % (16 * 64) == 0, "converter warps cover the A tile in float4 rounds");
   // Both CTAs' loads on the even CTA's "full" barrier (with kConvA: B only).
   constexpr uint32_t kATx = kConvA ? 0 : (kStrict ? 2 * kA : kA);
@@ -898,7 +902,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   uint64_t* tempty_bar = bars + 2 * kStages + 2;
   uint64_t* afull_bar = bars + 2 * kStages + 4;  // kConvA: this CTA's A tile landed
   uint64_t* conv_bar = bars + 3 * kStages + 4;   // kConvA: both CTAs' low parts written
-  uint32_t* tmem_slot = (uint32_t*)(bars + (kConvA ? 4 * kStages + 4 : 2 * kStages + 4));
+  uint64_t* ybar = bars + (kConvA ? 4 * kStages + 4 : 2 * kStages + 4);  // kSmx: two per accumulator warp
+  uint32_t* tmem_slot = (uint32_t*)(ybar + 2 * kAccWarps);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -928,6 +933,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         mbar_init(smem_u32(&conv_bar[s]), 4);  // two converter warps in each CTA
       }
     }
+    if (kSmx)
+      for (int b = 0; b < 2 * kAccWarps; ++b) mbar_init(smem_u32(&ybar[b]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -1094,12 +1101,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t ebox0 = smem_u32(epi) + (uint32_t)(warp - 2) * 8192u;
+    const bool smx = kSmx && splits == 1;
+    constexpr int kBoxes = kHalf / 32;  // output boxes per warp per tile
+    const uint32_t ybar0 = smem_u32(&ybar[2 * (warp - 2)]);
+    uint32_t yph = 0;   // phase bit of each of this warp's two probability barriers
+    int y_pending = 0;  // probability boxes loading and not yet waited for
     uint32_t ch = 0;
     bool have = true;
     for (int t = cluster; t < total && have; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
       if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
         continue;
+      if (smx) {
+        // The tile's first two probability boxes load while the tensor core
+        // finishes the tile (once this warp's earlier stores have read the
+        // boxes out).
+        if (lane == 0) {
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+#pragma unroll
+          for (int b = 0; b < 2 && b < kBoxes; ++b) {
+            mbar_expect_tx(ybar0 + 8u * b, 4096u);
+            tma_load_3d(ebox0 + (uint32_t)b * 4096u, &map_y, ybar0 + 8u * b, n0 + half * kHalf + 32 * b,
+                        m0 + quad * 32, bz);
+          }
+        }
+        y_pending += kBoxes < 2 ? kBoxes : 2;
+      }
       const int nch = (kb1 - kb0 + kChunkKb - 1) / kChunkKb;
       float acc[kHalf];
 #pragma unroll
@@ -1145,24 +1172,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
       const int zc = splits == 1 ? bz : ks * batch + bz;  // output (or workspace) batch index
       const int red = splits == 1 ? ep.accumulate : 0;
 #pragma unroll
-      for (int b = 0; b < kHalf / 32; ++b) {
+      for (int b = 0; b < kBoxes; ++b) {
         const uint32_t box = ebox0 + (uint32_t)(b & 1) * 4096u;
-        // The box is reused two stores later: wait until at most one store
-        // is still reading this warp's boxes.
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        __syncwarp();
+        if (smx) {
+          // dS in place of the probability box (the output's swizzled
+          // positions), 0 where the column exceeds the row.
+          have = mbar_wait(ybar0 + 8u * (b & 1), (yph >> (b & 1)) & 1u, err);
+          if (!have) break;
+          yph ^= 1u << (b & 1);
+          --y_pending;
+          const int row = m0 + quad * 32 + lane;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_shared_f4(box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4), acc[b * 32 + 4 * j],
-                       acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t a = box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4);
+            const float4 p = ld_shared_f4(a);
+            const int c = col0 + 32 * b + 4 * j;
+            const float* v = &acc[b * 32 + 4 * j];
+            st_shared_f4(a, c > row ? 0.0f : (p.x * (1.0f - p.x)) * v[0],
+                         c + 1 > row ? 0.0f : (p.y * (1.0f - p.y)) * v[1],
+                         c + 2 > row ? 0.0f : (p.z * (1.0f - p.z)) * v[2],
+                         c + 3 > row ? 0.0f : (p.w * (1.0f - p.w)) * v[3]);
+          }
+        } else {
+          // The box is reused two stores later: wait until at most one store
+          // is still reading this warp's boxes.
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_shared_f4(box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4), acc[b * 32 + 4 * j],
+                         acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
           if (col0 + 32 * b < N) tma_store_3d(&map_c32, box, col0 + 32 * b, m0 + quad * 32, zc, red);
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          if (smx && b + 2 < kBoxes) {
+            // This box's next probabilities, once the store has read it.
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            mbar_expect_tx(ybar0 + 8u * (b & 1), 4096u);
+            tma_load_3d(box, &map_y, ybar0 + 8u * (b & 1), col0 + 32 * (b + 2), m0 + quad * 32, bz);
+          }
         }
+        if (smx && b + 2 < kBoxes) ++y_pending;
       }
     }
+    // After a timed-out wait, probability loads may still be in flight:
+    // give each a bounded wait before the shared memory is released.
+    for (int b = 0; b < 2 && y_pending > 0; ++b)
+      if (mbar_wait(ybar0 + 8u * b, (yph >> b) & 1u, err)) --y_pending;
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   __syncwarp();
@@ -1428,12 +1487,12 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK>
+template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK, bool SMX = false>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
-               const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M, int N, int K, int splits,
-               int* d_err, cudaStream_t st) {
+               const CUtensorMap& mc32, const CUtensorMap& my, const GemmEpilogue& ep, int batch, int M, int N, int K,
+               int splits, int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfgP<BN, S, STACK>::kSmem;
-  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK>;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK, SMX>;
   static bool configured = false;
   if (!configured) {
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1444,22 +1503,22 @@ void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap
   int64_t clusters = sm_count() / 2;
   if (clusters > tiles) clusters = tiles;
   if (clusters < 1) clusters = 1;
-  kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), pp_threads<CONV>(), smem, st>>>(ma, malo, mb, mblo, mc32, ep, M,
-                                                                                  N, K, batch, splits, d_err);
+  kern<<<dim3((unsigned)(2 * clusters), 1u, 1u), pp_threads<CONV>(), smem, st>>>(ma, malo, mb, mblo, mc32, my, ep,
+                                                                                  M, N, K, batch, splits, d_err);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 template <int BN, bool S, bool CONV = false, bool STACK = false>
 void dispatch_pp(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb,
-                 const CUtensorMap& mblo, const CUtensorMap& mc32, const GemmEpilogue& ep, int batch, int M,
-                 int N, int K, int splits, int* d_err, cudaStream_t st) {
+                 const CUtensorMap& mblo, const CUtensorMap& mc32, const CUtensorMap& my, const GemmEpilogue& ep,
+                 int batch, int M, int N, int K, int splits, int* d_err, cudaStream_t st) {
   if (amn) {
-    if (bmn) launch_pp<BN, S, true, true, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, true, false, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, true, true, CONV, STACK>(ma, malo, mb, mblo, mc32, my, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, true, false, CONV, STACK>(ma, malo, mb, mblo, mc32, my, ep, batch, M, N, K, splits, d_err, st);
   } else {
-    if (bmn) launch_pp<BN, S, false, true, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
-    else launch_pp<BN, S, false, false, CONV, STACK>(ma, malo, mb, mblo, mc32, ep, batch, M, N, K, splits, d_err, st);
+    if (bmn) launch_pp<BN, S, false, true, CONV, STACK>(ma, malo, mb, mblo, mc32, my, ep, batch, M, N, K, splits, d_err, st);
+    else launch_pp<BN, S, false, false, CONV, STACK>(ma, malo, mb, mblo, mc32, my, ep, batch, M, N, K, splits, d_err, st);
   }
 }
 
@@ -1596,9 +1655,34 @@ void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOpe
   *b_elems = B.trans ? operand_span(B, batch, N, K) : operand_span(B, batch, K, N);
 }
 
+bool gemm_fuses_softmax_backward(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
+                                 int64_t ldc, int64_t stride_c) {
+  return mode == kGemmStrict && K > 0 && !ta && tb && N > 128 && g_two_sm_enabled && g_persistent_enabled &&
+         g_conv_a_enabled && M >= 256 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) &&
+         M <= INT32_MAX / 2 && N <= INT32_MAX / 2 && K <= INT32_MAX / 2;
+}
+
+int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
+                     const GemmOutput& C, const GemmEpilogue& ep, int mode, const GemmScratch& scratch, int* d_err,
+                     cudaStream_t st, bool* fused_smx);
+
 int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
                 const GemmOperand& B, const GemmOutput& C, const GemmEpilogue& ep, int mode,
                 const GemmScratch& scratch, int* d_err, cudaStream_t st) {
+  if (ep.smx_p && (ep.accumulate || ep.bias || ep.relu))
+    throw CudaError("the fused softmax backward epilogue takes no accumulate, bias or relu");
+  bool fused = false;
+  const int r = gemm_launch_impl(batch, M, N, K, A, B, C, ep, mode, scratch, d_err, st, &fused);
+  // Callers ask for the fused epilogue only where gemm_fuses_softmax_backward
+  // holds; another kernel form would have written dP, not dS.
+  if (ep.smx_p && !fused && M > 0 && N > 0 && batch > 0)
+    throw CudaError("fused softmax backward requested for a GEMM form without it");
+  return r;
+}
+
+int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
+                     const GemmOutput& C, const GemmEpilogue& ep, int mode, const GemmScratch& scratch, int* d_err,
+                     cudaStream_t st, bool* fused_smx) {
   if (M <= 0 || N <= 0 || batch <= 0) return 0;
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
     throw CudaError("matmul dimension too large");
@@ -1667,20 +1751,28 @@ int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A
     const CUtensorMap mc32 =
         splits > 1 ? make_map(scratch.ws, N, M, (uint64_t)splits * batch, ldw, M * ldw, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)
                    : make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    // The probabilities of a fused softmax backward, in C's layout.
+    const CUtensorMap my =
+        ep.smx_p ? make_map(ep.smx_p, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) : mc32;
     const int im = (int)M, in = (int)N, ik = (int)K;
     if (BN == 128) {
       const bool stack_b = strict && g_stack_b_enabled;
       if (conv_a && stack_b)
-        dispatch_pp<128, true, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
-      else if (conv_a) dispatch_pp<128, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+        dispatch_pp<128, true, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+      else if (conv_a) dispatch_pp<128, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
       else if (stack_b)
-        dispatch_pp<128, true, false, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
-      else if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
-      else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+        dispatch_pp<128, true, false, true>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+      else if (strict) dispatch_pp<128, true>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+      else dispatch_pp<128, false>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+    } else if (ep.smx_p && conv_a && !amn && !bmn && splits == 1) {
+      // The probability gradient of a causal softmax, written as dS.
+      launch_pp<256, true, false, false, true, false, true>(ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits,
+                                                            d_err, st);
+      *fused_smx = true;
     } else {
-      if (conv_a) dispatch_pp<256, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
-      else if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
-      else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, ep, batch, im, in, ik, splits, d_err, st);
+      if (conv_a) dispatch_pp<256, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+      else if (strict) dispatch_pp<256, true>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
+      else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
     }
     if (splits > 1) {
       splitk_reduce_kernel<<<elementwise_blocks((int64_t)batch * M * N, 256), 256, 0, st>>>(scratch.ws, splits, batch, im,
