@@ -150,6 +150,8 @@ struct Executor {
   std::vector<std::string> param_order;
   Slot* loss = nullptr;           // one float per step
   Slot* grad_block = nullptr;     // all parameter gradients + loss, contiguous
+  Slot* param_block = nullptr;    // the trained parameters, laid out like their gradients
+  size_t param_block_n = 0;       // floats of param_block (its padding included)
   size_t scratch_floats = 0;
   Slot* scratch = nullptr;
   void* arena = nullptr;
@@ -275,7 +277,8 @@ struct Executor {
     causal_probs.clear();
     folded_transpose.clear();
     grad_alias.clear();
-    loss = grad_block = scratch = nullptr;
+    loss = grad_block = scratch = param_block = nullptr;
+    param_block_n = 0;
     scratch_floats = 0;
     setup_done = false;
     stepped = false;
@@ -1311,7 +1314,22 @@ struct Executor {
     return {p.grad, acc};
   }
 
+  // In training a node's output gradient is dead once the node is done, so
+  // one input whose gradient it would merely copy (a view's input, one
+  // operand of '+' or '-') can take the buffer itself: later contributions
+  // add into it as they would into the copy.  One input per node at most
+  // (two sharing it would see each other's additions); the other copies
+  // run first, being emitted first.
+  Slot* given_g = nullptr;  // the node's gradient buffer, once handed to an input
+  bool give_gradient(Slot* g, int vid) {
+    if (mode != kModeTrain || vgrad.count(vid) || given_g == g) return false;
+    vgrad[vid] = g;
+    given_g = g;
+    return true;
+  }
+
   void emit_copy(Slot* g, int vid, int64_t n) {
+    if (give_gradient(g, vid)) return;
     auto [d, acc] = contrib(vid);
     backward.push_back([=](cudaStream_t st) {
       if (acc) launch_add_inplace(d->p, g->p, n, st);
@@ -1432,6 +1450,7 @@ struct Executor {
     for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
       const GNode& node = *it;
       cur_label = "bwd " + node_label(node);
+      given_g = nullptr;
       Slot* g = nullptr;
       float galpha = 1.0f;
       auto gi = vgrad.find(node.output);
@@ -1768,6 +1787,18 @@ struct Executor {
       (void)st;
       if (allreduce && (*gb)->n > 0) comm_allreduce(cx, (*gb)->p, (*gb)->n);
     });
+    // One SGD pass over all parameters when they sit in one block laid out
+    // like the gradient block (each element's update is the same p - lr * g;
+    // the order the reference visits them in does not change any value).
+    if (params_in_block()) {
+      Slot **pb = &param_block, **gbl = &grad_block;
+      size_t* pn = &param_block_n;
+      float* lr_ptr = &lr_f;
+      update.push_back([=](cudaStream_t st) {
+        if (*pn > 0) launch_sgd((*pb)->p, (*gbl)->p, *lr_ptr, (int64_t)*pn, st);
+      });
+      return;
+    }
     std::vector<std::string> names(param_order);
     std::sort(names.begin(), names.end());  // BTreeMap order (executor.rs:750)
     for (const std::string& name : names) {
@@ -1780,6 +1811,18 @@ struct Executor {
     }
   }
   float lr_f = 0.01f;
+
+  // Whether every trained parameter owns its value buffer (not a view) of
+  // its gradient's size, so the values can form one block.
+  bool params_in_block() const {
+    std::set<const Slot*> seen;
+    for (const std::string& name : param_order) {
+      const Param& p = params.at(name);
+      if (!p.grad) continue;
+      if (!p.value || p.value->base || p.value->n != p.grad->n || !seen.insert(p.value).second) return false;
+    }
+    return true;
+  }
 
   // ---- arena layout --------------------------------------------------------------------
   void layout() {
@@ -1809,6 +1852,17 @@ struct Executor {
       total += (s->n + 63) & ~(size_t)63;
     }
     const size_t gb_end = total;
+    // then the trained parameters, in the same order and padding
+    const bool pblock = mode == kModeTrain && params_in_block();
+    if (pblock) {
+      for (const std::string& name : param_order) {
+        Param& p = params.at(name);
+        if (!p.grad) continue;
+        off[p.value] = total;
+        total += (p.value->n + 63) & ~(size_t)63;
+      }
+    }
+    const size_t pb_end = total;
     for (Slot& s : slots) {
       if (s.base || off.count(&s)) continue;
       off[&s] = total;
@@ -1826,6 +1880,11 @@ struct Executor {
     if (mode == kModeTrain) {
       slots.push_back(Slot{gb_end - gb_start, nullptr, 0, basep + gb_start});
       grad_block = &slots.back();
+      if (pblock) {
+        slots.push_back(Slot{pb_end - gb_end, nullptr, 0, basep + gb_end});
+        param_block = &slots.back();
+        param_block_n = pb_end - gb_end;
+      }
     }
   }
 
