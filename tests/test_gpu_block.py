@@ -152,11 +152,13 @@ def test_traced_step_reports_every_item_and_matches_a_plain_step(cuda_ctx):
     ex.close()
 
 
-def test_fused_causal_attention_refuses_rows_whose_masked_entries_keep_probability(cuda_ctx):
+@pytest.mark.parametrize("seq", [256, 1024, 2048])
+def test_fused_causal_attention_refuses_rows_whose_masked_entries_keep_probability(cuda_ctx, seq):
     """The causal GEMM skipping treats masked probabilities as exact zeros,
     which holds unless a row's scores are all below about -9896 (then
     exp(-1e4 - max) is not zero).  Such inputs are reported as an error, not
-    computed wrongly."""
+    computed wrongly (one block per row at 256; one or two warps per row at
+    1024 and 2048)."""
     from tysor_b200 import native
     from tysor_b200.graph import GraphBuilder
     from tysor_b200.runtime import CudaGraphExecutor
@@ -167,7 +169,7 @@ def test_fused_causal_attention_refuses_rows_whose_masked_entries_keep_probabili
     b.ret(b.let("out", b.call("matmul", p, v)))
     b.train(objective="out", lr=0.0)
     g = b.build()
-    shape = [1, 1, 256, 32]
+    shape = [1, 1, seq, 32]
     ins = {"q": np.full(shape, -100.0, np.float32), "k": np.full(shape, 100.0, np.float32),
            "v": np.ones(shape, np.float32)}
     ex = CudaGraphExecutor(cuda_ctx, g, {n: shape for n in ins}, inputs=ins)
