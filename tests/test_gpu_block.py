@@ -206,3 +206,34 @@ def test_weight_gradients_with_split_k(cuda_ctx):
     for name, gt in grads.items():
         assert frob(ex.parameter_grad(name), gt.data) < 1e-5, name
     ex.close()
+
+
+def test_gradient_buffers_handed_to_inputs(cuda_ctx):
+    """Training hands a node's gradient buffer to one input instead of
+    copying it (a view's input, one operand of '+' or '-'); later
+    contributions then add into that buffer.  A graph where the same value
+    reaches the objective through a view, both operands of '+', and '-':
+    parameter gradients and updated parameters against the oracle."""
+    from tysor_b200.graph import GraphBuilder
+    from tysor_b200.runtime import CudaGraphExecutor
+    b = GraphBuilder()
+    x = b.param("x")
+    l1 = b.let("l1", b.ctor("linear", 64, 64, False))
+    a = b.let("a", b.apply(l1, x))
+    v = b.call("reshape", b.call("reshape", a, 8, 16, 64), 128, 64)
+    c = b.binary("+", a, v)
+    d = b.binary("-", c, b.binary("+", a, a))
+    e = b.binary("+", d, c)
+    b.ret(b.let("loss", b.binary("*", e, e)))
+    b.train(objective="loss", lr=1e-3, iterations=1)
+    g = b.build()
+    shapes = {"x": [128, 64]}
+    xv = np.random.default_rng(4).standard_normal((128, 64)).astype(np.float32)
+    params = params_for(g, seed=6)
+    oparams = {k: L.Tensor(list(p.shape), p.reshape(-1).copy()) for k, p in params.items()}
+    _, grads, _ = L.train_step_grads(g, shapes, inputs={"x": xv}, parameters=oparams)
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs={"x": xv}, parameters=params)
+    ex.train(1, 0.0)
+    for name, gt in grads.items():
+        assert frob(ex.parameter_grad(name), gt.data) < 1e-5, name
+    ex.close()
