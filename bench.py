@@ -465,7 +465,9 @@ def run_ours(args, rank, world, local_rank, dist):
     # pinned host memory (queued one step ahead on the library's copy stream,
     # as a data loader prefetches, so the copy overlaps the previous step),
     # then the step runs and its loss is read back.
-    e2e_steps = max(5, args.steps)
+    # At least 20 steps: the first step's copy, which nothing overlaps, is one
+    # of many, as in a training run.
+    e2e_steps = max(20, args.steps)
     e2e_sampler = ClockSampler(gpu_index_for(local_rank)) if rank == 0 else None
     if e2e_sampler:
         e2e_sampler.start()
