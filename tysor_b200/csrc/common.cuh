@@ -82,6 +82,9 @@ struct GemmEpilogue {
   // backward), 0 where col > row; `smx_p` holds p in C's layout.  Only
   // where gemm_fuses_softmax_backward holds.
   const float* smx_p = nullptr;
+  // Non-null: C = residual + the result (residual in C's layout; a residual
+  // connection around a linear).  Only where gemm_fuses_box_epilogue holds.
+  const float* residual = nullptr;
 };
 
 enum GemmMode : int {
@@ -116,11 +119,11 @@ int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mod
 // its scratch then needs no a_lo (only b_lo).
 bool gemm_converts_a(int batch, int64_t M, int64_t N, int64_t K, int mode, int64_t ldc, int64_t stride_c);
 
-// Whether gemm_launch computes GemmEpilogue::smx_p's softmax backward in the
-// GEMM's epilogue for this shape and operand layout (ta / tb as in
-// GemmOperand::trans).
-bool gemm_fuses_softmax_backward(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
-                                 int64_t ldc, int64_t stride_c);
+// Whether gemm_launch can run GemmEpilogue::smx_p's softmax backward or
+// GemmEpilogue::residual's addition in the GEMM's epilogue for this shape
+// and operand layout (ta / tb as in GemmOperand::trans).
+bool gemm_fuses_box_epilogue(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
+                             int64_t ldc, int64_t stride_c);
 
 // Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
 extern bool g_two_sm_enabled;

@@ -272,6 +272,8 @@ struct Executor {
     folded_scale.clear();
     masked_input.clear();
     fused_silu.clear();
+    residual_sum.clear();
+    residual_lin.clear();
     seqmajor_transpose.clear();
     causal_scores.clear();
     causal_probs.clear();
@@ -557,7 +559,7 @@ struct Executor {
   void gemm_step(StepList& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
                  Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu,
-                 int tri = 0, Slot* smx_p = nullptr) {
+                 int tri = 0, Slot* smx_p = nullptr, Slot* residual = nullptr) {
     Prepared pa, pb;
     pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
     pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
@@ -570,9 +572,14 @@ struct Executor {
     }
     Context* cx = ctx;
     const int mode_now = plan_matmul_mode;
+    // A residual is added in the GEMM's epilogue where the kernel form has
+    // it (operand layouts as prepared); otherwise by a kernel after it.
+    const bool res_in_gemm = residual && !acc && tc &&
+                             gemm_fuses_box_epilogue(batch, M, N, K, pa.trans, pb.trans, mode_now, ldc, sc);
     // Split-K workspace (the shared scratch slot) for GEMMs whose output
     // tiles cannot fill the GPU.
-    const int64_t ws_elems = tc && tri == 0 ? gemm_splitk_ws_elems(batch, M, N, K, mode_now, ldc, sc) : 0;
+    const int64_t ws_elems =
+        tc && tri == 0 && !res_in_gemm ? gemm_splitk_ws_elems(batch, M, N, K, mode_now, ldc, sc) : 0;
     if (ws_elems > 0) need_scratch((size_t)ws_elems);
     Slot** scr = &scratch;
     out.push_back([=](cudaStream_t st) {
@@ -581,6 +588,7 @@ struct Executor {
       GemmOutput O{c->p, ldc, sc};
       GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0, tri};
       ep.smx_p = smx_p ? smx_p->p : nullptr;
+      if (res_in_gemm) ep.residual = residual->p;
       GemmScratch s{nullptr, nullptr, 0, 0, 1};
       if (pa.lo) {
         s.a_lo = pa.lo->p;
@@ -595,6 +603,10 @@ struct Executor {
         s.ws_elems = ws_elems;
       }
       gemm_launch(batch, M, N, K, A, B, O, ep, mode_now, s, cx->d_err, st);
+      if (residual && !res_in_gemm) {
+        if (acc || ldc != N || (batch > 1 && sc != M * N)) throw CudaError("residual GEMM needs a fresh contiguous output");
+        launch_binary_tt(kAdd, residual->p, c->p, c->p, (int64_t)batch * M * N, st);
+      }
     });
   }
 
@@ -768,6 +780,7 @@ struct Executor {
 
   HVal plan_binary(const GNode& node) {
     if (folded_scale.count(node.output)) return plan_folded_scale(node);
+    if (auto rs = residual_sum.find(node.output); rs != residual_sum.end()) return rs->second;
     for (int side = 0; side < 2; ++side) {
       auto fs = fused_silu.find(node.inputs[side]);
       if (fs == fused_silu.end()) continue;
@@ -833,6 +846,8 @@ struct Executor {
   std::map<int, int> folded_scale;          // scale node out -> matmul out
   std::map<int, int> masked_input;          // causal_mask out -> its input
   std::map<int, int> fused_silu;            // SiLU out -> its input, computed inside the '*' reading it
+  std::map<int, HVal> residual_sum;         // '+' out -> its value, written by the linear it adds
+  std::set<int> residual_lin;               // linear outputs added to a residual inside their GEMM
   std::map<int, int> seqmajor_transpose;    // transpose(1, 2) out -> its input, read in place by rope / repeat_kv
   // Fused causal attention: score matmuls (output ids) whose scaled output
   // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
@@ -870,6 +885,21 @@ struct Executor {
     if (fused_silu.count(other)) return false;  // one fused operand per product
     const GNode* xp = sole_consumer(node.inputs.at(1));
     return xp && xp->output == node.output;
+  }
+
+  // The other operand of the '+' that is the sole consumer of linear node
+  // `node`'s [m, n] output, if that operand is a planned [m, n] tensor
+  // (train and run modes); -1 otherwise.
+  int residual_operand(const GNode& node, int64_t m, int64_t n) const {
+    if (mode == kModeBackward) return -1;
+    const GNode* c = sole_consumer(node.output);
+    if (!c || c->kind != kNBinary || c->binop != '+' || c->inputs.size() != 2 || c->inputs[0] == c->inputs[1])
+      return -1;
+    const int other = c->inputs[0] == node.output ? c->inputs[1] : c->inputs[0];
+    if (other < 0 || other >= (int)hv.size()) return -1;
+    const HVal& ov = hv[other];
+    if (ov.t != HVal::Tensor || !ov.slot || ov.shape != std::vector<int64_t>{m, n}) return -1;
+    return other;
   }
 
   // Gives a fused SiLU output its own buffer after all (its '*' turned out
@@ -1211,6 +1241,21 @@ struct Executor {
           else b = const_pattern({cl.out_features}, 1);
         }
         const int64_t m = x.shape[0], n = cl.out_features;
+        // A residual connection x + linear(.) (or linear(.) + x) whose other
+        // operand already exists: the GEMM writes the sum (its epilogue adds
+        // the residual) and the linear's own output is never stored.
+        const int res = residual_operand(node, m, n);
+        if (res >= 0) {
+          HVal sum = new_tensor({m, n});
+          gemm_step(forward, 1, m, n, in_f, x.slot, false, in_f, 0, w, false, n, 0, sum.slot, n, 0, b, 1.0f,
+                    false, false, 0, nullptr, val(res).slot);
+          residual_sum[sole_consumer(node.output)->output] = sum;
+          residual_lin.insert(node.output);
+          HVal o;
+          o.t = HVal::Tensor;
+          o.shape = {m, n};
+          return o;
+        }
         HVal o = new_tensor({m, n});
         gemm_step(forward, 1, m, n, in_f, x.slot, false, in_f, 0, w, false, n, 0, o.slot, n, 0, b, 1.0f,
                   false, false);
@@ -1376,7 +1421,7 @@ struct Executor {
     std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
     const int batch = (int)numel(lead);
     if (!tma_aligned(n, m * n, batch) || !tma_aligned(n, k * n, batch)) return false;
-    if (!gemm_fuses_softmax_backward(batch, m, k, n, false, true, plan_matmul_mode, k, m * k)) return false;
+    if (!gemm_fuses_box_epilogue(batch, m, k, n, false, true, plan_matmul_mode, k, m * k)) return false;
     auto [d, acc] = contrib(mi->second);
     gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr, alpha, acc,
               false, 1, l.slot);
@@ -1936,7 +1981,7 @@ Slot* value_slot(Executor* e, int id, std::vector<int64_t>* shape) {
   const HVal& h = e->hv[id];
   if (h.t == HVal::Tensor && !h.slot &&
       (e->folded_transpose.count(id) || e->masked_input.count(id) || e->fused_silu.count(id) ||
-       e->seqmajor_transpose.count(id)))
+       e->seqmajor_transpose.count(id) || e->residual_lin.count(id)))
     throw CudaError("value " + std::to_string(id) + " is not materialised: it was fused into its consumer");
   if (h.t != HVal::Tensor || !h.slot) throw CudaError("value " + std::to_string(id) + " is not a tensor");
   if (shape) *shape = h.shape;

@@ -855,7 +855,7 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   return true;
 }
 
-template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB, bool kSmx>
+template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB, int kEpi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>(), 1)
     gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_alo,
@@ -864,9 +864,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
                         const __grid_constant__ CUtensorMap map_c32,
                         const __grid_constant__ CUtensorMap map_y, GemmEpilogue ep, int M, int N, int K,
                         int batch, int splits, int* err) {
-  // kSmx: map_y addresses the probabilities p (C's geometry); each
-  // accumulator warp loads its boxes of p with TMA into its epilogue boxes
-  // and rewrites them in place as dS = (p * (1 - p)) * dP before storing.
+  // kEpi != 0: map_y addresses a second tensor in C's geometry; each
+  // accumulator warp loads its boxes of it with TMA into its epilogue boxes
+  // and rewrites them in place before storing: kEpi 1, the probabilities p,
+  // as dS = (p * (1 - p)) * dP (0 above the diagonal); kEpi 2, a residual r,
+  // as r + result.
   // splits > 1: map_c32 addresses the split-K workspace ([splits * batch][M]
   // [N] raw sums); alpha, bias, relu and accumulate are left to the
   // reduction that sums the parts.
@@ -902,7 +904,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   uint64_t* tempty_bar = bars + 2 * kStages + 2;
   uint64_t* afull_bar = bars + 2 * kStages + 4;  // kConvA: this CTA's A tile landed
   uint64_t* conv_bar = bars + 3 * kStages + 4;   // kConvA: both CTAs' low parts written
-  uint64_t* ybar = bars + (kConvA ? 4 * kStages + 4 : 2 * kStages + 4);  // kSmx: two per accumulator warp
+  uint64_t* ybar = bars + (kConvA ? 4 * kStages + 4 : 2 * kStages + 4);  // kEpi: two per accumulator warp
   uint32_t* tmem_slot = (uint32_t*)(ybar + 2 * kAccWarps);
 
   const int tid = threadIdx.x;
@@ -933,7 +935,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         mbar_init(smem_u32(&conv_bar[s]), 4);  // two converter warps in each CTA
       }
     }
-    if (kSmx)
+    if (kEpi != 0)
       for (int b = 0; b < 2 * kAccWarps; ++b) mbar_init(smem_u32(&ybar[b]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1101,7 +1103,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t ebox0 = smem_u32(epi) + (uint32_t)(warp - 2) * 8192u;
-    const bool smx = kSmx && splits == 1;
+    const bool smx = kEpi != 0 && splits == 1;  // boxes of map_y are loaded
     constexpr int kBoxes = kHalf / 32;  // output boxes per warp per tile
     const uint32_t ybar0 = smem_u32(&ybar[2 * (warp - 2)]);
     uint32_t yph = 0;   // phase bit of each of this warp's two probability barriers
@@ -1188,10 +1190,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
             const float4 p = ld_shared_f4(a);
             const int c = col0 + 32 * b + 4 * j;
             const float* v = &acc[b * 32 + 4 * j];
-            st_shared_f4(a, c > row ? 0.0f : (p.x * (1.0f - p.x)) * v[0],
-                         c + 1 > row ? 0.0f : (p.y * (1.0f - p.y)) * v[1],
-                         c + 2 > row ? 0.0f : (p.z * (1.0f - p.z)) * v[2],
-                         c + 3 > row ? 0.0f : (p.w * (1.0f - p.w)) * v[3]);
+            if (kEpi == 1)
+              st_shared_f4(a, c > row ? 0.0f : (p.x * (1.0f - p.x)) * v[0],
+                           c + 1 > row ? 0.0f : (p.y * (1.0f - p.y)) * v[1],
+                           c + 2 > row ? 0.0f : (p.z * (1.0f - p.z)) * v[2],
+                           c + 3 > row ? 0.0f : (p.w * (1.0f - p.w)) * v[3]);
+            else
+              st_shared_f4(a, p.x + v[0], p.y + v[1], p.z + v[2], p.w + v[3]);
           }
         } else {
           // The box is reused two stores later: wait until at most one store
@@ -1487,12 +1492,12 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK, bool SMX = false>
+template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK, int EPI = 0>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
                const CUtensorMap& mc32, const CUtensorMap& my, const GemmEpilogue& ep, int batch, int M, int N, int K,
                int splits, int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfgP<BN, S, STACK>::kSmem;
-  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK, SMX>;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK, EPI>;
   static bool configured = false;
   if (!configured) {
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1655,8 +1660,8 @@ void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOpe
   *b_elems = B.trans ? operand_span(B, batch, N, K) : operand_span(B, batch, K, N);
 }
 
-bool gemm_fuses_softmax_backward(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
-                                 int64_t ldc, int64_t stride_c) {
+bool gemm_fuses_box_epilogue(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
+                             int64_t ldc, int64_t stride_c) {
   return mode == kGemmStrict && K > 0 && !ta && tb && N > 128 && g_two_sm_enabled && g_persistent_enabled &&
          g_conv_a_enabled && M >= 256 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) &&
          M <= INT32_MAX / 2 && N <= INT32_MAX / 2 && K <= INT32_MAX / 2;
@@ -1669,14 +1674,15 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
 int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
                 const GemmOperand& B, const GemmOutput& C, const GemmEpilogue& ep, int mode,
                 const GemmScratch& scratch, int* d_err, cudaStream_t st) {
-  if (ep.smx_p && (ep.accumulate || ep.bias || ep.relu))
-    throw CudaError("the fused softmax backward epilogue takes no accumulate, bias or relu");
+  if (ep.smx_p && (ep.accumulate || ep.bias || ep.relu || ep.residual))
+    throw CudaError("the fused softmax backward epilogue takes no accumulate, bias, relu or residual");
+  if (ep.residual && ep.accumulate) throw CudaError("a GEMM adds a residual or accumulates, not both");
   bool fused = false;
   const int r = gemm_launch_impl(batch, M, N, K, A, B, C, ep, mode, scratch, d_err, st, &fused);
   // Callers ask for the fused epilogue only where gemm_fuses_softmax_backward
   // holds; another kernel form would have written dP, not dS.
-  if (ep.smx_p && !fused && M > 0 && N > 0 && batch > 0)
-    throw CudaError("fused softmax backward requested for a GEMM form without it");
+  if ((ep.smx_p || ep.residual) && !fused && M > 0 && N > 0 && batch > 0)
+    throw CudaError("fused GEMM epilogue requested for a GEMM form without it");
   return r;
 }
 
@@ -1744,7 +1750,7 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
     // Split-K into the caller's workspace when it has one and it pays.
     int splits = 1;
     const int64_t ldw = (N + 3) & ~(int64_t)3;
-    if (ep.tri == 0 && scratch.ws != nullptr && (((uintptr_t)scratch.ws) & 15) == 0) {
+    if (ep.tri == 0 && !ep.residual && scratch.ws != nullptr && (((uintptr_t)scratch.ws) & 15) == 0) {
       splits = splitk_parts(batch, M, N, K);
       if ((int64_t)splits * batch * M * ldw > scratch.ws_elems) splits = 1;
     }
@@ -1752,8 +1758,9 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
         splits > 1 ? make_map(scratch.ws, N, M, (uint64_t)splits * batch, ldw, M * ldw, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B)
                    : make_map(C.ptr, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     // The probabilities of a fused softmax backward, in C's layout.
+    const float* yp = ep.smx_p ? ep.smx_p : ep.residual;
     const CUtensorMap my =
-        ep.smx_p ? make_map(ep.smx_p, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) : mc32;
+        yp ? make_map(yp, N, M, batch, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) : mc32;
     const int im = (int)M, in = (int)N, ik = (int)K;
     if (BN == 128) {
       const bool stack_b = strict && g_stack_b_enabled;
@@ -1768,6 +1775,11 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
       // The probability gradient of a causal softmax, written as dS.
       launch_pp<256, true, false, false, true, false, true>(ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits,
                                                             d_err, st);
+      *fused_smx = true;
+    } else if (ep.residual && conv_a && !amn && !bmn && splits == 1) {
+      // C = residual + the product (a residual connection around a linear).
+      launch_pp<256, true, false, false, true, false, 2>(ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits,
+                                                         d_err, st);
       *fused_smx = true;
     } else {
       if (conv_a) dispatch_pp<256, true, true>(amn, bmn, ma, ma, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
