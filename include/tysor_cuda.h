@@ -248,7 +248,10 @@ const char* tysor_cuda_graph_trace_label(void* graph, int item);
 int tysor_cuda_graph_value_rank(void* graph, int value_id);
 bool tysor_cuda_graph_value_shape(void* graph, int value_id, int64_t* dims);
 bool tysor_cuda_graph_read_value(void* graph, int value_id, float* out, size_t count);
-/* Gradient of a value after tysor_cuda_graph_backward (false if none). */
+/* Gradient of a value after tysor_cuda_graph_backward (false if none).
+ * After tysor_cuda_graph_train only graph parameters' gradients are
+ * defined: training hands an intermediate value's dead gradient buffer on
+ * to one of its inputs, which adds its own gradient into it. */
 bool tysor_cuda_graph_read_value_grad(void* graph, int value_id, float* out, size_t count);
 /* Trainable parameters after tysor_cuda_graph_train. */
 int tysor_cuda_graph_num_parameters(void* graph);
