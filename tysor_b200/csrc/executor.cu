@@ -1543,6 +1543,14 @@ struct Executor {
                   });
                   break;
                 }
+                if (li == ri && !vgrad.count(li)) {
+                  // x * x into a fresh gradient: both contributions in one pass.
+                  auto [d, acc] = contrib(li);
+                  (void)acc;
+                  Slot* xs = l.slot;
+                  backward.push_back([=](cudaStream_t st) { launch_square_backward(g->p, xs->p, d->p, n, st); });
+                  break;
+                }
                 emit_tt(kMul, g, r.slot, li, n);
                 emit_tt(kMul, g, l.slot, ri, n);
                 break;

@@ -185,6 +185,15 @@ __global__ void unary_kernel(const float* x, float* out, int64_t n, float p) {
   ew_run<1>(In<1>{{x}}, out, n, 0, [=](const float (&a)[1]) { return apply_unary(OP, a[0], p); });
 }
 
+// Gradient of x * x from g, as the '*' backward's two contributions give it
+// to a fresh buffer: t = g * x stored, then t added: t + t.
+__global__ void square_backward_kernel(const float* g, const float* x, float* out, int64_t n) {
+  ew_run<2>(In<2>{{g, x}}, out, n, 0, [=](const float (&v)[2]) {
+    const float t = v[0] * v[1];
+    return t + t;
+  });
+}
+
 __global__ void binary_tt_kernel(int op, const float* a, const float* b, float* out, int64_t n) {
   ew_run<2>(In<2>{{a, b}}, out, n, 0, [=](const float (&v)[2]) { return apply_binary(op, v[0], v[1]); });
 }
@@ -1466,6 +1475,12 @@ void launch_unary(int op, const float* x, float* out, int64_t n, float param, cu
     case kUnaryNeg: unary_kernel<kUnaryNeg><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
     default: unary_kernel<-1><<<blocks, kThreads, 0, st>>>(x, out, n, param); break;
   }
+  check_launch();
+}
+
+void launch_square_backward(const float* g, const float* x, float* out, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  square_backward_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(g, x, out, n);
   check_launch();
 }
 

@@ -23,6 +23,8 @@ void launch_pattern(float* out, int64_t n, int mod, float add, float div, cudaSt
 void launch_fill(float* out, int64_t n, float value, cudaStream_t st);
 
 void launch_unary(int op, const float* x, float* out, int64_t n, float param, cudaStream_t st);
+// out = t + t with t = g * x: the gradient of x * x into a fresh buffer.
+void launch_square_backward(const float* g, const float* x, float* out, int64_t n, cudaStream_t st);
 void launch_binary_tt(int op, const float* a, const float* b, float* out, int64_t n,
                       cudaStream_t st);
 void launch_binary_ts(int op, const float* a, float s, float* out, int64_t n, cudaStream_t st);
