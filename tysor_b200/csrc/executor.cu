@@ -102,7 +102,6 @@ struct StepList {
     labels.clear();
   }
   size_t size() const { return fns.size(); }
-  bool empty() const { return fns.empty(); }
   std::vector<StepFn>::const_iterator begin() const { return fns.begin(); }
   std::vector<StepFn>::const_iterator end() const { return fns.end(); }
 };

@@ -33,9 +33,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 16;  // fp32 elements of K per stage (64 bytes)
-constexpr int kThreads = 128;
 constexpr int kGroupM = 16;  // tile rows per raster group of the 1-SM kernel
-constexpr int kStages = 4;
 constexpr long long kWaitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -179,19 +177,6 @@ constexpr int kThreadsTC = 64 + 32 * kAccWarps;
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
 }
 
 // Causal attention GEMMs (GemmEpilogue::tri): for a tile of rows
