@@ -52,10 +52,10 @@ sys.path.insert(0, ROOT)
 D_MODEL, HEADS, KV_HEADS, FFN, VOCAB = 2048, 16, 4, 5632, 32000
 
 
-def _oracle():
+def _oracle(threads=None):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import local as L
-    L.set_threads(os.cpu_count() or 1)
+    L.set_threads(threads or os.cpu_count() or 1)
     return L
 
 
@@ -64,13 +64,19 @@ def _oracle_params(L, params):
             for k, v in params.items()}
 
 
-def _calibrate(L) -> float:
-    """GFLOP/s of the oracle's matmul on this host (one [512,2048]x[2048,2048])."""
-    a = L.Tensor([512, 2048], np.ones(512 * 2048, np.float32))
-    b = L.Tensor([2048, 2048], np.ones(2048 * 2048, np.float32))
+def cpu_sample(wl, units, threads):
+    """One fwd+bwd+SGD step of workload `wl` on a fixed sample of `units`
+    (tokens or rows) with the oracle on `threads` host threads; returns
+    the units, the seconds and a description of the sample."""
+    from tysor_b200.programs import random_parameters
+    L = _oracle(threads)
+    g, shapes, ins = wl.cpu_case(units)
+    params = _oracle_params(L, random_parameters(g, 1234))
     t0 = time.perf_counter()
-    L.matmul(a, b)
-    return 2 * 512 * 2048 * 2048 / (time.perf_counter() - t0) / 1e9
+    L.train(g, shapes, inputs=ins, parameters=params, iterations=1)
+    dt = time.perf_counter() - t0
+    return {"units": units, "seconds": dt, "threads": threads,
+            "sample": f"{wl.describe_sample(units)}, one fwd+bwd+SGD step on {threads} thread(s) ({dt:.1f} s)"}
 
 
 # ---- workloads ------------------------------------------------------------------------------
@@ -114,26 +120,19 @@ class Block:
                 "model": "llama_block", "global_batch": self.batch * world, "seq_len": self.seq,
                 "parallelism": f"dp{world}", "l2": self.l2}
 
-    def cpu_sample(self, budget):
-        """One fwd+bwd+SGD step of the block for one sequence, the longest of
-        2048/1024/512 tokens whose estimated oracle time fits the budget."""
-        from tysor_b200.programs import llama_block_flops, random_parameters
-        L = _oracle()
-        gflops = _calibrate(L)
-        seq = 512
-        for s in (2048, 1024):
-            if llama_block_flops(1, s, D_MODEL, HEADS, KV_HEADS, FFN) / (gflops * 1e9) <= budget:
-                seq = s
-                break
-        g = self.graph(1, batch=1, seq=seq)
-        params = _oracle_params(L, random_parameters(g, 1234))
-        ins = self.inputs(7, 1, tokens=seq)
-        t0 = time.perf_counter()
-        L.train(g, self.shapes(1, tokens=seq), inputs=ins, parameters=params, iterations=1)
-        dt = time.perf_counter() - t0
-        return {"units": seq, "seconds": dt,
-                "sample": f"1 sequence x {seq} tokens, one fwd+bwd+SGD step of the same block "
-                          f"({dt:.1f} s; oracle matmul calibrated at {gflops:.1f} GFLOP/s)"}
+    # Fixed CPU samples: one whole sequence on all host threads, and a
+    # 256-token sequence on one thread (the reference's `local` backend is
+    # single-threaded; 2048 tokens would take minutes there).
+    cpu_units, cpu_units_single = 2048, 256
+    cpu_extrapolation = ("tokens/s of one sequence stands for the 8-sequence step: every sequence of the block "
+                         "costs the same per token (sequences are independent)")
+
+    def cpu_case(self, tokens):
+        g = self.graph(1, batch=1, seq=tokens)
+        return g, self.shapes(1, tokens=tokens), self.inputs(7, 1, tokens=tokens)
+
+    def describe_sample(self, tokens):
+        return f"1 sequence x {tokens} tokens of the same block (d 2048, 16/4 heads, ffn 5632)"
 
 
 class Mlp:
@@ -185,20 +184,15 @@ class Mlp:
                 "model": "mlp", "global_batch": self.rows, "seq_len": 1, "parallelism": f"dp{world}",
                 "l2": self.l2}
 
-    def cpu_sample(self, budget):
-        from tysor_b200.programs import random_parameters
-        L = _oracle()
-        gflops = _calibrate(L)
-        per_row = 6 * 2 * self.d_in * self.d_hidden
-        rows = int(max(64, min(self.rows, budget * gflops * 1e9 / per_row)) // 64 * 64)
-        g = self.graph(1)
-        params = _oracle_params(L, random_parameters(g, 1234))
-        ins = self.inputs(0, 1, tokens=rows)
-        t0 = time.perf_counter()
-        L.train(g, self.shapes(1, tokens=rows), inputs=ins, parameters=params, iterations=1)
-        dt = time.perf_counter() - t0
-        return {"units": rows, "seconds": dt,
-                "sample": f"{rows} of the 8192 rows, one fwd+bwd+SGD step ({dt:.1f} s)"}
+    cpu_units, cpu_units_single = 1024, 128
+    cpu_extrapolation = ("rows/s of a row sample stands for the 8192-row step: the MLP's work is linear in "
+                         "the rows")
+
+    def cpu_case(self, rows):
+        return self.graph(1), self.shapes(1, tokens=rows), self.inputs(0, 1, tokens=rows)
+
+    def describe_sample(self, rows):
+        return f"{rows} of the 8192 rows (1024 -> 4096 -> 1024)"
 
 
 class Lm:
@@ -250,19 +244,19 @@ class Lm:
                 "model": "llama_lm_4l", "global_batch": self.batch * world, "seq_len": self.seq,
                 "parallelism": f"dp{world}", "l2": self.l2}
 
-    def cpu_sample(self, budget):
-        from tysor_b200.programs import random_parameters
-        L = _oracle()
-        seq = 256
-        g = self.graph(1, batch=1, seq=seq)
-        params = _oracle_params(L, random_parameters(g, 1234))
-        ins = self.inputs(0, 1, tokens=seq)
-        t0 = time.perf_counter()
-        L.train(g, self.shapes(1, tokens=seq), inputs=ins, parameters=params, iterations=1)
-        dt = time.perf_counter() - t0
-        return {"units": seq, "seconds": dt,
-                "sample": f"1 sequence x {seq} tokens (not 2048: attention is cheaper per token at this "
-                          f"length), one fwd+bwd+SGD step of the same 4-layer LM ({dt:.1f} s)"}
+    # Attention is cheaper per token at 256 than at 2048 tokens; the linear
+    # layers and the 32000-way head, which dominate, cost the same per token.
+    cpu_units, cpu_units_single = 256, 64
+    cpu_extrapolation = ("tokens/s of one short sequence stands for the 8 x 2048-token step: the linear "
+                         "layers and the head cost the same per token, attention less at 256 tokens "
+                         "(an upper bound on the CPU rate)")
+
+    def cpu_case(self, tokens):
+        g = self.graph(1, batch=1, seq=tokens)
+        return g, self.shapes(1, tokens=tokens), self.inputs(0, 1, tokens=tokens)
+
+    def describe_sample(self, tokens):
+        return f"1 sequence x {tokens} tokens of the same 4-layer LM (vocab 32000)"
 
 
 WORKLOADS = {w.key: w for w in (Block(), Mlp(), Lm())}
@@ -506,9 +500,14 @@ def run_ours(args, rank, world, local_rank, dist):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        info = wl.cpu_sample(args.ref_budget)
-        cpu = {"value": info["units"] / info["seconds"], "unit": wl.unit, "cores": os.cpu_count() or 1,
-               "kind": "port", "sample": info["sample"]}
+        cores = os.cpu_count() or 1
+        info = cpu_sample(wl, wl.cpu_units, cores)
+        one = cpu_sample(wl, wl.cpu_units_single, 1)
+        cpu = {"value": round(info["units"] / info["seconds"], 2), "unit": wl.unit, "cores": cores,
+               "kind": "port", "sample": info["sample"],
+               "single_thread": {"value": round(one["units"] / one["seconds"], 2), "unit": wl.unit, "cores": 1,
+                                 "sample": one["sample"]},
+               "extrapolation": wl.cpu_extrapolation}
 
     if rank == 0:
         cfg = wl.config(world)
@@ -544,15 +543,17 @@ def run_reference(args, rank, world):
     wl = WORKLOADS[args.workload]
     samples = []
     info = None
+    cores = os.cpu_count() or 1
     for i in range(args.warmup + args.steps):
-        info = wl.cpu_sample(args.ref_budget)
+        info = cpu_sample(wl, wl.cpu_units, cores)
         if i >= args.warmup:
             samples.append(info["seconds"])
     sec = float(np.median(samples))
     value = info["units"] / sec
-    cores = os.cpu_count() or 1
     cfg = wl.config(world)
-    cfg["parallelism"] = "cpu"
+    cfg["parallelism"] = f"cpu ({cores} threads)"
+    cfg["cpu_sample"] = info["sample"]
+    cfg["extrapolation"] = wl.cpu_extrapolation
     line = {
         "metric": wl.metric, "value": round(value, 2), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": True,
@@ -573,7 +574,6 @@ def main():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="block", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ref-budget", type=float, default=12.0, help="seconds per reference sample step")
     args = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

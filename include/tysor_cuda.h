@@ -44,6 +44,12 @@ bool tysor_cuda_synchronize(void* context);
 /* Matmul arithmetic: 0 = strict (3xTF32, the default), 1 = fast (1xTF32),
  * 2 = exact (CUDA-core fp32 in k order).  No reference counterpart. */
 bool tysor_cuda_set_matmul_mode(void* context, int mode);
+/* Runs the tensor-core pipelines' bounded barrier wait on a barrier that
+ * nothing arrives at, giving up after `limit_cycles` (1 to 4e9) SM cycles:
+ * returns false with "a tensor-core pipeline wait timed out", and the context
+ * stays usable.  Exercises the timeout path without a fault.  No reference
+ * counterpart. */
+bool tysor_cuda_probe_wait_timeout(void* context, int64_t limit_cycles);
 /* The context's CUDA stream (a cudaStream_t), for callers that time or
  * order their own work against it.  No reference counterpart. */
 void* tysor_cuda_context_stream(void* context);
@@ -274,12 +280,25 @@ bool tysor_cuda_graph_set_capture(void* graph, bool enable);
  * 3xTF32, enqueued on `stream` (a cudaStream_t; NULL = default stream).  It
  * needs no context and allocates nothing: the split operands live in a fixed
  * 32 MiB device array inside the library, so A and B together may span at
- * most 8,388,608 elements (larger calls fail with an error).  The first call
- * on each device looks up that array's address; make it before any stream
- * capture.  All calls on a device share the array, so calls that overlap on
- * the GPU race; order them on one stream. */
+ * most 8,388,608 elements (larger calls fail with an error).  The runtime
+ * claims those 32 MiB on a device when it loads the library's module there:
+ * at the first call on that device under CUDA's default lazy module loading,
+ * or when the process initialises the device with CUDA_MODULE_LOADING=EAGER.
+ * A caller that reserves most of the GPU's memory for its own pool should
+ * make the first call before reserving it.  The first call on each device
+ * also looks up that array's address; make it before any stream capture.
+ * All calls on a device share the array, so calls that overlap on the GPU
+ * race; order them on one stream.  The call only enqueues the work: a
+ * kernel-side failure is recorded on the device and reported by
+ * tysor_cuda_matmul_noalloc_status. */
 bool tysor_cuda_matmul_noalloc(void* stream, uint32_t m, uint32_t n, uint32_t k, const float* a,
                                const float* b, float* c);
+/* Companion of tysor_cuda_matmul_noalloc (no counterpart in the reference):
+ * waits for `stream`, then reads and clears the current device's no-alloc
+ * error word.  False (with tysor_cuda_last_error naming the failure, e.g. a
+ * tensor-core pipeline wait that timed out) if a call since the last check
+ * recorded one; its output is then incomplete.  Allocates nothing. */
+bool tysor_cuda_matmul_noalloc_status(void* stream);
 
 /* ---- data-parallel gradient all-reduce (NCCL over NVLink) ----------------
  * No reference counterpart: the reference has no multi-device code. */

@@ -1,10 +1,10 @@
 """Micro-benchmark of single kernels through the C ABI (used for the ncu
 captures summarised under profiles/).
 
-    python -m tysor_b200.kernel_bench matmul --m 4096 --n 5632 --k 2048 [--mode strict]
+    python kernel_bench.py matmul --m 4096 --n 5632 --k 2048 [--mode strict]
         [--ta] [--tb] [--reps 10]
-    python -m tysor_b200.kernel_bench rowop --op softmax --rows 65536 --width 4096
-    python -m tysor_b200.kernel_bench sweep [--div 1] [--reps 20] [--warmup 3]
+    python kernel_bench.py rowop --op softmax --rows 65536 --width 4096
+    python kernel_bench.py sweep [--div 1] [--reps 20] [--warmup 3]
 
 Prints one JSON line with the average time per call (CUDA events on the
 library's stream) and the achieved FLOP/s or GB/s.  `sweep` prints one line
@@ -19,15 +19,19 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 
 def main() -> None:
     import torch
 
-    from . import native
-    from .runtime import CudaContext, DeviceBuffer
+    from tysor_b200 import native
+    from tysor_b200.runtime import CudaContext, DeviceBuffer
 
     p = argparse.ArgumentParser()
     p.add_argument("kind", choices=["matmul", "rowop", "sweep"])
@@ -129,8 +133,8 @@ def measured_peaks():
 def sweep(ctx, lib, stream, a) -> None:
     """The norm/activation/loss op sweep and matmul+relu at their full sizes
     (rows divided by --div)."""
-    from . import native
-    from .runtime import DeviceBuffer
+    from tysor_b200 import native
+    from tysor_b200.runtime import DeviceBuffer
     peaks, src = measured_peaks()
     rng = np.random.default_rng(0)
     rows, width = 65536 // a.div, 4096

@@ -1,12 +1,12 @@
 """Summaries of ncu output for profiles/.
 
-    python -m tysor_b200.profiling launches gpurun_out/launches.csv [N]
+    python profiling.py launches launches.csv [N]
         per-kernel launches, total device time and share of a
         `ncu --metrics gpu__time_duration.sum --csv` launch list (N: only
         the N launches after the bench's pre-timing spin kernel)
-    python -m tysor_b200.profiling report prof.ncu-rep
+    python profiling.py report prof.ncu-rep
         the headline metrics of an `ncu --set full` capture
-    python -m tysor_b200.profiling traffic gpurun_out/sweep_ncu.csv
+    python profiling.py traffic sweep_ncu.csv
         per-launch duration and DRAM bytes of a `--metrics` capture
 """
 from __future__ import annotations

@@ -12,7 +12,9 @@ small seeded inputs.  The committed JSON is the golden set the oracle is
 checked against (tests/test_oracle_golden.py); nothing at test time reads the
 reference tree.
 
-Run from the repository root:  python tests/golden/make_golden.py
+Run from the repository root with the reference checkout's path:
+
+    python tests/golden/make_golden.py <path to the tysor reference checkout>
 """
 from __future__ import annotations
 
@@ -24,7 +26,7 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference/src/backend/pytorch/runtime.rs"
+HELPERS = os.path.join("src", "backend", "pytorch", "runtime.rs")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "torch_helper_golden.json")
 
 
@@ -46,8 +48,11 @@ def seeded(shape, seed, lo=-1.0, hi=1.0):
 
 
 def main() -> None:
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the tysor reference checkout>")
+    ref = os.path.join(sys.argv[1], HELPERS)
     ns: dict = {}
-    exec(compile(extract_helpers(REF), REF, "exec"), ns)
+    exec(compile(extract_helpers(ref), ref, "exec"), ns)
     T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
     cases = []
 

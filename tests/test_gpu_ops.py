@@ -228,7 +228,8 @@ def test_rms_norm_softmax_silu_sweep(dev, rows, width):
 @pytest.mark.parametrize("rows,width", [(2, 3), (17, 1000), (8192, 32000)])
 def test_cross_entropy_sweep(dev, rows, width):
     """Dense-target CE (reference) and class-label CE (extension), forward
-    and backward; the largest case is logits [8192, 32000] ~ N(0, 2)."""
+    and backward; the largest case is logits [8192, 32000] ~ N(0, 2), for
+    both forms."""
     L.set_threads(16)
     rng = np.random.default_rng(width)
     logits = (2.0 * rng.standard_normal((rows, width))).astype(np.float32)
@@ -240,11 +241,35 @@ def test_cross_entropy_sweep(dev, rows, width):
     dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy_labels_backward(dev.h, LG.handle, LB.handle, G.handle, rows,
                                                                      width, False))
     close(G.read(), L.cross_entropy_backward(lt, T([rows], labels)).data)
+    # Dense target (the reference's own form, layers.rs:301-324): a general
+    # non-negative target at the small sizes; at [8192, 32000] the one-hot
+    # rows of the labels, as the config's parity path feeds it.
     if rows * width <= 17 * 1000:
         target = np.abs(rng.standard_normal((rows, width))).astype(np.float32)
-        TG = dev.buf(target)
-        dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy(dev.h, LG.handle, TG.handle, O.handle, rows, width))
-        close(O.read(), L.cross_entropy(lt, T(target.shape, target)).data)
-        dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy_backward(dev.h, LG.handle, TG.handle, G.handle, rows, width,
-                                                                  False))
-        close(G.read(), L.cross_entropy_backward(lt, T(target.shape, target)).data)
+    else:
+        target = np.zeros((rows, width), np.float32)
+        target[np.arange(rows), labels.astype(np.int64)] = 1.0
+    TG = dev.buf(target)
+    dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy(dev.h, LG.handle, TG.handle, O.handle, rows, width))
+    close(O.read(), L.cross_entropy(lt, T(target.shape, target)).data)
+    dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy_backward(dev.h, LG.handle, TG.handle, G.handle, rows, width,
+                                                              False))
+    close(G.read(), L.cross_entropy_backward(lt, T(target.shape, target)).data)
+
+
+def test_pipeline_wait_gives_up_and_reports(dev):
+    """The tensor-core pipelines' mbarrier wait is bounded: a wait on a
+    barrier that nothing arrives at gives up after its cycle limit and
+    records an error that the host reads as a failure.  The context stays
+    usable afterwards (a matmul then runs and matches the oracle)."""
+    from tysor_b200 import native
+    assert not dev.lib.tysor_cuda_probe_wait_timeout(dev.h, 20000)
+    assert "wait timed out" in native.last_error()
+    assert not dev.lib.tysor_cuda_probe_wait_timeout(dev.h, 0)  # limit outside [1, 4e9]
+    assert "limit" in native.last_error()
+    a, b = rnd((256, 64), 30), rnd((64, 128), 31)
+    A, B, C = dev.buf(a), dev.buf(b), dev.zeros(256 * 128)
+    dev.ok(dev.lib.tysor_cuda_dispatch_matmul(dev.h, A.handle, B.handle, C.handle, 256, 128, 64))
+    want = L.matmul(T(a.shape, a), T(b.shape, b)).data
+    got = C.read()
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-5

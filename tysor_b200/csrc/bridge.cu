@@ -193,6 +193,14 @@ bool tysor_cuda_synchronize(void* context) {
   return guarded([&] { ctx_of(context)->sync_and_check(); });
 }
 
+bool tysor_cuda_probe_wait_timeout(void* context, int64_t limit_cycles) {
+  return guarded([&] {
+    Context* c = ctx_of(context);
+    launch_wait_timeout_probe(c->d_err, (long long)limit_cycles, c->stream);
+    c->sync_and_check();
+  });
+}
+
 void* tysor_cuda_context_stream(void* context) {
   void* out = nullptr;
   guarded([&] { out = (void*)ctx_of(context)->stream; });

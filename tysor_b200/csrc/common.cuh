@@ -128,6 +128,12 @@ bool gemm_fuses_box_epilogue(int batch, int64_t M, int64_t N, int64_t K, bool ta
 // Whether gemm_launch may use the 2-SM (cta_group::2 cluster pair) kernel.
 extern bool g_two_sm_enabled;
 
+// One thread waits, with the GEMM pipelines' bounded mbarrier wait, on a
+// barrier that nothing arrives at; after `limit_cycles` the wait gives up
+// and records kErrBarrierTimeout in *err.  Checks the timeout path without
+// faulting or hanging the GPU.
+void launch_wait_timeout_probe(int* err, long long limit_cycles, cudaStream_t st);
+
 // lo(x) = x - tf32_trunc(x) over n contiguous elements.
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st);
 // Per batch item b: hi_t[b][c][r] = x[b][r][c] and lo_t = lo(hi_t) (lo_t may

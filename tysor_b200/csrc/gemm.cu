@@ -61,18 +61,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the given phase parity; gives up after kWaitCycles, recording
-// kErrBarrierTimeout, so a lost arrival can never hang the GPU.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+// Waits for the given phase parity; gives up after `limit` cycles,
+// recording kErrBarrierTimeout, so a lost arrival can never hang the GPU.
+__device__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, int* err, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(err, 0, (int)kErrBarrierTimeout);
       return false;
     }
   }
   return true;
+}
+
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+  return mbar_wait_limit(bar, parity, err, kWaitCycles);
+}
+
+// One thread initialises a barrier that expects one arrival, never arrives,
+// and waits on it with the pipelines' own wait: the wait must give up after
+// `limit` cycles and record kErrBarrierTimeout.  No copy or MMA is in flight.
+__global__ void wait_timeout_probe_kernel(int* err, long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  mbar_wait_limit(b, 0, err, limit);
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
@@ -1609,6 +1624,13 @@ int64_t gemm_splitk_ws_elems(int batch, int64_t M, int64_t N, int64_t K, int mod
   const int parts = splitk_parts(batch, M, N, K);
   if (parts <= 1) return 0;
   return (int64_t)parts * batch * M * ((N + 3) & ~(int64_t)3);
+}
+
+void launch_wait_timeout_probe(int* err, long long limit_cycles, cudaStream_t st) {
+  if (limit_cycles < 1 || limit_cycles > kWaitCycles) throw CudaError("wait probe: limit outside [1, 4e9] cycles");
+  wait_timeout_probe_kernel<<<1, 1, 0, st>>>(err, limit_cycles);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st) {

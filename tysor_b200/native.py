@@ -31,6 +31,7 @@ SIGNATURES = {
     "tysor_cuda_synchronize": (c_bool, [V]),
     "tysor_cuda_set_matmul_mode": (c_bool, [V, c_int]),
     "tysor_cuda_context_stream": (V, [V]),
+    "tysor_cuda_probe_wait_timeout": (c_bool, [V, c_int64]),
     "tysor_cuda_buffer_new_with_data": (V, [V, FP, c_size_t]),
     "tysor_cuda_buffer_new_zeroed": (V, [V, c_size_t]),
     "tysor_cuda_buffer_free": (None, [V]),
@@ -94,6 +95,7 @@ SIGNATURES = {
     "tysor_cuda_graph_launch_count": (c_int64, [V]),
     "tysor_cuda_graph_set_capture": (c_bool, [V, c_bool]),
     "tysor_cuda_matmul_noalloc": (c_bool, [V, U32, U32, U32, V, V, V]),
+    "tysor_cuda_matmul_noalloc_status": (c_bool, [V]),
     "tysor_cuda_nccl_get_unique_id": (c_bool, [U8P]),
     "tysor_cuda_comm_init": (c_bool, [V, c_int, c_int, U8P, c_int]),
     "tysor_cuda_comm_free": (c_bool, [V]),
