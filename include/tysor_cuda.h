@@ -271,6 +271,14 @@ int64_t tysor_cuda_graph_launch_count(void* graph);
 /* Capture one train step in a CUDA graph and replay it for later steps
  * (default on for train). */
 bool tysor_cuda_graph_set_capture(void* graph, bool enable);
+/* How a train step sums its objective into the loss.  0 (default): a
+ * parallel tree sum in f32, typically closer to the exact sum.  1: the
+ * reference's tensor_sum (training/executor.rs:109-111), one f32 accumulator
+ * in index order, which reproduces the reference's rounding (over millions
+ * of terms it can drift by 1e-3..1e-2 from the exact sum) at the cost of one
+ * thread walking the objective (about 70 ms per 33.5M elements).  The loss
+ * does not feed the gradients, so training is the same either way. */
+bool tysor_cuda_graph_set_loss_order(void* graph, int order);
 
 /* ---- matmul without allocation ---------------------------------------------
  * No counterpart in the reference.  For callers that must not allocate

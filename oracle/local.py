@@ -27,7 +27,12 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "libtysor_oracle.so")
-_lib = None
+# The f64 twin of the C library (tysor_local.c built with TL_F64): the same
+# algorithm in double precision, used only to measure errors against a
+# nearly exact answer (precision(64)).
+_LIB64_PATH = os.path.join(_HERE, "libtysor_oracle64.so")
+_libs: Dict[int, ctypes.CDLL] = {}
+_bits = 32
 
 OPS = {"+": 0, "-": 1, "*": 2, "/": 3}
 
@@ -38,11 +43,12 @@ def build() -> str:
 
 
 def lib():
-    global _lib
-    if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+    """The C op library of the current precision (f32 unless precision(64))."""
+    if _bits not in _libs:
+        path = _LIB64_PATH if _bits == 64 else _LIB_PATH
+        if not os.path.exists(path):
             build()
-        _lib = ctypes.CDLL(_LIB_PATH)
+        _lib = ctypes.CDLL(path)
         P = ctypes.c_void_p
         I = ctypes.c_int64
         D = ctypes.c_double
@@ -87,21 +93,54 @@ def lib():
             "tl_transpose": (None, [P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
             "tl_bias_grad": (None, [P, P, I, I]),
             "tl_sgd": (None, [P, P, D, I]),
-            "tl_sum": (F, [P, I]),
+            "tl_sum": (D, [P, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(_lib, name)
             fn.restype = res
             fn.argtypes = args
-    return _lib
+        _lib.tl_set_threads(_threads)
+        _libs[_bits] = _lib
+    return _libs[_bits]
+
+
+_threads = 1
 
 
 def set_threads(n: int) -> None:
-    lib().tl_set_threads(int(n))
+    global _threads
+    _threads = int(n)
+    for handle in _libs.values():
+        handle.tl_set_threads(_threads)
+
+
+def _dt():
+    """numpy dtype of tensor data at the current precision."""
+    return np.float64 if _bits == 64 else np.float32
+
+
+class precision:
+    """`with precision(64):` runs the oracle in f64 (the same loops in double;
+    tensors hold float64 data) -- an error-budget reference, not the
+    reference's own arithmetic."""
+
+    def __init__(self, bits: int):
+        if bits not in (32, 64):
+            raise ValueError("precision is 32 or 64 bits")
+        self.bits = bits
+
+    def __enter__(self):
+        global _bits
+        self._saved, _bits = _bits, self.bits
+        return self
+
+    def __exit__(self, *exc):
+        global _bits
+        _bits = self._saved
 
 
 def _p(a: np.ndarray):
-    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    assert a.dtype == _dt() and a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
@@ -124,7 +163,7 @@ class Tensor:
 
 
 def _new(shape, dtype="float32") -> Tensor:
-    return Tensor(list(shape), np.zeros(_numel(shape), dtype=np.float32), dtype)
+    return Tensor(list(shape), np.zeros(_numel(shape), dtype=_dt()), dtype)
 
 
 class OracleError(RuntimeError):
@@ -164,7 +203,7 @@ def backward_fake_weight(i, o, dtype="float32") -> Tensor:
 
 
 def ones_gain(n) -> Tensor:
-    return Tensor([n], np.ones(n, dtype=np.float32))
+    return Tensor([n], np.ones(n, dtype=_dt()))
 
 
 def binary_tt(op, a: Tensor, b: Tensor) -> Tensor:
@@ -261,7 +300,7 @@ def matmul(a: Tensor, b: Tensor) -> Tensor:
     for i in range(nb):
         ai = np.ascontiguousarray(av[i])
         bi = np.ascontiguousarray(bv[i])
-        oi = np.zeros(m * n, dtype=np.float32)
+        oi = np.zeros(m * n, dtype=_dt())
         lib().tl_matmul(_p(ai), _p(bi), _p(oi), m, k, n)
         ov[i] = oi
     return out
@@ -278,7 +317,7 @@ def transpose_last2(t: Tensor) -> Tensor:
     dst = out.data.reshape(nb, r * c)
     for i in range(nb):
         si = np.ascontiguousarray(src[i])
-        di = np.zeros(r * c, dtype=np.float32)
+        di = np.zeros(r * c, dtype=_dt())
         lib().tl_transpose2d(_p(si), _p(di), r, c)
         dst[i] = di
     return out
@@ -667,7 +706,7 @@ def _primitive_forward(node, values):
 
 def _input_tensor(value, shapes, inputs):
     if inputs is not None and value.name in inputs:
-        arr = np.ascontiguousarray(np.asarray(inputs[value.name], dtype=np.float32).reshape(-1))
+        arr = np.ascontiguousarray(np.asarray(inputs[value.name], dtype=_dt()).reshape(-1))
         shape = shapes.get(value.name, [arr.size])
         if _numel(shape) != arr.size:
             raise OracleError(f"input '{value.name}' has {arr.size} values, shape {shape}")
@@ -820,7 +859,7 @@ def compute_value_gradients(graph, shapes, inputs=None):
     oid = graph.objective_id()
     obj = _tensor(values.get(oid))
     grads: Dict[int, Tensor] = {}
-    _acc(grads, oid, Tensor(list(obj.shape), np.ones(obj.data.size, dtype=np.float32), obj.dtype))
+    _acc(grads, oid, Tensor(list(obj.shape), np.ones(obj.data.size, dtype=_dt()), obj.dtype))
     for node in reversed(graph.nodes):
         if node.output not in grads:
             continue
@@ -934,7 +973,7 @@ def compute_parameter_gradients(graph, values, oid, parameters, value_grads=None
     """training/executor.rs:563-743.  If `value_grads` is a dict it receives
     the per-value gradients of the walk as well."""
     obj = _tensor(values.get(oid))
-    vgrads: Dict[int, Tensor] = {oid: Tensor(list(obj.shape), np.ones(obj.data.size, np.float32), obj.dtype)}
+    vgrads: Dict[int, Tensor] = {oid: Tensor(list(obj.shape), np.ones(obj.data.size, _dt()), obj.dtype)}
     pgrads: Dict[str, Tensor] = {}
     for node in reversed(graph.nodes):
         if node.output not in vgrads:

@@ -15,10 +15,23 @@ own seeded inputs and parameters, on the device against the oracle.
 * The 4-layer LM (full block dimensions, vocab 32000, tied head, next-token
   cross entropy) on one sequence of 256 tokens for 2 steps.
 
-Bars (the accuracy contract: strict matmul and fp32 ops rel 1e-5, training
-losses rel 1e-4): forward values and parameters Frobenius rel 1e-5; losses
-rel 1e-4; parameter gradients Frobenius rel GRAD_BAR.  Every measured error
-is printed (run with -s) so the margin is visible.
+How each tensor is judged.  At these sizes the f32 oracle is itself a few
+1e-6..1e-5 away from the exact answer (sequential f32 sums over K up to
+16384, a dozen chained ops), so the device is compared with the oracle's f64
+twin (the same algorithm in double precision, `local.precision(64)`):
+    err_dev = |device - f64| / |f64|,  err_ref = |oracle f32 - f64| / |f64|
+(Frobenius).  A tensor passes if err_dev < 1e-5 (the accuracy contract for
+strict matmul and fp32 ops) or err_dev <= err_ref (the device is no further
+from the exact answer than the reference's own f32 arithmetic); the device
+and the f32 oracle must also agree within 1e-4 on every tensor.
+
+The loss is the sum of millions of terms.  The reference sums it with one
+f32 accumulator in index order (training/executor.rs:109-111), which drifts
+by ~1e-3..1e-2 from the exact sum at these sizes.  The device's default tree
+sum is judged against the exact sum of the f64 objective (rel 1e-5); with
+the reference's order selected (`set_loss_order("sequential")`) the device
+must track the f32 oracle's printed loss within rel 1e-4, the tracking bar
+for training losses.  Every measured error is printed (run with -s).
 """
 import os
 import sys
@@ -36,7 +49,7 @@ import bench  # noqa: E402  (the workloads' seeded inputs)
 
 pytestmark = pytest.mark.gpu
 
-GRAD_BAR = 1e-5
+BAR = 1e-5
 
 
 def frob(a, b):
@@ -45,16 +58,33 @@ def frob(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def to_oracle(params):
-    return {k: L.Tensor(list(v.shape), np.ascontiguousarray(v, np.float32).reshape(-1).copy())
-            for k, v in params.items()}
+def to_oracle(params, dt=np.float32):
+    return {k: L.Tensor(list(v.shape), np.ascontiguousarray(v, dt).reshape(-1).copy()) for k, v in params.items()}
 
 
-def report(title, errs):
-    worst = max(errs.items(), key=lambda kv: kv[1])
-    print(f"\n{title}: worst {worst[0]} {worst[1]:.3e}")
-    for k, v in sorted(errs.items()):
-        print(f"  {k}: {v:.3e}")
+def f64_inputs(ins):
+    return {k: np.asarray(v, np.float64) for k, v in ins.items()}
+
+
+class Ledger:
+    """Per-tensor errors: device vs f64, f32 oracle vs f64, device vs oracle."""
+
+    def __init__(self, title):
+        self.title, self.rows = title, {}
+
+    def add(self, name, dev, ref32, ref64):
+        self.rows[name] = (frob(dev, ref64), frob(ref32, ref64), frob(dev, ref32))
+
+    def report(self):
+        print(f"\n{self.title}: tensor  err_dev(vs f64)  err_ref(f32 oracle vs f64)  dev-vs-oracle")
+        for k, (d, r, p) in sorted(self.rows.items()):
+            print(f"  {k}: {d:.2e}  {r:.2e}  {p:.2e}")
+
+    def check(self):
+        self.report()
+        for k, (d, r, p) in self.rows.items():
+            assert d < BAR or d <= r, (k, d, r)
+            assert p < 1e-4, (k, p)
 
 
 def test_block_full_dims_one_sequence(cuda_ctx):
@@ -66,34 +96,44 @@ def test_block_full_dims_one_sequence(cuda_ctx):
     ins = wl.inputs(0, 1, tokens=seq)
     params = random_parameters(g, 1234)
     L.set_threads(os.cpu_count() or 1)
+    out_id, oid = g.named["out"], g.objective_id()
     values, grads, _ = L.train_step_grads(g, shapes, inputs=ins, parameters=to_oracle(params))
     want_params = to_oracle(params)
     L.apply_sgd(want_params, grads, wl.lr)
+    ref_loss = L.tensor_sum(values[oid][1])
+    with L.precision(64):
+        v64, g64, _ = L.train_step_grads(g, shapes, inputs=f64_inputs(ins), parameters=to_oracle(params, np.float64))
+        p64 = to_oracle(params, np.float64)
+        L.apply_sgd(p64, g64, wl.lr)
+    exact_loss = float(v64[oid][1].data.sum())
 
     ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins, parameters=params)
     losses = ex.train(1, wl.lr)
-    errs = {}
-    out_id = g.named["out"]
-    errs["value out"] = frob(ex.value(out_id).data, values[out_id][1].data)
-    loss_id = g.objective_id()
-    want_loss = L.tensor_sum(values[loss_id][1])
-    errs["loss"] = abs(losses[0] - want_loss) / abs(want_loss)
+    led = Ledger("block 1 x 2048, full dims")
+    led.add("value out", ex.value(out_id).data, values[out_id][1].data, v64[out_id][1].data)
     assert len(grads) == len(params)
-    for name, gt in grads.items():
+    for name in grads:
         got = ex.parameter_grad(name)
         assert np.isfinite(got).all(), name
-        errs["grad " + name] = frob(got, gt.data)
-    for name, t in want_params.items():
-        errs["param " + name] = frob(ex.parameter(name), t.data)
+        led.add("grad " + name, got, grads[name].data, g64[name].data)
+    for name in want_params:
+        led.add("param " + name, ex.parameter(name), want_params[name].data, p64[name].data)
     ex.close()
-    report("block 1 x 2048, full dims", errs)
-    assert errs["value out"] < 1e-5
-    assert errs["loss"] < 1e-4
-    for k, v in errs.items():
-        if k.startswith("grad "):
-            assert v < GRAD_BAR, (k, v)
-        if k.startswith("param "):
-            assert v < 1e-5, (k, v)
+    tree = abs(losses[0] - exact_loss) / abs(exact_loss)
+    ref = abs(ref_loss - exact_loss) / abs(exact_loss)
+    print(f"\nloss: device tree sum vs exact {tree:.2e}; reference's f32 sum vs exact {ref:.2e}")
+    led.check()
+    assert tree < BAR
+
+    # The reference's summation order: the loss tracks the oracle's.
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins, parameters=params)
+    ex.set_loss_order("sequential")
+    seq_loss = ex.train(1, wl.lr)[0]
+    objective = ex.value(oid).data
+    ex.close()
+    print(f"loss: device sequential vs reference {abs(seq_loss - ref_loss) / abs(ref_loss):.2e}")
+    assert seq_loss == L.tensor_sum(L.Tensor([objective.size], objective))  # same order, same rounding
+    assert abs(seq_loss - ref_loss) <= 1e-4 * abs(ref_loss)
 
 
 def test_mlp_full_size_three_steps(cuda_ctx):
@@ -105,15 +145,26 @@ def test_mlp_full_size_three_steps(cuda_ctx):
     params = random_parameters(g, 1234)
     L.set_threads(os.cpu_count() or 1)
     want, wparams = L.train(g, shapes, inputs=ins, parameters=to_oracle(params), lr=wl.lr, iterations=3)
-    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins, parameters=params)
-    got = ex.train(3, wl.lr)
-    errs = {f"loss {i}": abs(a - b) / abs(b) for i, (a, b) in enumerate(zip(got, want))}
-    for name, t in wparams.items():
-        errs["param " + name] = frob(ex.parameter(name), t.data)
-    ex.close()
-    report("mlp [8192,1024]->4096->1024, 3 steps", errs)
-    for k, v in errs.items():
-        assert v < (1e-4 if k.startswith("loss") else 1e-5), (k, v)
+    with L.precision(64):
+        want64, wparams64 = L.train(g, shapes, inputs=f64_inputs(ins), parameters=to_oracle(params, np.float64),
+                                    lr=wl.lr, iterations=3)
+    for order in ("tree", "sequential"):
+        ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins, parameters=params)
+        ex.set_loss_order(order)
+        got = ex.train(3, wl.lr)
+        led = Ledger(f"mlp [8192,1024]->4096->1024, 3 steps ({order} loss)")
+        for name in wparams:
+            led.add("param " + name, ex.parameter(name), wparams[name].data, wparams64[name].data)
+        ex.close()
+        led.check()
+        for i, (a, r, x) in enumerate(zip(got, want, want64)):
+            print(f"  loss {i}: device vs exact {abs(a - x) / abs(x):.2e}, device vs reference "
+                  f"{abs(a - r) / abs(r):.2e}, reference vs exact {abs(r - x) / abs(x):.2e}")
+            if order == "sequential":
+                assert abs(a - r) <= 1e-4 * abs(r), (i, a, r)
+            else:
+                # want64 sums the f64 objective in f64 order: nearly exact.
+                assert abs(a - x) <= BAR * abs(x), (i, a, x)
 
 
 def test_lm_4_layers_vocab_32000_two_steps(cuda_ctx):
@@ -126,26 +177,32 @@ def test_lm_4_layers_vocab_32000_two_steps(cuda_ctx):
     ins = wl.inputs(0, 1, tokens=seq)
     params = random_parameters(g, 1234)
     L.set_threads(os.cpu_count() or 1)
-    # Step 1 with its gradients, then step 2 from the updated parameters.
-    values, grads, _ = L.train_step_grads(g, shapes, inputs=ins, parameters=to_oracle(params))
     oid = g.objective_id()
-    want_losses = [L.tensor_sum(values[oid][1])]
-    p1 = to_oracle(params)
-    L.apply_sgd(p1, grads, lr)
-    more, p2 = L.train(g, shapes, inputs=ins, parameters=p1, lr=lr, iterations=1)
-    want_losses += more
+
+    def oracle(dt):
+        # Step 1 with its gradients, then step 2 from the updated parameters.
+        inputs = ins if dt == np.float32 else f64_inputs(ins)
+        values, grads, _ = L.train_step_grads(g, shapes, inputs=inputs, parameters=to_oracle(params, dt))
+        losses = [L.tensor_sum(values[oid][1]) if dt == np.float32 else float(values[oid][1].data.sum())]
+        p1 = to_oracle(params, dt)
+        L.apply_sgd(p1, grads, lr)
+        more, p2 = L.train(g, shapes, inputs=inputs, parameters=p1, lr=lr, iterations=1)
+        return grads, losses + more, p2
+
+    grads, want, p2 = oracle(np.float32)
+    with L.precision(64):
+        grads64, want64, p2_64 = oracle(np.float64)
 
     ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins, parameters=params)
     got = ex.train(1, lr)
-    errs = {}
-    for name, gt in grads.items():
-        errs["grad " + name] = frob(ex.parameter_grad(name), gt.data)
+    led = Ledger("lm 4 layers, vocab 32000, 1 x 256 tokens, 2 steps")
+    for name in grads:
+        led.add("grad " + name, ex.parameter_grad(name), grads[name].data, grads64[name].data)
     got += ex.train(1, lr)
-    errs.update({f"loss {i}": abs(a - b) / abs(b) for i, (a, b) in enumerate(zip(got, want_losses))})
-    for name, t in p2.items():
-        errs["param " + name] = frob(ex.parameter(name), t.data)
+    for name in p2:
+        led.add("param " + name, ex.parameter(name), p2[name].data, p2_64[name].data)
     ex.close()
-    report("lm 4 layers, vocab 32000, 1 x 256 tokens, 2 steps", errs)
-    for k, v in errs.items():
-        bar = 1e-4 if k.startswith("loss") else (GRAD_BAR if k.startswith("grad") else 1e-5)
-        assert v < bar, (k, v)
+    led.check()
+    for i, (a, r, x) in enumerate(zip(got, want, want64)):
+        print(f"  loss {i}: device vs exact {abs(a - x) / abs(x):.2e}, device vs reference {abs(a - r) / abs(r):.2e}")
+        assert abs(a - r) <= 1e-4 * abs(r), (i, a, r)  # 256 terms: the orders agree closely

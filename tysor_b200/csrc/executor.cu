@@ -1832,7 +1832,11 @@ struct Executor {
     Slot** ls = &loss;
     need_scratch(1024);
     Slot** scr = &scratch;
-    update.push_back([=](cudaStream_t st) { launch_reduce_sum(o->p, (*ls)->p, (*scr)->p, n, st); });
+    const int* order = &loss_order;
+    update.push_back([=](cudaStream_t st) {
+      if (*order == 1) launch_sequential_sum(o->p, (*ls)->p, n, st);
+      else launch_reduce_sum(o->p, (*ls)->p, (*scr)->p, n, st);
+    });
     Context* cx = ctx;
     Slot** gb = &grad_block;
     update.push_back([=, this](cudaStream_t st) {
@@ -1863,6 +1867,9 @@ struct Executor {
     }
   }
   float lr_f = 0.01f;
+  // 0: tree sum of the objective (default); 1: the reference's sequential f32
+  // sum in index order (tysor_cuda_graph_set_loss_order).
+  int loss_order = 0;
 
   // Whether every trained parameter owns its value buffer (not a view) of
   // its gradient's size, so the values can form one block.
@@ -2337,6 +2344,20 @@ bool tysor_cuda_graph_set_capture(void* graph, bool enable) {
       cudaGraphExecDestroy(e->exec);
       e->exec = nullptr;
     }
+  });
+}
+
+bool tysor_cuda_graph_set_loss_order(void* graph, int order) {
+  return guarded_g([&] {
+    Executor* e = E(graph);
+    if (order != 0 && order != 1) throw CudaError("loss order must be 0 (tree) or 1 (sequential, the reference's)");
+    if (order != e->loss_order && e->exec) {
+      // The captured step holds the other reduction: capture again.
+      TYSOR_CUDA(cudaStreamSynchronize(e->ctx->stream));
+      cudaGraphExecDestroy(e->exec);
+      e->exec = nullptr;
+    }
+    e->loss_order = order;
   });
 }
 

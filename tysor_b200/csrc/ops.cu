@@ -1431,6 +1431,37 @@ __global__ void reduce_final_kernel(const float* __restrict__ partial, float* ou
   if (threadIdx.x == 0) out[0] = acc;
 }
 
+// The reference's tensor_sum (training/executor.rs:109-111): one f32
+// accumulator adding x[0], x[1], ... in index order from 0.0, so the result
+// rounds exactly as the reference's loss does.  One thread walks the whole
+// tensor (each add waits for the previous one); it reads four float4 ahead
+// of the adds so the loads overlap the chain.  Opt-in: a tree sum is
+// typically closer to the exact sum, this one reproduces the reference.
+__global__ void sequential_sum_kernel(const float* __restrict__ x, float* out, int64_t n) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float acc = 0.0f;
+  int64_t i = 0;
+  if ((((uintptr_t)x) & 15) == 0) {
+    const float4* v = reinterpret_cast<const float4*>(x);
+    const int64_t nv = n / 4;
+    int64_t j = 0;
+    for (; j + 4 <= nv; j += 4) {
+      const float4 a = v[j], b = v[j + 1], c = v[j + 2], d = v[j + 3];
+      acc = acc + a.x; acc = acc + a.y; acc = acc + a.z; acc = acc + a.w;
+      acc = acc + b.x; acc = acc + b.y; acc = acc + b.z; acc = acc + b.w;
+      acc = acc + c.x; acc = acc + c.y; acc = acc + c.z; acc = acc + c.w;
+      acc = acc + d.x; acc = acc + d.y; acc = acc + d.z; acc = acc + d.w;
+    }
+    for (; j < nv; ++j) {
+      const float4 a = v[j];
+      acc = acc + a.x; acc = acc + a.y; acc = acc + a.z; acc = acc + a.w;
+    }
+    i = nv * 4;
+  }
+  for (; i < n; ++i) acc = acc + x[i];
+  out[0] = acc;
+}
+
 int row_threads(int64_t width) {
   if (width >= 8192) return 1024;
   if (width >= 2048) return 512;
@@ -1860,6 +1891,11 @@ void launch_reduce_sum(const float* x, float* out, float* partial, int64_t n, cu
   reduce_partial_kernel<<<blocks, 256, 0, st>>>(x, partial, n);
   check_launch();
   reduce_final_kernel<<<1, 1024, 0, st>>>(partial, out, blocks);
+  check_launch();
+}
+
+void launch_sequential_sum(const float* x, float* out, int64_t n, cudaStream_t st) {
+  sequential_sum_kernel<<<1, 32, 0, st>>>(x, out, n);
   check_launch();
 }
 

@@ -137,6 +137,9 @@ void launch_colsum(const float* grad, float* out, float* partial, int64_t rows, 
                    int accumulate, cudaStream_t st);
 // Sum of all elements into out[0]; `partial` needs 1024 floats.
 void launch_reduce_sum(const float* x, float* out, float* partial, int64_t n, cudaStream_t st);
+// out[0] = x[0] + x[1] + ... in index order with one f32 accumulator (the
+// reference's tensor_sum rounding; one thread, so slow on large tensors).
+void launch_sequential_sum(const float* x, float* out, int64_t n, cudaStream_t st);
 
 // p = p - (lr * g), each product and difference rounded separately.
 void launch_sgd(float* p, const float* g, float lr, int64_t n, cudaStream_t st);

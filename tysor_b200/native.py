@@ -94,6 +94,7 @@ SIGNATURES = {
     "tysor_cuda_graph_read_parameter_grad": (c_bool, [V, c_char_p, FP, c_size_t]),
     "tysor_cuda_graph_launch_count": (c_int64, [V]),
     "tysor_cuda_graph_set_capture": (c_bool, [V, c_bool]),
+    "tysor_cuda_graph_set_loss_order": (c_bool, [V, c_int]),
     "tysor_cuda_matmul_noalloc": (c_bool, [V, U32, U32, U32, V, V, V]),
     "tysor_cuda_matmul_noalloc_status": (c_bool, [V]),
     "tysor_cuda_nccl_get_unique_id": (c_bool, [U8P]),

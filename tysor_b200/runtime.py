@@ -173,6 +173,13 @@ class CudaGraphExecutor:
     def set_capture(self, enable: bool) -> None:
         check(self._lib.tysor_cuda_graph_set_capture(self.handle, bool(enable)), "set_capture")
 
+    def set_loss_order(self, order: str) -> None:
+        """"tree" (default) or "sequential" (the reference's f32 tensor_sum order)."""
+        codes = {"tree": 0, "sequential": 1}
+        if order not in codes:
+            raise ValueError("loss order is 'tree' or 'sequential'")
+        check(self._lib.tysor_cuda_graph_set_loss_order(self.handle, codes[order]), "set_loss_order")
+
     def enable_allreduce(self, enable: bool = True) -> None:
         check(self._lib.tysor_cuda_graph_enable_allreduce(self.handle, bool(enable)), "enable_allreduce")
 
