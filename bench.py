@@ -390,6 +390,8 @@ def run_ours(args, rank, world, local_rank, dist):
     wl = WORKLOADS[args.workload]
     torch.cuda.set_device(local_rank)
     ctx = CudaContext(local_rank)
+    if args.accum_chunk:
+        ctx.set_matmul_accumulation(args.accum_chunk)
     lib = native.lib()
     stream = torch.cuda.ExternalStream(lib.tysor_cuda_context_stream(ctx.handle))
     graph = wl.graph(world)
@@ -512,6 +514,8 @@ def run_ours(args, rank, world, local_rank, dist):
     if rank == 0:
         cfg = wl.config(world)
         cfg["last_loss"] = losses[-1] if losses else None
+        if args.accum_chunk:
+            cfg["accum_chunk_kblocks"] = args.accum_chunk
         line = {
             "metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
@@ -574,6 +578,8 @@ def main():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="block", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--accum-chunk", type=int, default=0,
+                   help="k-blocks per tensor-memory accumulation chunk of the matmuls (0: default 8)")
     args = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -44,6 +44,18 @@ bool tysor_cuda_synchronize(void* context);
 /* Matmul arithmetic: 0 = strict (3xTF32, the default), 1 = fast (1xTF32),
  * 2 = exact (CUDA-core fp32 in k order).  No reference counterpart. */
 bool tysor_cuda_set_matmul_mode(void* context, int mode);
+/* Tensor-core matmuls (strict and fast): how many k-blocks of 16 the tensor
+ * core accumulates in tensor memory before the partial sum is added into
+ * fp32 registers with round-to-nearest.  The tensor core adds each MMA into
+ * its accumulator rounding toward zero, a systematic shrink of up to one
+ * ulp per instruction (three instructions per k-slice in strict mode), so
+ * shorter chunks are more accurate and read the accumulator more often.
+ * 0 = the default, 8 (128 elements of K).  Measured on the Llama block,
+ * the 4-layer LM and the MLP at full size (gradients against an f64 answer):
+ * within 2.1e-5 at 8, 7.5e-6 at 2 (the step 9.6% slower), 5.3e-6 at 1 (19%
+ * slower), the f32 reference's own arithmetic being 5.5e-6 away.  Graphs
+ * re-plan at their next run.  No reference counterpart. */
+bool tysor_cuda_set_matmul_accumulation(void* context, int kblocks);
 /* Runs the tensor-core pipelines' bounded barrier wait on a barrier that
  * nothing arrives at, giving up after `limit_cycles` (1 to 4e9) SM cycles:
  * returns false with "a tensor-core pipeline wait timed out", and the context

@@ -705,15 +705,18 @@ def _primitive_forward(node, values):
 
 
 def _input_tensor(value, shapes, inputs):
+    """graph_executor.rs:80-93: the parameter's --shape, pattern data (or the
+    given input values) and its annotated dtype string (float32 if none)."""
+    dtype = getattr(value, "dtype", "") or "float32"
     if inputs is not None and value.name in inputs:
         arr = np.ascontiguousarray(np.asarray(inputs[value.name], dtype=_dt()).reshape(-1))
         shape = shapes.get(value.name, [arr.size])
         if _numel(shape) != arr.size:
             raise OracleError(f"input '{value.name}' has {arr.size} values, shape {shape}")
-        return Tensor(list(shape), arr.copy())
+        return Tensor(list(shape), arr.copy(), dtype)
     if value.name not in shapes:
         raise OracleError(f"Missing --shape for tensor parameter '{value.name}'")
-    return synthetic(shapes[value.name])
+    return synthetic(shapes[value.name], dtype)
 
 
 def _forward(graph, shapes, inputs, parameters: Optional[Dict[str, Tensor]]):

@@ -31,6 +31,7 @@ pub mod ffi {
         pub fn tysor_cuda_context_free(context: *mut c_void);
         pub fn tysor_cuda_synchronize(context: *mut c_void) -> bool;
         pub fn tysor_cuda_set_matmul_mode(context: *mut c_void, mode: c_int) -> bool;
+        pub fn tysor_cuda_set_matmul_accumulation(context: *mut c_void, kblocks: c_int) -> bool;
         pub fn tysor_cuda_probe_wait_timeout(context: *mut c_void, limit_cycles: i64) -> bool;
         pub fn tysor_cuda_context_stream(context: *mut c_void) -> *mut c_void;
         pub fn tysor_cuda_buffer_new_with_data(context: *mut c_void, data: *const f32, count: usize) -> *mut c_void;

@@ -34,6 +34,7 @@ def test_run_fixture(cuda_ctx, fx):
     ex = CudaGraphExecutor(cuda_ctx, g, fx.shapes)
     got = ex.run()
     assert got.shape == want.shape
+    assert got.dtype == want.dtype  # the printed dtype string (tensor.rs:48-58)
     close(got.data, want.data, 1e-5)
     ex.close()
 
@@ -48,6 +49,7 @@ def test_backward_fixture(cuda_ctx, fx):
     assert [n for n, _ in got] == [n for n, _ in want]
     for (_, gt), (_, wt) in zip(got, want):
         assert gt.shape == wt.shape
+        assert gt.dtype == wt.dtype
         close(gt.data, wt.data, 1e-5)
     ex.close()
 

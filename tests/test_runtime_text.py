@@ -50,3 +50,22 @@ def test_no_dump_without_a_directory(monkeypatch):
     from tysor_b200.runtime import DUMP_ENV, dump_tensor
     monkeypatch.delenv(DUMP_ENV, raising=False)
     assert dump_tensor("x", HostTensor([1], np.zeros(1, np.float32))) is None
+
+
+def test_fixture_dtype_strings_follow_the_reference_rules():
+    """Every allowlisted fixture declares `tensor[float16]` parameters; the
+    oracle's forward carries that string to the output except where an
+    Embedding (whose builtin constructor declares no dtype) produces the
+    values, and the graph's own dtype pass agrees for every fixture."""
+    import local as L
+    from tysor_b200.programs import FIXTURES
+    seen = set()
+    for fx in FIXTURES.values():
+        g = fx.build()
+        assert all(v.dtype == "float16" for v in g.parameters())
+        if "run" not in fx.modes:
+            continue
+        want, _ = L.run_forward(g, fx.shapes)
+        assert g.value_dtypes()[g.outputs[0]] == want.dtype, fx.name
+        seen.add(want.dtype)
+    assert seen == {"float16", "float32"}  # the transformer fixture starts at an Embedding

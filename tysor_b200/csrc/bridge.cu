@@ -136,7 +136,9 @@ GemmScratch gemm_scratch(Context* c, int batch, int64_t M, int64_t N, int64_t K,
 }
 
 void run_gemm(Context* c, int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
-              const GemmOperand& Bm, const GemmOutput& out, const GemmEpilogue& ep) {
+              const GemmOperand& Bm, const GemmOutput& out, const GemmEpilogue& ep_in) {
+  GemmEpilogue ep = ep_in;
+  ep.chunk_kb = c->accum_chunk_kb;
   GemmScratch s = gemm_scratch(c, batch, M, N, K, A, Bm);
   gemm_launch(batch, M, N, K, A, Bm, out, ep, c->matmul_mode, s, c->d_err, c->stream);
 }
@@ -191,6 +193,13 @@ void tysor_cuda_context_free(void* context) {
 
 bool tysor_cuda_synchronize(void* context) {
   return guarded([&] { ctx_of(context)->sync_and_check(); });
+}
+
+bool tysor_cuda_set_matmul_accumulation(void* context, int kblocks) {
+  return guarded([&] {
+    if (kblocks < 0 || kblocks > 64) throw CudaError("accumulation chunk must be 0 (default) or 1..64 k-blocks");
+    ctx_of(context)->accum_chunk_kb = kblocks;
+  });
 }
 
 bool tysor_cuda_probe_wait_timeout(void* context, int64_t limit_cycles) {

@@ -76,11 +76,13 @@ void wait_comm(ncclComm_t comm, int timeout_ms, const char* what) {
 
 }  // namespace
 
-void comm_allreduce(Context* ctx, float* data, size_t count) {
+void comm_allreduce(Context* ctx, float* data, size_t count) { comm_allreduce_on(ctx, data, count, ctx->stream); }
+
+void comm_allreduce_on(Context* ctx, float* data, size_t count, cudaStream_t stream) {
   if (!ctx->comm) throw CudaError("no communicator: call tysor_cuda_comm_init first");
   if (count == 0) return;
   ncclComm_t comm = (ncclComm_t)ctx->comm;
-  ncclResult_t r = nccl().all_reduce(data, data, count, ncclFloat, ncclSum, comm, ctx->stream);
+  ncclResult_t r = nccl().all_reduce(data, data, count, ncclFloat, ncclSum, comm, stream);
   if (r == ncclInProgress) {
     wait_comm(comm, 60000, "ncclAllReduce");
   } else if (r != ncclSuccess) {

@@ -11,6 +11,18 @@
 
 namespace tysor {
 
+// The low part of x for 3xTF32: x - tf32_trunc(x) (exact in fp32; the
+// tensor core reads x itself as the high part and ignores its low 13 mantissa
+// bits), rounded to the nearest tf32 value, ties to even.  Left unrounded, the
+// tensor core would truncate the low part too, a bias toward zero of about
+// 2^-22 of x on every operand; rounded, it reads the low part exactly and the
+// remaining error (at most 2^-12 of the low part) is unbiased.
+__device__ __forceinline__ float tf32_lo(float x) {
+  const float lo = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  const uint32_t u = __float_as_uint(lo);
+  return __uint_as_float((u + 0x0FFFu + ((u >> 13) & 1u)) & 0xFFFFE000u);
+}
+
 // Kernel launches enqueued by this library (every launcher adds to it).
 extern std::atomic<int64_t> g_launches;
 
@@ -85,6 +97,12 @@ struct GemmEpilogue {
   // Non-null: C = residual + the result (residual in C's layout; a residual
   // connection around a linear).  Only where gemm_fuses_box_epilogue holds.
   const float* residual = nullptr;
+  // Tensor-core kernels: k-blocks (16 elements of K each) accumulated in
+  // tensor memory before the accumulator warps add the partial sum into
+  // fp32 registers with round-to-nearest; 0 = the default (8).  The tensor
+  // core adds each MMA into its accumulator rounding toward zero, so shorter
+  // chunks shrink that systematic error (and cost the readout more often).
+  int chunk_kb = 0;
 };
 
 enum GemmMode : int {
@@ -134,7 +152,7 @@ extern bool g_two_sm_enabled;
 // faulting or hanging the GPU.
 void launch_wait_timeout_probe(int* err, long long limit_cycles, cudaStream_t st);
 
-// lo(x) = x - tf32_trunc(x) over n contiguous elements.
+// lo(x) = tf32_lo(x) (x - tf32_trunc(x), rounded to tf32) over n contiguous elements.
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st);
 // Per batch item b: hi_t[b][c][r] = x[b][r][c] and lo_t = lo(hi_t) (lo_t may
 // be null), for a contiguous [batch][rows][cols] x.

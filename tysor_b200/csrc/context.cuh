@@ -22,6 +22,9 @@ struct Context {
   cudaStream_t stream = nullptr;
   int* d_err = nullptr;  // device error word (DeviceError)
   int matmul_mode = kGemmStrict;
+  // k-blocks per tensor-memory accumulation chunk of the tensor-core
+  // matmuls (GemmEpilogue::chunk_kb; 0 = the default).
+  int accum_chunk_kb = 0;
   // Scratch shared by per-op dispatches (split operands, partial sums).
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
@@ -51,5 +54,7 @@ const char* device_error_message(int code);
 
 // All-reduce (sum) of `count` floats in place on the context stream.
 void comm_allreduce(Context* ctx, float* data, size_t count);
+// The same on another stream of the context's device.
+void comm_allreduce_on(Context* ctx, float* data, size_t count, cudaStream_t stream);
 
 }  // namespace tysor

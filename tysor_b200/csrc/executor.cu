@@ -81,6 +81,9 @@ struct Param {
   Slot* value = nullptr;
   Slot* grad = nullptr;
   bool grad_written = false;
+  // Backward items that must run before the gradient is final (the index
+  // just past the last item that writes it).
+  size_t grad_ready = 0;
   // initialiser: 0 linear weight, 1 linear bias, 2 embedding weight, 3 ones
   int init = 0;
 };
@@ -248,6 +251,13 @@ struct Executor {
         if (b.consumed) cudaEventDestroy(b.consumed);
       }
     if (copy_stream) cudaStreamDestroy(copy_stream);
+    for (Bucket& b : buckets)
+      if (b.ready_ev) cudaEventDestroy(b.ready_ev);
+    if (comm_stream) {
+      cudaStreamSynchronize(comm_stream);
+      cudaStreamDestroy(comm_stream);
+    }
+    if (comm_done) cudaEventDestroy(comm_done);
   }
 
   void release() {
@@ -481,6 +491,7 @@ struct Executor {
     return lo;
   }
   int plan_matmul_mode = kGemmStrict;
+  int plan_accum_chunk = 0;  // the context's accumulation chunk when planned
 
   static bool tma_aligned(int64_t ld, int64_t bs, int batch) {
     return (ld % 4) == 0 && (batch == 1 || (bs % 4) == 0);
@@ -571,6 +582,7 @@ struct Executor {
     }
     Context* cx = ctx;
     const int mode_now = plan_matmul_mode;
+    const int chunk_now = plan_accum_chunk;
     // A residual is added in the GEMM's epilogue where the kernel form has
     // it (operand layouts as prepared); otherwise by a kernel after it.
     const bool res_in_gemm = residual && !acc && tc &&
@@ -586,6 +598,7 @@ struct Executor {
       GemmOperand B{pb.hi->p, pb.trans, pb.ld, pb.bs};
       GemmOutput O{c->p, ldc, sc};
       GemmEpilogue ep{bias ? bias->p : nullptr, alpha, acc ? 1 : 0, relu ? 1 : 0, tri};
+      ep.chunk_kb = chunk_now;
       ep.smx_p = smx_p ? smx_p->p : nullptr;
       if (res_in_gemm) ep.residual = residual->p;
       GemmScratch s{nullptr, nullptr, 0, 0, 1};
@@ -1355,7 +1368,15 @@ struct Executor {
     if (!p.grad) p.grad = alloc((size_t)numel(p.shape));
     bool acc = p.grad_written;
     p.grad_written = true;
+    grads_touched.push_back(name);
     return {p.grad, acc};
+  }
+  // Parameters whose gradient the node being planned writes; its items are
+  // all pushed before the next node is planned.
+  std::vector<std::string> grads_touched;
+  void mark_grads_ready() {
+    for (const std::string& name : grads_touched) params.at(name).grad_ready = backward.size();
+    grads_touched.clear();
   }
 
   // In training a node's output gradient is dead once the node is done, so
@@ -1491,7 +1512,9 @@ struct Executor {
       backward.push_back([=](cudaStream_t st) { launch_fill(s->p, n, 1.0f, st); });
     }
     const bool train = mode == kModeTrain;
+    grads_touched.clear();
     for (auto it = nodes.rbegin(); it != nodes.rend(); ++it) {
+      mark_grads_ready();
       const GNode& node = *it;
       cur_label = "bwd " + node_label(node);
       given_g = nullptr;
@@ -1614,6 +1637,7 @@ struct Executor {
         case kNApply: plan_apply_backward(node, g, out, n, train); break;
       }
     }
+    mark_grads_ready();
   }
 
   void plan_call_backward(const GNode& node, Slot* g, const HVal& out, int64_t n, bool train) {
@@ -1824,8 +1848,10 @@ struct Executor {
   // ---- update planning (train) ------------------------------------------------------
   void plan_update() {
     cur_label = "update (loss, all-reduce, sgd)";
-    // The loss (sum of the objective) is computed before the update, from
-    // the forward values of this step (executor.rs:803-811).
+    // The loss (sum of the objective) comes from this step's forward values
+    // (executor.rs:803-811); it is reduced before the backward starts, so
+    // that it can travel with the first gradient bucket of a data-parallel
+    // step.
     const HVal& obj = val(objective);
     const int64_t n = numel(obj.shape);
     Slot* o = obj.slot;
@@ -1833,15 +1859,20 @@ struct Executor {
     need_scratch(1024);
     Slot** scr = &scratch;
     const int* order = &loss_order;
-    update.push_back([=](cudaStream_t st) {
+    backward.fns.insert(backward.fns.begin(), [=](cudaStream_t st) {
       if (*order == 1) launch_sequential_sum(o->p, (*ls)->p, n, st);
       else launch_reduce_sum(o->p, (*ls)->p, (*scr)->p, n, st);
     });
-    Context* cx = ctx;
-    Slot** gb = &grad_block;
-    update.push_back([=, this](cudaStream_t st) {
-      (void)st;
-      if (allreduce && (*gb)->n > 0) comm_allreduce(cx, (*gb)->p, (*gb)->n);
+    backward.labels.insert(backward.labels.begin(), "bwd loss (sum of the objective)");
+    for (auto& [name, p] : params) (void)name, p.grad_ready += 1;
+    // Data parallel: the gradient buckets are all-reduced on the comm stream
+    // as the backward finishes them (see place_buckets); the update waits
+    // for the last one.
+    update.push_back([this](cudaStream_t st) {
+      if (allreduce && !buckets.empty()) {
+        TYSOR_CUDA(cudaEventRecord(comm_done, comm_stream));
+        TYSOR_CUDA(cudaStreamWaitEvent(st, comm_done, 0));
+      }
     });
     // One SGD pass over all parameters when they sit in one block laid out
     // like the gradient block (each element's update is the same p - lr * g;
@@ -1850,8 +1881,11 @@ struct Executor {
       Slot **pb = &param_block, **gbl = &grad_block;
       size_t* pn = &param_block_n;
       float* lr_ptr = &lr_f;
+      // The gradient block starts with the loss and its padding (64
+      // floats); the parameters' gradients follow in the parameter block's
+      // order.
       update.push_back([=](cudaStream_t st) {
-        if (*pn > 0) launch_sgd((*pb)->p, (*gbl)->p, *lr_ptr, (int64_t)*pn, st);
+        if (*pn > 0) launch_sgd((*pb)->p, (*gbl)->p + kLossFloats, *lr_ptr, (int64_t)*pn, st);
       });
       return;
     }
@@ -1867,6 +1901,21 @@ struct Executor {
     }
   }
   float lr_f = 0.01f;
+  // The loss's slot at the head of the gradient block, padded like every
+  // slot to 64 floats.
+  static constexpr size_t kLossFloats = 64;
+  // Data-parallel gradient buckets: contiguous ranges of the gradient block
+  // (laid out in the order the backward finishes the gradients), each
+  // all-reduced on comm_stream once the backward item that completes it has
+  // run.
+  struct Bucket {
+    size_t begin = 0, count = 0;  // floats of the gradient block
+    size_t ready = 0;             // backward items that must run first
+    cudaEvent_t ready_ev = nullptr;
+  };
+  std::vector<Bucket> buckets;
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t comm_done = nullptr;
   // 0: tree sum of the objective (default); 1: the reference's sequential f32
   // sum in index order (tysor_cuda_graph_set_loss_order).
   int loss_order = 0;
@@ -1884,22 +1933,35 @@ struct Executor {
   }
 
   // ---- arena layout --------------------------------------------------------------------
+  // Trained parameters in the order the backward finishes their gradients
+  // (ties in parameter order): the gradient and parameter blocks follow it,
+  // so each all-reduce bucket is one contiguous range.
+  std::vector<std::string> grad_order() const {
+    std::vector<std::string> names;
+    for (const std::string& name : param_order)
+      if (params.at(name).grad) names.push_back(name);
+    std::stable_sort(names.begin(), names.end(), [this](const std::string& a, const std::string& b) {
+      return params.at(a).grad_ready < params.at(b).grad_ready;
+    });
+    return names;
+  }
+
   void layout() {
-    // Parameter gradients and the loss share one contiguous block so that a
-    // data-parallel step all-reduces them with one collective.
+    // The loss and the parameter gradients share one contiguous block so
+    // that a data-parallel step all-reduces them in a few bucketed
+    // collectives (the loss first: it is reduced before the backward).
     size_t gtotal = 0;
     std::vector<Slot*> gslots;
-    for (const std::string& name : param_order) {
-      Param& p = params.at(name);
-      if (p.grad) {
-        gslots.push_back(p.grad);
-        gtotal += (p.grad->n + 63) & ~(size_t)63;
-      }
-    }
     if (mode == kModeTrain) {
       loss = alloc(1);
       gslots.push_back(loss);
-      gtotal += 64;
+      gtotal += kLossFloats;
+    }
+    const std::vector<std::string> gorder = grad_order();
+    for (const std::string& name : gorder) {
+      Param& p = params.at(name);
+      gslots.push_back(p.grad);
+      gtotal += (p.grad->n + 63) & ~(size_t)63;
     }
     scratch = alloc(scratch_floats + 64);
     size_t total = 0;
@@ -1914,9 +1976,8 @@ struct Executor {
     // then the trained parameters, in the same order and padding
     const bool pblock = mode == kModeTrain && params_in_block();
     if (pblock) {
-      for (const std::string& name : param_order) {
+      for (const std::string& name : gorder) {
         Param& p = params.at(name);
-        if (!p.grad) continue;
         off[p.value] = total;
         total += (p.value->n + 63) & ~(size_t)63;
       }
@@ -1944,14 +2005,87 @@ struct Executor {
         param_block = &slots.back();
         param_block_n = pb_end - gb_end;
       }
+      place_buckets(gorder, off);
     }
   }
 
+  // Cuts the gradient block into buckets of at least bucket_floats() (the
+  // last may be smaller) and inserts, after the backward item that completes
+  // each bucket, an item that (when data parallel) hands it to comm_stream:
+  // an event on the compute stream, a wait on the comm stream, the NCCL
+  // all-reduce there.  The collectives thus overlap the rest of the
+  // backward; every rank issues the same buckets in the same order.
+  void place_buckets(const std::vector<std::string>& gorder, const std::map<Slot*, size_t>& off) {
+    for (Bucket& b : buckets)
+      if (b.ready_ev) cudaEventDestroy(b.ready_ev);
+    buckets.clear();
+    const size_t target = bucket_floats();
+    Bucket cur;
+    cur.begin = 0;
+    cur.ready = 1;  // the loss item
+    size_t end = kLossFloats;  // the loss and its padding
+    for (const std::string& name : gorder) {
+      const Param& p = params.at(name);
+      end = off.at(p.grad) + ((p.grad->n + 63) & ~(size_t)63);
+      cur.ready = std::max(cur.ready, p.grad_ready);
+      if (end - cur.begin >= target) {
+        cur.count = end - cur.begin;
+        buckets.push_back(cur);
+        cur = Bucket();
+        cur.begin = end;
+      }
+    }
+    if (end > cur.begin) {
+      cur.count = end - cur.begin;
+      buckets.push_back(cur);
+    }
+    for (Bucket& b : buckets) TYSOR_CUDA(cudaEventCreateWithFlags(&b.ready_ev, cudaEventDisableTiming));
+    if (!comm_done) TYSOR_CUDA(cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming));
+    if (!comm_stream) {
+      int lo = 0, hi = 0;
+      TYSOR_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+      TYSOR_CUDA(cudaStreamCreateWithPriority(&comm_stream, cudaStreamNonBlocking, hi));
+    }
+    // Rebuild the backward list with the bucket hand-offs in place.
+    StepList out{{}, {}, backward.cur};
+    size_t next = 0;
+    for (size_t i = 0; i <= backward.fns.size(); ++i) {
+      while (next < buckets.size() && buckets[next].ready == i) {
+        const size_t k = next++;
+        out.fns.push_back([this, k](cudaStream_t st) {
+          if (!allreduce) return;
+          Bucket& b = buckets[k];
+          TYSOR_CUDA(cudaEventRecord(b.ready_ev, st));
+          TYSOR_CUDA(cudaStreamWaitEvent(comm_stream, b.ready_ev, 0));
+          comm_allreduce_on(ctx, grad_block->p + b.begin, b.count, comm_stream);
+        });
+        out.labels.push_back("bwd all-reduce bucket " + std::to_string(k) + " (" +
+                             std::to_string(buckets[k].count * 4 / (1 << 20)) + " MB)");
+      }
+      if (i < backward.fns.size()) {
+        out.fns.push_back(std::move(backward.fns[i]));
+        out.labels.push_back(std::move(backward.labels[i]));
+      }
+    }
+    backward.fns = std::move(out.fns);
+    backward.labels = std::move(out.labels);
+  }
+
+  // Bucket size: TYSOR_CUDA_BUCKET_MB (default 64 MB), read when planning.
+  static size_t bucket_floats() {
+    const char* v = getenv("TYSOR_CUDA_BUCKET_MB");
+    long mb = v ? atol(v) : 64;
+    if (mb < 1) mb = 1;
+    return (size_t)mb * (1 << 20) / sizeof(float);
+  }
+
   void plan(int m) {
-    if (!dirty && mode == m && plan_matmul_mode == ctx->matmul_mode) return;
+    if (!dirty && mode == m && plan_matmul_mode == ctx->matmul_mode && plan_accum_chunk == ctx->accum_chunk_kb)
+      return;
     release();
     mode = m;
     plan_matmul_mode = ctx->matmul_mode;
+    plan_accum_chunk = ctx->accum_chunk_kb;
     build_uses();
     plan_forward();
     if (mode != kModeRun) plan_backward();

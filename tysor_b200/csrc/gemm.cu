@@ -187,6 +187,8 @@ struct PipeCfg {
 // buffer.  The error stays at the chunk level (about 1.4e-6 relative in
 // strict mode) whatever K is.
 constexpr int kChunkKb = 8;
+
+__device__ __forceinline__ int chunk_kb(const GemmEpilogue& ep) { return ep.chunk_kb > 0 ? ep.chunk_kb : kChunkKb; }
 constexpr int kAccWarps = 8;
 constexpr int kThreadsTC = 64 + 32 * kAccWarps;
 
@@ -354,7 +356,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   int kb_begin = 0, kb_end = (K + BK - 1) / BK;
   if (ep.tri != 0 && causal_range(ep.tri, m0, BM, n0, &kb_begin, &kb_end)) return;  // tile not needed
   const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
-  const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
+  const int ckb = chunk_kb(ep);
+  const int nchunks = (num_kb + ckb - 1) / ckb;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -411,12 +414,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: chunk c accumulates into tensor-memory buffer c & 1.
+    int chunk = 0, cpos = 0;  // chunk index, k-block within the chunk
     for (int kb = 0; kb < num_kb && ok; ++kb) {
       const int s = kb % kStages;
-      const int chunk = kb / kChunkKb;
       const int buf = chunk & 1;
-      const bool first = (kb % kChunkKb) == 0;
-      const bool last = (kb % kChunkKb) == kChunkKb - 1 || kb == num_kb - 1;
+      const bool first = cpos == 0;
+      const bool last = cpos == ckb - 1 || kb == num_kb - 1;
       if (first && chunk >= 2) {
         ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((chunk >> 1) - 1) & 1, err);
         if (!ok) break;
@@ -445,7 +448,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
       }
       umma_commit(smem_u32(&empty_bar[s]));
-      if (last) umma_commit(smem_u32(&tfull_bar[buf]));
+      if (last) {
+        umma_commit(smem_u32(&tfull_bar[buf]));
+        ++chunk;
+        cpos = 0;
+      } else {
+        ++cpos;
+      }
     }
   }
   __syncwarp();
@@ -633,7 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
   // before any cluster barrier, when the tile is not needed).
   if (ep.tri != 0 && causal_range(ep.tri, m0 - (int)rank * BM, 2 * BM, n0, &kb_begin, &kb_end)) return;
   const int num_kb = kb_end > kb_begin ? kb_end - kb_begin : 0;
-  const int nchunks = (num_kb + kChunkKb - 1) / kChunkKb;
+  const int ckb = chunk_kb(ep);
+  const int nchunks = (num_kb + ckb - 1) / ckb;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -690,12 +700,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 1 && lane == 0 && leader) {
     // MMA issuer (even CTA only): M=256 over both CTAs' operands.
+    int chunk = 0, cpos = 0;  // chunk index, k-block within the chunk
     for (int kb = 0; kb < num_kb && ok; ++kb) {
       const int s = kb % kStages;
-      const int chunk = kb / kChunkKb;
       const int buf = chunk & 1;
-      const bool first = (kb % kChunkKb) == 0;
-      const bool last = (kb % kChunkKb) == kChunkKb - 1 || kb == num_kb - 1;
+      const bool first = cpos == 0;
+      const bool last = cpos == ckb - 1 || kb == num_kb - 1;
       if (first && chunk >= 2) {
         ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((chunk >> 1) - 1) & 1, err);
         if (!ok) break;
@@ -723,7 +733,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
         }
       }
       umma_commit_pair(smem_u32(&empty_bar[s]));
-      if (last) umma_commit_pair(smem_u32(&tfull_bar[buf]));
+      if (last) {
+        umma_commit_pair(smem_u32(&tfull_bar[buf]));
+        ++chunk;
+        cpos = 0;
+      } else {
+        ++cpos;
+      }
     }
   }
   __syncwarp();
@@ -780,7 +796,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
 //
 // kConvA (strict mode): the low part of A is made in shared memory instead
 // of being loaded.  Each CTA's A tile lands on a barrier of its own
-// ("A full"); two converter warps per CTA write lo = a - tf32_trunc(a) beside
+// ("A full"); two converter warps per CTA write lo = tf32_lo(a) beside
 // it, in the same swizzled positions, and arrive on the even CTA's
 // "converted" barrier, which the MMA issuer waits for besides "full".  The
 // A stream read from HBM halves and no split pass over A runs; the two
@@ -1019,18 +1035,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     }
   } else if (warp == 1 && lane == 0 && leader) {
     // MMA issuer (even CTA): stage counter and chunk counter across tiles.
-    uint32_t it = 0, ch = 0;
+    const int ckb = chunk_kb(ep);
+    uint32_t it = 0, gch = 0;  // stages and chunks issued so far (all tiles)
     for (int t = cluster; t < total && ok; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
       if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
         continue;
       const int nkb = kb1 - kb0;
+      int cpos = 0;  // k-block within the chunk
       for (int j = 0; j < nkb && ok; ++j, ++it) {
         const int s = (int)(it % kStages);
-        const uint32_t gch = ch + (uint32_t)(j / kChunkKb);
         const int buf = (int)(gch & 1);
-        const bool first = (j % kChunkKb) == 0;
-        const bool last = (j % kChunkKb) == kChunkKb - 1 || j == nkb - 1;
+        const bool first = cpos == 0;
+        const bool last = cpos == ckb - 1 || j == nkb - 1;
         if (first && gch >= 2) {
           ok = mbar_wait(smem_u32(&tempty_bar[buf]), ((gch >> 1) - 1) & 1, err);
           if (!ok) break;
@@ -1064,9 +1081,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
           }
         }
         umma_commit_pair(smem_u32(&empty_bar[s]));
-        if (last) umma_commit_pair(smem_u32(&tfull_bar[buf]));
+        if (last) {
+          umma_commit_pair(smem_u32(&tfull_bar[buf]));
+          ++gch;
+          cpos = 0;
+        } else {
+          ++cpos;
+        }
       }
-      ch += (uint32_t)((nkb + kChunkKb - 1) / kChunkKb);
     }
   } else if (kConvA && warp >= 2 + kAccWarps) {
     // Converter warps (both CTAs): the low part of each landed A tile,
@@ -1089,10 +1111,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
 #pragma unroll
         for (int i = 0; i < kPer; ++i)
           st_shared_f4(hi + (uint32_t)kA + (uint32_t)(ct + 64 * i) * 16u,
-                       v[i].x - __uint_as_float(__float_as_uint(v[i].x) & 0xFFFFE000u),
-                       v[i].y - __uint_as_float(__float_as_uint(v[i].y) & 0xFFFFE000u),
-                       v[i].z - __uint_as_float(__float_as_uint(v[i].z) & 0xFFFFE000u),
-                       v[i].w - __uint_as_float(__float_as_uint(v[i].w) & 0xFFFFE000u));
+                       tf32_lo(v[i].x),
+                       tf32_lo(v[i].y),
+                       tf32_lo(v[i].z),
+                       tf32_lo(v[i].w));
         // Generic-proxy writes made visible to the tensor core's reads.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -1129,7 +1151,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         }
         y_pending += kBoxes < 2 ? kBoxes : 2;
       }
-      const int nch = (kb1 - kb0 + kChunkKb - 1) / kChunkKb;
+      const int nch = (kb1 - kb0 + chunk_kb(ep) - 1) / chunk_kb(ep);
       float acc[kHalf];
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
@@ -1261,7 +1283,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   }
 }
 
-// lo(x) = x - tf32_trunc(x), elementwise over a contiguous span.
+// lo(x) = tf32_lo(x), elementwise over a contiguous span.
 __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n >> 2;
   const float4* x4 = (const float4*)x;
@@ -1270,16 +1292,16 @@ __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__
        i += (int64_t)gridDim.x * blockDim.x) {
     float4 v = x4[i];
     float4 r;
-    r.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    r.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    r.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    r.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    r.x = tf32_lo(v.x);
+    r.y = tf32_lo(v.y);
+    r.z = tf32_lo(v.z);
+    r.w = tf32_lo(v.w);
     lo4[i] = r;
   }
   for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float v = x[i];
-    lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    lo[i] = tf32_lo(v);
   }
 }
 
@@ -1303,7 +1325,7 @@ __global__ void split_transpose_kernel(const float* __restrict__ x, float* __res
     if (r < rows && c < cols) {
       const float v = tile[threadIdx.x][i];
       hb[c * rows + r] = v;
-      if (lb) lb[c * rows + r] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+      if (lb) lb[c * rows + r] = tf32_lo(v);
     }
   }
 }
@@ -1350,10 +1372,10 @@ __global__ void __launch_bounds__(256) split_transpose64_kernel(const float* __r
       *(float4*)(hb + c * rows + r) = v;
       if (lb) {
         float4 l;
-        l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-        l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-        l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-        l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        l.x = tf32_lo(v.x);
+        l.y = tf32_lo(v.y);
+        l.z = tf32_lo(v.z);
+        l.w = tf32_lo(v.w);
         *(float4*)(lb + c * rows + r) = l;
       }
     }

@@ -16,7 +16,7 @@ constexpr int kThreads = 256;
 __device__ __forceinline__ bool aligned16(const void* p) { return (((uintptr_t)p) & 15) == 0; }
 
 // x - tf32(x): the low part a strict 3xTF32 GEMM multiplies separately.
-__device__ __forceinline__ float lo_part(float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ float lo_part(float x) { return tf32_lo(x); }
 __device__ __forceinline__ float4 lo_part4(float4 v) {
   return make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
 }

@@ -42,6 +42,10 @@ class Value:
     kind: str
     is_parameter: bool = False
     name: str = ""
+    # A tensor parameter's annotated dtype (`x: tensor[float16]`); "" when
+    # unannotated.  The string is carried and printed, never computed in:
+    # every tensor is f32 (runtime/tensor.rs:3-8).
+    dtype: str = ""
 
 
 @dataclass
@@ -80,6 +84,33 @@ class Graph:
         if not self.outputs:
             raise ValueError("Graph does not have a return value")
         return self.outputs[0]
+
+    def value_dtypes(self) -> Dict[int, str]:
+        """The dtype string each tensor value carries in the reference's local
+        executor: a parameter its annotation or "float32"
+        (graph_executor.rs:90-93); an embedding lookup the constructor's
+        declared return dtype, which builtin constructors leave unset, so
+        "float32" (graph_executor.rs:208-213, compiler/builtins/registry.rs);
+        `scalar op tensor` the tensor's (tensor.rs:149); every other op its
+        first tensor operand's (tensor.rs:121-258, layers.rs:127-322)."""
+        dt: Dict[int, str] = {}
+        for v in self.values:
+            if v.is_parameter and v.kind == "tensor":
+                dt[v.id] = v.dtype or "float32"
+        ctors: Dict[int, str] = {}
+        for n in self.nodes:
+            if n.kind == "ctor":
+                ctors[n.output] = n.op
+                continue
+            if n.kind == "apply":
+                out = "float32" if ctors.get(n.inputs[0]) == "Embedding" else dt.get(n.inputs[1])
+            elif n.kind in ("binary", "primitive", "call"):
+                out = next((dt[i] for i in n.inputs if i in dt), None)
+            else:
+                out = None
+            if out is not None:
+                dt[n.output] = out
+        return dt
 
     def producer(self, value_id: int) -> Optional[Node]:
         for node in self.nodes:
@@ -130,8 +161,9 @@ class GraphBuilder:
     constant arguments before the call that consumes them.
     """
 
-    def __init__(self, name: str = "model"):
+    def __init__(self, name: str = "model", param_dtype: str = ""):
         self.g = Graph(name=name)
+        self.param_dtype = param_dtype
 
     # values
     def _value(self, kind: str, name: str = "", is_parameter: bool = False) -> Ref:
@@ -141,9 +173,12 @@ class GraphBuilder:
             self.g.named[name] = vid
         return Ref(vid)
 
-    def param(self, name: str) -> Ref:
-        """A function parameter (always a tensor on the hot path)."""
-        return self._value("tensor", name, True)
+    def param(self, name: str, dtype: Optional[str] = None) -> Ref:
+        """A function parameter (always a tensor on the hot path); `dtype` is
+        its annotation (default: the builder's param_dtype)."""
+        ref = self._value("tensor", name, True)
+        self.g.values[ref].dtype = self.param_dtype if dtype is None else dtype
+        return ref
 
     def _arg(self, a: Arg) -> Ref:
         if isinstance(a, Ref):

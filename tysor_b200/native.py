@@ -32,6 +32,7 @@ SIGNATURES = {
     "tysor_cuda_set_matmul_mode": (c_bool, [V, c_int]),
     "tysor_cuda_context_stream": (V, [V]),
     "tysor_cuda_probe_wait_timeout": (c_bool, [V, c_int64]),
+    "tysor_cuda_set_matmul_accumulation": (c_bool, [V, c_int]),
     "tysor_cuda_buffer_new_with_data": (V, [V, FP, c_size_t]),
     "tysor_cuda_buffer_new_zeroed": (V, [V, c_size_t]),
     "tysor_cuda_buffer_free": (None, [V]),

@@ -31,8 +31,13 @@ class Fixture:
 
 # ---- reference fixtures ----------------------------------------------------
 
+# Every allowlisted fixture declares its parameters `tensor[float16]`; the
+# string is carried into the printed results (computation stays f32).
+FIXTURE_DTYPE = "float16"
+
+
 def _model_matmul_relu() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x, w = b.param("x"), b.param("w")
     y = b.let("y", b.call("matmul", x, w))
     z = b.let("z", b.call("relu", y))
@@ -41,7 +46,7 @@ def _model_matmul_relu() -> Graph:
 
 
 def _run_activation_layers() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     sm = b.ctor("Softmax")
     si = b.ctor("SiLU")
@@ -50,7 +55,7 @@ def _run_activation_layers() -> Graph:
 
 
 def _run_binary_ops() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x, y = b.param("x"), b.param("y")
     s = b.let("sum", b.binary("+", x, y))
     d = b.let("diff", b.binary("-", s, y))
@@ -61,14 +66,14 @@ def _run_binary_ops() -> Graph:
 
 
 def _run_cross_entropy() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     lg, t = b.param("logits"), b.param("target")
     b.ret(b.call("cross_entropy", lg, t))
     return b.build()
 
 
 def _run_dropout() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     drop = b.let("drop", b.ctor("Dropout", 0.25))
     b.ret(b.apply(drop, x))
@@ -76,7 +81,7 @@ def _run_dropout() -> Graph:
 
 
 def _run_linear_bias() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     proj = b.let("proj", b.ctor("linear", 3, 2, True))
     b.ret(b.apply(proj, x))
@@ -98,21 +103,21 @@ def _transformer(b: GraphBuilder, idx, mask: bool):
 
 
 def _run_transformer_mask() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     idx = b.param("idx")
     b.ret(_transformer(b, idx, True))
     return b.build()
 
 
 def _run_rms_norm() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     b.ret(b.call("rms_norm", x, 3))
     return b.build()
 
 
 def _run_scale_builtin() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     y = b.let("y", b.call("scale", x, 2.0))
     z = b.let("z", b.call("relu", y))
@@ -121,7 +126,7 @@ def _run_scale_builtin() -> Graph:
 
 
 def _run_two_layer_mlp() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     hidden = b.let("hidden", b.ctor("linear", 3, 4))
     out = b.let("out", b.ctor("linear", 4, 2, False))
@@ -130,7 +135,7 @@ def _run_two_layer_mlp() -> Graph:
 
 
 def _backward_basic_ops() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x, y, w = b.param("x"), b.param("y"), b.param("w")
     prod = b.let("prod", b.binary("*", x, y))
     logits = b.let("logits", b.call("matmul", prod, w))
@@ -141,7 +146,7 @@ def _backward_basic_ops() -> Graph:
 
 
 def _backward_cross_entropy() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     lg, t = b.param("logits"), b.param("target")
     b.ret(b.let("loss", b.call("cross_entropy", lg, t)))
     b.train(objective="loss", lr=0.1)
@@ -149,7 +154,7 @@ def _backward_cross_entropy() -> Graph:
 
 
 def _backward_dropout() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     drop = b.let("drop", b.ctor("Dropout", 0.25))
     b.ret(b.let("y", b.apply(drop, x)))
@@ -159,7 +164,7 @@ def _backward_dropout() -> Graph:
 
 def _backward_linear(bias: bool) -> Callable[[], Graph]:
     def build() -> Graph:
-        b = GraphBuilder()
+        b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
         x = b.param("x")
         proj = b.let("proj", b.ctor("linear", 3, 2, bias))
         b.ret(b.let("y", b.apply(proj, x)))
@@ -169,7 +174,7 @@ def _backward_linear(bias: bool) -> Callable[[], Graph]:
 
 
 def _backward_rms_norm() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x = b.param("x")
     b.ret(b.let("y", b.call("rms_norm", x, 3)))
     b.train(objective="y", lr=0.1)
@@ -178,7 +183,7 @@ def _backward_rms_norm() -> Graph:
 
 def _backward_act(op: str) -> Callable[[], Graph]:
     def build() -> Graph:
-        b = GraphBuilder()
+        b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
         x = b.param("x")
         b.ret(b.let("y", b.apply(b.ctor(op), x)))
         b.train(objective="y", lr=0.1)
@@ -188,7 +193,7 @@ def _backward_act(op: str) -> Callable[[], Graph]:
 
 def _train_linear_ce(bias: bool, iterations: int) -> Callable[[], Graph]:
     def build() -> Graph:
-        b = GraphBuilder()
+        b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
         x, t = b.param("x"), b.param("target")
         proj = b.let("proj", b.ctor("linear", 3, 3, bias))
         logits = b.let("logits", b.apply(proj, x))
@@ -199,7 +204,7 @@ def _train_linear_ce(bias: bool, iterations: int) -> Callable[[], Graph]:
 
 
 def _train_dropout() -> Graph:
-    b = GraphBuilder()
+    b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
     x, t = b.param("x"), b.param("target")
     proj = b.let("proj", b.ctor("linear", 3, 3, False))
     drop = b.let("drop", b.ctor("Dropout", 0.25))
@@ -211,7 +216,7 @@ def _train_dropout() -> Graph:
 
 def _train_transformer(mask: bool) -> Callable[[], Graph]:
     def build() -> Graph:
-        b = GraphBuilder()
+        b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
         idx, t = b.param("idx"), b.param("target")
         logits = _transformer(b, idx, mask)
         b.ret(b.let("loss", b.call("cross_entropy", logits, t)))
@@ -222,7 +227,7 @@ def _train_transformer(mask: bool) -> Callable[[], Graph]:
 
 def _train_mlp(act: str) -> Callable[[], Graph]:
     def build() -> Graph:
-        b = GraphBuilder()
+        b = GraphBuilder(param_dtype=FIXTURE_DTYPE)
         x, t = b.param("x"), b.param("target")
         hidden = b.let("hidden", b.ctor("linear", 3, 4, False))
         out = b.let("out", b.ctor("linear", 4, 3, False))

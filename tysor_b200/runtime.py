@@ -49,6 +49,11 @@ class CudaContext:
     def _adopt(self, child) -> None:
         self._children.add(child)
 
+    def set_matmul_accumulation(self, kblocks: int) -> None:
+        """k-blocks (16 elements of K) per tensor-memory accumulation chunk;
+        0 = the default (8).  Shorter is more accurate and slower."""
+        check(native.lib().tysor_cuda_set_matmul_accumulation(self.handle, int(kblocks)), "set_matmul_accumulation")
+
     def set_matmul_mode(self, mode: str) -> None:
         check(self._lib.tysor_cuda_set_matmul_mode(self.handle, MATMUL_MODES[mode]), "set_matmul_mode")
 
@@ -146,6 +151,10 @@ class CudaGraphExecutor:
         self._lib = native.lib()
         self.handle = self._lib.tysor_cuda_graph_new(ctx.handle, graph.to_text().encode())
         check(self.handle, "graph_new")
+        # dtype strings carried with the values (computation is f32);
+        # gradients carry the objective's (the ones seed's, backward.rs:178).
+        self._dtypes = graph.value_dtypes()
+        self._grad_dtype = self._dtypes.get(graph.objective_id(), "float32") if graph.outputs else "float32"
         # host arrays of queued prefetches (at most two wait per input, one
         # more may still be copying)
         self._prefetched: Dict[str, collections.deque] = {}
@@ -237,14 +246,14 @@ class CudaGraphExecutor:
         s = self.shape(value_id)
         out = np.empty(int(np.prod(s, dtype=np.int64)), dtype=np.float32)
         check(self._lib.tysor_cuda_graph_read_value(self.handle, int(value_id), fptr(out), out.size), "read_value")
-        return HostTensor(s, out)
+        return HostTensor(s, out, self._dtypes.get(int(value_id), "float32"))
 
     def value_grad(self, value_id: int) -> Optional[HostTensor]:
         s = self.shape(value_id)
         out = np.empty(int(np.prod(s, dtype=np.int64)), dtype=np.float32)
         if not self._lib.tysor_cuda_graph_read_value_grad(self.handle, int(value_id), fptr(out), out.size):
             return None
-        return HostTensor(s, out)
+        return HostTensor(s, out, self._grad_dtype)
 
     def parameter_names(self) -> List[str]:
         n = self._lib.tysor_cuda_graph_num_parameters(self.handle)
