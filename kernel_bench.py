@@ -121,7 +121,7 @@ def time_calls(ctx, stream, call, reps: int, warmup: int) -> float:
 
 def measured_peaks():
     import os
-    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             pk = json.load(f)

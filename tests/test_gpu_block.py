@@ -152,29 +152,50 @@ def test_traced_step_reports_every_item_and_matches_a_plain_step(cuda_ctx):
     ex.close()
 
 
-@pytest.mark.parametrize("seq", [256, 1024, 2048])
-def test_fused_causal_attention_refuses_rows_whose_masked_entries_keep_probability(cuda_ctx, seq):
-    """The causal GEMM skipping treats masked probabilities as exact zeros,
-    which holds unless a row's scores are all below about -9896 (then
-    exp(-1e4 - max) is not zero).  Such inputs are reported as an error, not
-    computed wrongly (one block per row at 256; one or two warps per row at
-    1024 and 2048)."""
-    from tysor_b200 import native
+@pytest.mark.parametrize("seq", [200, 256, 1024, 2048])
+def test_fused_causal_attention_rows_whose_masked_entries_keep_probability(cuda_ctx, seq):
+    """The causal GEMMs skip masked entries as exact zeros, which they are
+    unless a row's visible scores all lie below about -9896: then every
+    masked entry keeps probability exp(-1e4 - max) / d (here 1 / #masked).
+    Such rows are computed as the reference computes them: the softmax
+    records each row's masked probability and fix-ups after P.V and after
+    dV add the skipped terms.  Head 0 has ordinary scores.  In head 1 every
+    key is the constant 60 and the first half of the queries the constant
+    -60 (scores -19584: those rows leak, their visible entries get
+    probability 0 and every masked one 1 / #masked), the second half
+    ordinary (each row's scores equal across keys); constant operands keep
+    the scores exact, so the check is not swamped by the conditioning of
+    softmax at scores of -2e4.  Probabilities, output and the gradients
+    reaching q, k and v against the op-by-op oracle.  (At 200 tokens the
+    GEMMs take 128-row tiles, at 256 and more 256-row pair tiles.)"""
     from tysor_b200.graph import GraphBuilder
     from tysor_b200.runtime import CudaGraphExecutor
     b = GraphBuilder()
     q, k, v = b.param("q"), b.param("k"), b.param("v")
     s = b.call("scale", b.call("matmul", q, b.call("transpose", k, 2, 3)), 0.17)
-    p = b.apply(b.ctor("Softmax"), b.call("causal_mask", s))
-    b.ret(b.let("out", b.call("matmul", p, v)))
+    p = b.let("p", b.apply(b.ctor("Softmax"), b.call("causal_mask", s)))
+    out = b.let("out", b.call("matmul", p, v))
+    b.ret(out)
     b.train(objective="out", lr=0.0)
     g = b.build()
-    shape = [1, 1, seq, 32]
-    ins = {"q": np.full(shape, -100.0, np.float32), "k": np.full(shape, 100.0, np.float32),
-           "v": np.ones(shape, np.float32)}
-    ex = CudaGraphExecutor(cuda_ctx, g, {n: shape for n in ins}, inputs=ins)
-    with pytest.raises(native.NativeError, match="fused causal attention"):
-        ex.train(1, 0.0)
+    shape = [1, 2, seq, 32]
+    rng = np.random.default_rng(seq)
+    ins = {n: rng.standard_normal(shape).astype(np.float32) for n in ("q", "k", "v")}
+    ins["k"][0, 1] = 60.0
+    ins["q"][0, 1, : seq // 2] = -60.0
+    shapes = {n: shape for n in ins}
+    vgrads = {}
+    L.set_threads(16)
+    values, _, _ = L.train_step_grads(g, shapes, inputs=ins, value_grads=vgrads)
+    want_p = values[g.named["p"]][1].data.reshape(shape[:2] + [seq, seq])
+    assert want_p[0, 1, 0, 1] > 0.0  # the second head's rows do leak
+    ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs=ins)
+    ex.train(1, 0.0)
+    assert frob(ex.value(g.named["p"]).data, values[g.named["p"]][1].data) < 1e-5
+    assert frob(ex.value(out).data, values[out][1].data) < 1e-5
+    for name in ("q", "k", "v"):
+        vid = g.named[name]
+        assert frob(ex.value_grad(vid).data, vgrads[vid].data) < 1e-5, name
     ex.close()
 
 

@@ -27,9 +27,6 @@ const char* device_error_message(int code) {
     case kErrIndexRange: return "Embedding index out of range";
     case kErrBarrierTimeout: return "a tensor-core pipeline wait timed out";
     case kErrTmemAlloc: return "tensor memory allocation failed";
-    case kErrCausalSkip:
-      return "fused causal attention: a masked score row kept a nonzero probability (scores below -9896); "
-             "the causal GEMM skipping is not valid for these inputs";
     default: return "unknown device error";
   }
 }

@@ -34,7 +34,6 @@ enum DeviceError : int {
   kErrIndexRange = 1,      // embedding / label index outside [0, n)
   kErrBarrierTimeout = 2,  // an mbarrier wait ran past its time limit
   kErrTmemAlloc = 3,
-  kErrCausalSkip = 4,      // a fused causal softmax row gave a masked entry a nonzero probability
 };
 
 struct CudaError : std::runtime_error {
@@ -163,6 +162,13 @@ void launch_split_transpose(const float* x, float* hi_t, float* lo_t, int64_t ba
 // mode (0 when the call runs on the CUDA-core path).
 void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
                        const GemmOperand& B, int mode, int64_t* a_elems, int64_t* b_elems);
+
+// Rows per tile of the causal ranges (GemmEpilogue::tri) gemm_launch would
+// use for this GEMM: with tri 2 a row's contraction ends at the end of its
+// tile of this many rows (rounded up to 16), with tri 3 it starts at the
+// start of its tile.  0: the CUDA-core path, which contracts all of K.
+int gemm_causal_tile_rows(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
+                          const GemmOutput& C, int mode);
 
 // Launches the GEMM on `stream`.  Throws CudaError on a launch problem.
 // Picks the tcgen05 path when every TMA alignment rule holds, else the

@@ -76,6 +76,15 @@ struct HVal {
   int ctor_id = -1;
 };
 
+// A causal softmax's per-row masked probabilities (launch_masked_softmax's
+// `leak`) for a GEMM that skips masked entries: the terms of rows where they
+// are not zero are added back after it (launch_causal_leak_fix).
+struct LeakFix {
+  Slot* leak = nullptr;
+  int64_t rows = 0;  // softmax rows per batch item
+  int mode = 0;      // 2: O = P.V; 3: dV = P^T.dO
+};
+
 struct Param {
   std::vector<int64_t> shape;
   Slot* value = nullptr;
@@ -286,6 +295,7 @@ struct Executor {
     seqmajor_transpose.clear();
     causal_scores.clear();
     causal_probs.clear();
+    causal_leak.clear();
     folded_transpose.clear();
     grad_alias.clear();
     loss = grad_block = scratch = param_block = nullptr;
@@ -569,7 +579,7 @@ struct Executor {
   void gemm_step(StepList& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
                  Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu,
-                 int tri = 0, Slot* smx_p = nullptr, Slot* residual = nullptr) {
+                 int tri = 0, Slot* smx_p = nullptr, Slot* residual = nullptr, LeakFix fix = LeakFix()) {
     Prepared pa, pb;
     pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
     pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
@@ -615,6 +625,12 @@ struct Executor {
         s.ws_elems = ws_elems;
       }
       gemm_launch(batch, M, N, K, A, B, O, ep, mode_now, s, cx->d_err, st);
+      if (fix.leak) {
+        const int tile_rows = gemm_causal_tile_rows(batch, M, N, K, A, B, O, mode_now);
+        if (tile_rows > 0)
+          launch_causal_leak_fix(fix.mode, fix.leak->p, fix.rows, B.ptr, B.trans, B.ld, B.batch_stride, c->p, ldc, sc,
+                                 batch, M, K, N, tile_rows, st);
+      }
       if (residual && !res_in_gemm) {
         if (acc || ldc != N || (batch > 1 && sc != M * N)) throw CudaError("residual GEMM needs a fresh contiguous output");
         launch_binary_tt(kAdd, residual->p, c->p, c->p, (int64_t)batch * M * N, st);
@@ -661,8 +677,10 @@ struct Executor {
       tb = true;
       ldb = k;
     }
+    LeakFix fix;
+    if (auto lk = causal_leak.find(lid); tri == 2 && lk != causal_leak.end()) fix = {lk->second, m, 2};
     gemm_step(out, batch, m, n, k, as, ta, lda, m * k, bs, tb, ldb, k * n, o.slot, n, m * n, nullptr, alpha, false,
-              false, tri);
+              false, tri, nullptr, nullptr, fix);
     return o;
   }
 
@@ -865,6 +883,7 @@ struct Executor {
   // feeds a fused mask+softmax, and the fused softmax outputs (probabilities).
   std::set<int> causal_scores;
   std::set<int> causal_probs;
+  std::map<int, Slot*> causal_leak;  // probabilities -> per-row masked probability
   // transpose(x, -2, -1) outputs read only by one matmul: the GEMM reads x
   // with its trans flag flipped and the copy is never made (value -> x).
   std::map<int, int> folded_transpose;
@@ -1322,9 +1341,11 @@ struct Executor {
             const int64_t q = x.shape[x.shape.size() - 2];
             const int64_t outer = n / (q * w);
             causal_probs.insert(node.output);
-            // The guard is armed when a matmul will skip the masked entries.
+            // When a matmul will skip the masked entries, the kernel records
+            // each row's masked probability for the GEMMs' fix-ups.
             const bool lhs = is_matmul_lhs(node.output);
-            int* err = lhs ? ctx->d_err : nullptr;
+            Slot* leak = lhs ? alloc((size_t)(outer * q)) : nullptr;
+            if (leak) causal_leak[node.output] = leak;
             // A strict GEMM reading the probabilities as its left operand and
             // needing their low part gets it from this kernel (offered where
             // the GEMM's operand preparation looks it up) instead of a split
@@ -1335,7 +1356,8 @@ struct Executor {
             if (lhs && plan_matmul_mode == kGemmStrict && w % 4 == 0)
               lo = offer_lo(std::make_tuple(c, false, q, w, w, q * w, outer), (size_t)n);
             forward.push_back([=](cudaStream_t st) {
-              launch_masked_softmax(src->p, c->p, outer, q, w, err, lo && lo->slot ? lo->slot->p : nullptr, 1, st);
+              launch_masked_softmax(src->p, c->p, outer, q, w, leak ? leak->p : nullptr, lo && lo->slot ? lo->slot->p : nullptr,
+                                    1, st);
             });
           } else {
             forward.push_back([=](cudaStream_t st) { launch_softmax(a->p, c->p, n / w, w, st); });
@@ -1481,10 +1503,12 @@ struct Executor {
       if (!fold_r) {
         // d(r) [k, n] = l^T . g
         auto [d, acc] = contrib(rid);
+        LeakFix fix;
+        if (auto lk = causal_leak.find(lid); tri_r == 3 && lk != causal_leak.end()) fix = {lk->second, m, 3};
         if (fold_l) gemm_step(backward, batch, k, n, m, lp, false, m, k * m, g, false, n, m * n, d, n, k * n, nullptr,
-                              alpha, acc, false, tri_r);
+                              alpha, acc, false, tri_r, nullptr, nullptr, fix);
         else gemm_step(backward, batch, k, n, m, lp, true, k, m * k, g, false, n, m * n, d, n, k * n, nullptr, alpha,
-                       acc, false, tri_r);
+                       acc, false, tri_r, nullptr, nullptr, fix);
       } else {
         // d(y) [n, k] = (l^T . g)^T = g^T . l.  A causal contraction that
         // started at the output's first column (keys) now starts at its first

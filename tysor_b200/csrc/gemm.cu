@@ -1700,6 +1700,22 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
                      const GemmOutput& C, const GemmEpilogue& ep, int mode, const GemmScratch& scratch, int* d_err,
                      cudaStream_t st, bool* fused_smx);
 
+int gemm_causal_tile_rows(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
+                          const GemmOutput& C, int mode) {
+  // The same choice as gemm_launch_impl: the CUDA-core path contracts all
+  // of K; the cluster-pair kernels (persistent or not) decide the causal
+  // range on 256-row pair tiles (pp_tile, gemm_tf32_2sm_kernel), the 1-SM
+  // kernel on its 128-row tiles.
+  if (M <= 0 || N <= 0 || batch <= 0) return 0;
+  const bool tc = mode != kGemmExact && K > 0 && tma_ok(A, batch) && tma_ok(B, batch);
+  if (!tc) return 0;
+  const int BN = N <= 128 ? 128 : 256;
+  const GemmOperand Cview{C.ptr, false, C.ld, C.batch_stride};
+  const bool persistent = g_two_sm_enabled && g_persistent_enabled && M >= 256 && tma_ok(Cview, batch);
+  const bool two_sm = persistent || (g_two_sm_enabled && BN == 256 && M >= 256);
+  return two_sm ? 2 * BM : BM;
+}
+
 int gemm_launch(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A,
                 const GemmOperand& B, const GemmOutput& C, const GemmEpilogue& ep, int mode,
                 const GemmScratch& scratch, int* d_err, cudaStream_t st) {

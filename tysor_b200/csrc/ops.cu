@@ -17,6 +17,15 @@ __device__ __forceinline__ bool aligned16(const void* p) { return (((uintptr_t)p
 
 // x - tf32(x): the low part a strict 3xTF32 GEMM multiplies separately.
 __device__ __forceinline__ float lo_part(float x) { return tf32_lo(x); }
+
+// The probability every masked entry of a causal softmax row keeps: the
+// masked scores all read -1e4, so each is exp(-1e4 - max) / d, the value the
+// row stores there.  It is 0 unless the row's visible scores all lie below
+// about -9896 (then exp(-1e4 - max) does not underflow); a row with nothing
+// masked (qi = width - 1) has none.
+__device__ __forceinline__ float masked_leak(int qi, int width, bool masked_zero, float m, float d) {
+  return (qi < width - 1 && !masked_zero) ? expf(-1.0e4f - m) / d : 0.0f;
+}
 __device__ __forceinline__ float4 lo_part4(float4 v) {
   return make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
 }
@@ -524,7 +533,7 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
 template <int VPT>
 __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restrict__ x,
                                                           float* __restrict__ out, int64_t rows,
-                                                          int q, int masked, int* err,
+                                                          int q, int masked, float* __restrict__ leak,
                                                           float* __restrict__ lo, int skip_zero) {
   __shared__ float red[33];
   constexpr int kWidth = 1024 * VPT;
@@ -547,11 +556,7 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
       m = fmaxf(fmaxf(fmaxf(m, t.x), fmaxf(t.y, t.z)), t.w);
     }
     m = block_max(m, red);
-    // With `err`, later GEMMs skip the masked entries as exact zeros; flag the
-    // (scores below about -9896) rows where exp(-1e4 - max) is not zero.
     const bool masked_zero = expf(-1.0e4f - m) == 0.0f;  // the row's masked entries underflow to 0
-    if (err != nullptr && threadIdx.x == 0 && qi < kWidth - 1 && !masked_zero)
-      atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -571,6 +576,7 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
       s += v[i].w;
     }
     const float d = fmaxf(block_sum(s, red), 1.1920928955078125e-7f);
+    if (leak != nullptr && threadIdx.x == 0) leak[r] = masked_leak(qi, kWidth, masked_zero, m, d);
     float4* yr = (float4*)(out + r * kWidth);
     float4* lr = lo ? (float4*)(lo + r * kWidth) : nullptr;
 #pragma unroll
@@ -595,14 +601,15 @@ __global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restric
 }
 
 // WPR warps per row for rows of 128 * NPL * WPR values (NPL float4 per
-// lane): the row stays in registers and both reductions are warp shuffles,
+// lane; at most 64 registers, so four blocks share an SM): the row stays in
+// registers and both reductions are warp shuffles,
 // joined across the row's warps through shared memory under a named barrier
 // of the row's 32 * WPR threads (no block-wide barrier).  A block of 8 warps
 // has 8 / WPR rows in flight.  Same arithmetic and options as
 // softmax_reg_kernel.
 template <int NPL, int WPR>
-__global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                                           int64_t rows, int q, int masked, int* err,
+__global__ void __launch_bounds__(256, 4) softmax_warp_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                           int64_t rows, int q, int masked, float* __restrict__ leak,
                                                            float* __restrict__ lo, int skip_zero) {
   constexpr int kWidth = 128 * NPL * WPR;
   constexpr int kRowsPerBlock = 8 / WPR;
@@ -635,7 +642,6 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
       for (int w = 1; w < WPR; ++w) m = fmaxf(m, red[grp][0][w]);
     }
     const bool masked_zero = expf(-1.0e4f - m) == 0.0f;
-    if (err != nullptr && t == 0 && qi < kWidth - 1 && !masked_zero) atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < NPL; ++i) {
@@ -663,6 +669,7 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
       for (int w = 1; w < WPR; ++w) s += red[grp][1][w];
     }
     const float d = fmaxf(s, 1.1920928955078125e-7f);
+    if (leak != nullptr && t == 0) leak[r] = masked_leak(qi, kWidth, masked_zero, m, d);
     float4* yr = (float4*)(out + r * kWidth);
     float4* lr = lo ? (float4*)(lo + r * kWidth) : nullptr;
 #pragma unroll
@@ -689,7 +696,8 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
 // Row r of [outer*q] rows of width k; row index within its q x k block is
 // r % q.  Values with col > row read as -1e4.
 __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                      int64_t rows, int q, int width, int* err, float* __restrict__ lo) {
+                                      int64_t rows, int q, int width, float* __restrict__ leak,
+                                      float* __restrict__ lo) {
   __shared__ float red[33];
   const bool vec = (width & 3) == 0 && aligned16(x) && aligned16(out);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -710,8 +718,6 @@ __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __rest
       for (int j = threadIdx.x; j < width; j += blockDim.x) m = fmaxf(m, j > qi ? -1.0e4f : xr[j]);
     }
     m = block_max(m, red);
-    if (err != nullptr && threadIdx.x == 0 && qi < width - 1 && expf(-1.0e4f - m) != 0.0f)
-      atomicCAS(err, 0, (int)kErrCausalSkip);
     float s = 0.0f;
     if (vec) {
       for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
@@ -726,6 +732,7 @@ __global__ void masked_softmax_kernel(const float* __restrict__ x, float* __rest
       for (int j = threadIdx.x; j < width; j += blockDim.x) s += expf((j > qi ? -1.0e4f : xr[j]) - m);
     }
     const float d = fmaxf(block_sum(s, red), 1.1920928955078125e-7f);
+    if (leak != nullptr && threadIdx.x == 0) leak[r] = masked_leak(qi, width, expf(-1.0e4f - m) == 0.0f, m, d);
     if (vec) {
       for (int j = threadIdx.x; j < width / 4; j += blockDim.x) {
         const float4 v = ((const float4*)xr)[j];
@@ -1647,7 +1654,7 @@ void launch_rms_norm_gain_backward(const float* x, const float* g, const float* 
 
 // Launches the register-resident form when the width allows; false if not.
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 int* err, float* lo, int skip_zero, cudaStream_t st);
+                 float* leak, float* lo, int skip_zero, cudaStream_t st);
 
 void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cudaStream_t st) {
   if (rows <= 0) return;
@@ -1657,7 +1664,7 @@ void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cud
 }
 
 bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_t q, int masked,
-                 int* err, float* lo, int skip_zero, cudaStream_t st) {
+                 float* leak, float* lo, int skip_zero, cudaStream_t st) {
   if (width % 1024 != 0 || !aligned16_host(x) || !aligned16_host(out) || (lo && !aligned16_host(lo))) return false;
   if (width == 1024 || width == 2048) {
     const int wpr = (int)(width / 1024);
@@ -1665,29 +1672,100 @@ bool softmax_reg(const float* x, float* out, int64_t rows, int64_t width, int64_
     const int wblocks = (int)(want < 148 * 16 ? want : 148 * 16);
     // Two warps per 2048-wide row measured faster than one warp holding 16
     // float4 per lane (128 registers, half the resident warps) or four warps.
-    if (width == 1024) softmax_warp_kernel<8, 1><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero);
-    else softmax_warp_kernel<8, 2><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero);
+    if (width == 1024) softmax_warp_kernel<8, 1><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero);
+    else softmax_warp_kernel<8, 2><<<wblocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero);
     check_launch();
     return true;
   }
   const int blocks = row_blocks(rows);
   switch (width / 1024) {
-    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
-    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
-    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
-    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, err, lo, skip_zero); break;
+    case 1: softmax_reg_kernel<1><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero); break;
+    case 2: softmax_reg_kernel<2><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero); break;
+    case 4: softmax_reg_kernel<4><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero); break;
+    case 8: softmax_reg_kernel<8><<<blocks, 256, 0, st>>>(x, out, rows, (int)q, masked, leak, lo, skip_zero); break;
     default: return false;
   }
   check_launch();
   return true;
 }
 
+// Causal attention rows whose masked entries keep a probability (leak[r] =
+// c_r != 0, see masked_leak) lose terms where the causal GEMMs skip masked
+// entries as zeros; these kernels add them back, one block per batch item
+// (head).  A head none of whose rows leaks returns after reading its rows'
+// leak values.
+//
+// mode 2, after O = P.V with GemmEpilogue::tri 2: row r was contracted over
+// keys k < kend(r) = the end of its tile of tile_rows rows (rounded up to
+// 16); the keys after that are all masked for r, each with probability c_r,
+// so o[r] += c_r * sum_{k >= kend(r)} v[k].
+// mode 3, after dV = P^T.dO with tri 3: output row j (a key) was contracted
+// over queries from the start of its tile; the queries before it all mask
+// key j, each with its own c_q, so dv[j] += sum_{q < start(j)} c_q * dO[q].
+// `x` is the GEMM's B operand (v or dO; x_trans: stored [n, k]); `out` its
+// output, rows = the GEMM's M, `kn` its K, `n` its N.
+__global__ void causal_leak_fix_kernel(int mode, const float* __restrict__ leak, int lrows,
+                                       const float* __restrict__ x, int x_trans, int64_t x_ld, int64_t x_bs,
+                                       float* __restrict__ out, int64_t o_ld, int64_t o_bs, int rows, int kn, int n,
+                                       int tile_rows) {
+  const int b = blockIdx.x;
+  const float* lk = leak + (int64_t)b * lrows;
+  int any = 0;
+  for (int r = threadIdx.x; r < lrows; r += blockDim.x) any |= lk[r] != 0.0f;
+  if (!__syncthreads_or(any)) return;
+  const float* xb = x + (int64_t)b * x_bs;
+  float* ob = out + (int64_t)b * o_bs;
+  auto xv = [&](int k, int d) { return x_trans ? xb[(int64_t)d * x_ld + k] : xb[(int64_t)k * x_ld + d]; };
+  for (int d = threadIdx.x; d < n; d += blockDim.x) {
+    if (mode == 2) {
+      // Tiles from the last: the suffix sum over keys grows as kend falls.
+      float acc = 0.0f;
+      int kk = kn;
+      const int last = ((rows - 1) / tile_rows) * tile_rows;
+      for (int t0 = last; t0 >= 0; t0 -= tile_rows) {
+        int kend = ((t0 + tile_rows + 15) / 16) * 16;
+        if (kend > kn) kend = kn;
+        while (kk > kend) acc = acc + xv(--kk, d);
+        const int t1 = t0 + tile_rows < rows ? t0 + tile_rows : rows;
+        for (int r = t0; r < t1; ++r) {
+          const float c = lk[r];
+          if (c != 0.0f) ob[(int64_t)r * o_ld + d] = ob[(int64_t)r * o_ld + d] + c * acc;
+        }
+      }
+    } else {
+      // Tiles from the first: the prefix sum over queries grows with start.
+      float acc = 0.0f;
+      int qq = 0;
+      for (int t0 = 0; t0 < rows; t0 += tile_rows) {
+        for (; qq < t0 && qq < kn; ++qq) {
+          const float c = lk[qq];
+          if (c != 0.0f) acc = acc + c * xv(qq, d);
+        }
+        if (acc == 0.0f) continue;
+        const int t1 = t0 + tile_rows < rows ? t0 + tile_rows : rows;
+        for (int j = t0; j < t1; ++j) ob[(int64_t)j * o_ld + d] = ob[(int64_t)j * o_ld + d] + acc;
+      }
+    }
+  }
+}
+
+void launch_causal_leak_fix(int mode, const float* leak, int64_t lrows, const float* x, bool x_trans, int64_t x_ld,
+                            int64_t x_bs, float* out, int64_t o_ld, int64_t o_bs, int batch, int64_t rows, int64_t kn,
+                            int64_t n, int tile_rows, cudaStream_t st) {
+  if (batch <= 0 || rows <= 0 || n <= 0 || tile_rows <= 0) return;
+  if (mode != 2 && mode != 3) throw CudaError("causal leak fix: mode is 2 or 3");
+  if (rows > INT32_MAX || kn > INT32_MAX || n > INT32_MAX || lrows > INT32_MAX) throw CudaError("causal leak fix: too large");
+  causal_leak_fix_kernel<<<batch, 128, 0, st>>>(mode, leak, (int)lrows, x, x_trans ? 1 : 0, x_ld, x_bs, out, o_ld,
+                                                 o_bs, (int)rows, (int)kn, (int)n, tile_rows);
+  check_launch();
+}
+
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           int* err, float* lo, int skip_zero, cudaStream_t st) {
+                           float* leak, float* lo, int skip_zero, cudaStream_t st) {
   const int64_t rows = outer * q;
   if (rows <= 0) return;
-  if (softmax_reg(x, out, rows, k, q, 1, err, lo, skip_zero, st)) return;
-  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k, err, lo);
+  if (softmax_reg(x, out, rows, k, q, 1, leak, lo, skip_zero, st)) return;
+  masked_softmax_kernel<<<row_blocks(rows), row_threads(k / 4), 0, st>>>(x, out, rows, (int)q, (int)k, leak, lo);
   check_launch();
 }
 

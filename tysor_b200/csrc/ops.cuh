@@ -72,15 +72,26 @@ void launch_softmax(const float* x, float* out, int64_t rows, int64_t width, cud
 // Softmax of causal_mask(x) over [outer][q][k] in one pass: entries with
 // col > row take the mask's -1e4 (layers.rs:217-236), then the row softmax
 // (tensor.rs:235-260) — the same arithmetic as the two ops in sequence.
-// With `err`, a row whose masked entries would get a nonzero probability
-// (possible only when its scores are all below about -9896) records
-// kErrCausalSkip: GEMMs that treat those entries as zeros would be wrong.
-// With `lo`, also writes each probability's low part x - tf32(x) (the
-// operand split a strict GEMM consuming them needs).  With `skip_zero`,
-// wholly masked groups (exact zeros) are not stored: for buffers known to
-// hold zeros there already.
+// With `leak` ([outer * q]), writes each row's masked-entry probability
+// exp(-1e4 - max) / d, which is 0 unless the row's visible scores all lie
+// below about -9896 (and 0 for a row with nothing masked): causal GEMMs that
+// skip masked entries as zeros add those terms back with
+// launch_causal_leak_fix.  With `lo`, also writes each probability's low
+// part (tf32_lo, the operand split a strict GEMM consuming them needs).
+// With `skip_zero`, wholly masked groups (exact zeros) are not stored: for
+// buffers known to hold zeros there already.
 void launch_masked_softmax(const float* x, float* out, int64_t outer, int64_t q, int64_t k,
-                           int* err, float* lo, int skip_zero, cudaStream_t st);
+                           float* leak, float* lo, int skip_zero, cudaStream_t st);
+// After a causal GEMM that skipped masked entries as zeros (mode 2: O = P.V,
+// GemmEpilogue::tri 2; mode 3: dV = P^T.dO, tri 3; tile_rows as
+// gemm_causal_tile_rows reports for it), adds back the terms of rows whose
+// masked entries keep probability leak[row] (see launch_masked_softmax).
+// x: the GEMM's B operand (V or dO) with its layout; out: its output; rows,
+// kn, n: its M, K, N; lrows: the softmax rows per batch item.  A batch item
+// without such a row costs one read of its leak values.
+void launch_causal_leak_fix(int mode, const float* leak, int64_t lrows, const float* x, bool x_trans, int64_t x_ld,
+                            int64_t x_bs, float* out, int64_t o_ld, int64_t o_bs, int batch, int64_t rows, int64_t kn,
+                            int64_t n, int tile_rows, cudaStream_t st);
 // Backward of Softmax(causal_mask(x)) with the reference rules: the
 // diagonal softmax term y(1-y)g (layers.rs:350-364), then the mask zeroes
 // col > row (layers.rs:418-436): dx (+)= col > row ? 0 : y(1-y)g.
