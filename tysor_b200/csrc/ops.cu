@@ -528,10 +528,10 @@ __global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ 
 
 // Register-resident row softmax for widths of 1024 * VPT: each of 256
 // threads keeps VPT float4 of its row, so the row is read from HBM once and
-// written once.  With `masked`, row r's entries with col > r % q read as
+// written once (registers capped so five blocks share an SM, four at VPT 8).  With `masked`, row r's entries with col > r % q read as
 // -1e4 (causal_mask fused in front).  Same arithmetic as softmax_kernel.
 template <int VPT>
-__global__ void __launch_bounds__(256) softmax_reg_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(256, VPT >= 8 ? 4 : 5) softmax_reg_kernel(const float* __restrict__ x,
                                                           float* __restrict__ out, int64_t rows,
                                                           int q, int masked, float* __restrict__ leak,
                                                           float* __restrict__ lo, int skip_zero) {
