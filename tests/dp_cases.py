@@ -5,7 +5,7 @@ worker (tests/dp_worker.py): one rank's share of a seeded batch.
   sharded evenly (tysor_b200.dist.shard_rows), mean squared error over the
   global batch.
 * `lm`: a 2-layer llama_lm (d 128, 4/2 heads, ffn 192, vocab 512) on
-  2 sequences of 64 tokens, one sequence per rank at world size 2.
+  4 sequences of 64 tokens, split evenly at world sizes 2 and 4.
 
 world == 1 gives the full batch, whose gradient the ranks' summed
 gradients must equal.
@@ -23,7 +23,7 @@ from tysor_b200.dist import shard_rows  # noqa: E402
 from tysor_b200.programs import llama_lm, mlp_train, random_parameters  # noqa: E402
 
 MLP = dict(rows=8192, d_in=1024, d_hidden=4096)
-LM = dict(layers=2, batch=2, seq=64, d_model=128, n_heads=4, n_kv_heads=2, hidden=192, vocab=512)
+LM = dict(layers=2, batch=4, seq=64, d_model=128, n_heads=4, n_kv_heads=2, hidden=192, vocab=512)
 
 
 def case(workload, rank, world):

@@ -6,10 +6,10 @@ gradient all-reduce (tysor_cuda_graph_enable_allreduce).
   identity, so a step with it enabled must give bit-identical gradients,
   loss and parameters to a step without it, and tysor_cuda_allreduce_sum on
   a buffer must leave it unchanged.
-* Two ranks (needs 2 GPUs): each rank trains on half of the batch with the
-  all-reduce on; the summed gradients must equal the one-rank full-batch
-  gradient (Frobenius rel 1e-5: only the fp32 summation order differs), and
-  the summed loss the full-batch loss.  Run under torch.distributed.run
+* Two and four ranks (needs that many GPUs): each rank trains on its share
+  of the batch with the all-reduce on; the summed gradients must equal the
+  one-rank full-batch gradient (Frobenius rel 1e-5: only the fp32 summation
+  order differs), and the summed loss the full-batch loss.  Run under torch.distributed.run
   with a gloo group for the id exchange and a bounded process lifetime.
 """
 import os
@@ -78,14 +78,15 @@ def free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("workload", ["mlp", "lm"])
-def test_two_ranks_sum_to_the_full_batch_gradient(workload, tmp_path):
+def test_ranks_sum_to_the_full_batch_gradient(workload, world, tmp_path):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     out = tmp_path / f"{workload}.npz"
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            os.path.join(HERE, "dp_worker.py"), "--workload", workload, "--out", str(out)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     res = subprocess.run(cmd, capture_output=True, text=True, env=env)
@@ -94,6 +95,6 @@ def test_two_ranks_sum_to_the_full_batch_gradient(workload, tmp_path):
     want_losses, want_grads = full_batch(workload)
     assert abs(float(got["loss"][0]) - want_losses[0]) <= 1e-5 * abs(want_losses[0])
     errs = {name: frob(got[name], w) for name, w in want_grads.items()}
-    print(f"\n{workload} 2-rank vs 1-rank gradients:", {k: f"{v:.2e}" for k, v in errs.items()})
+    print(f"\n{workload} {world}-rank vs 1-rank gradients:", {k: f"{v:.2e}" for k, v in errs.items()})
     for name, e in errs.items():
         assert e < 1e-5, (name, e)
