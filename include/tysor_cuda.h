@@ -253,6 +253,15 @@ bool tysor_cuda_graph_backward(void* graph);
 /* --train: `iterations` SGD steps (executor.rs:764-816); losses[i] receives
  * the summed objective of step i (may be NULL). */
 bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losses);
+/* The same steps enqueued on the context stream without waiting: each
+ * step's loss is copied to host_losses[i] on the stream (pinned host memory
+ * keeps the copies asynchronous; NULL: not copied), valid once
+ * tysor_cuda_synchronize returns, which also reports any error a step's
+ * kernels recorded.  A trainer that prefetches its next inputs
+ * (tysor_cuda_graph_prefetch_input) and enqueues its next step while this
+ * one runs keeps the device busy between steps.  Extension: the reference
+ * trains synchronously (executor.rs:764-816). */
+bool tysor_cuda_graph_train_enqueue(void* graph, int iterations, double lr, float* host_losses);
 /* Extension (no reference counterpart): one train step launched op by op
  * with a CUDA event after each planned step item (forward, backward, update
  * order); item_ms[i] (i < capacity) receives item i's device time and

@@ -82,6 +82,7 @@ pub mod ffi {
         pub fn tysor_cuda_graph_run(graph: *mut c_void) -> bool;
         pub fn tysor_cuda_graph_backward(graph: *mut c_void) -> bool;
         pub fn tysor_cuda_graph_train(graph: *mut c_void, iterations: c_int, lr: f64, losses: *mut f32) -> bool;
+        pub fn tysor_cuda_graph_train_enqueue(graph: *mut c_void, iterations: c_int, lr: f64, host_losses: *mut f32) -> bool;
         pub fn tysor_cuda_graph_train_traced(graph: *mut c_void, lr: f64, item_ms: *mut f32, capacity: c_int, n_items: *mut c_int) -> bool;
         pub fn tysor_cuda_graph_trace_label(graph: *mut c_void, item: c_int) -> *const c_char;
         pub fn tysor_cuda_graph_value_rank(graph: *mut c_void, value_id: c_int) -> c_int;

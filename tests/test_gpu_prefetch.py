@@ -1,7 +1,10 @@
 """Prefetched inputs (tysor_cuda_graph_prefetch_input): values queued from
 pinned host memory on the copy stream are taken by the following train
 calls in order, and training on them gives exactly the losses and
-parameters of uploading each value right before its step."""
+parameters of uploading each value right before its step -- also when the
+steps are enqueued without waiting (tysor_cuda_graph_train_enqueue), the
+host running ahead of the device, and each loss is read back on the
+stream."""
 import numpy as np
 import pytest
 import torch
@@ -26,6 +29,42 @@ def make(ctx, first):
     ex = CudaGraphExecutor(ctx, g, {"x": [ROWS, D_IN], "target": [ROWS, D_IN]}, inputs=first,
                            parameters=random_parameters(g, 5))
     return g, ex
+
+
+def reference_run(ctx, data):
+    """Upload each batch, then step (synchronously)."""
+    g, ex = make(ctx, data[0])
+    ex.train(1, 0.0)  # plans the buffers (lr 0: parameters unchanged)
+    want = []
+    for b in data:
+        for name, arr in b.items():
+            ex.upload_input(name, arr)
+        want += ex.train(1, 0.01)
+    want_p = {n: ex.parameter(n) for n in random_parameters(g, 5)}
+    ex.close()
+    return want, want_p
+
+
+def test_enqueued_prefetched_steps_match_synchronous_steps(cuda_ctx):
+    data = batches(6)
+    want, want_p = reference_run(cuda_ctx, data)
+    g, ex = make(cuda_ctx, data[0])
+    ex.train(1, 0.0)
+    pinned = [{k: torch.from_numpy(v).pin_memory() for k, v in b.items()} for b in data]
+    losses = torch.zeros(len(data), dtype=torch.float32).pin_memory()
+    host = losses.numpy()
+    for name, t in pinned[0].items():
+        ex.prefetch_input(name, t.numpy())
+    for i in range(len(data)):
+        if i + 1 < len(data):
+            for name, t in pinned[i + 1].items():
+                ex.prefetch_input(name, t.numpy())
+        ex.train_enqueue(1, 0.01, host[i:i + 1])  # returns at once
+    cuda_ctx.synchronize()
+    assert [float(v) for v in host] == want
+    for n, w in want_p.items():
+        np.testing.assert_array_equal(ex.parameter(n), w)
+    ex.close()
 
 
 def test_prefetched_steps_match_uploaded_steps(cuda_ctx):

@@ -2283,69 +2283,84 @@ bool tysor_cuda_graph_backward(void* graph) {
   });
 }
 
+// Enqueues `iterations` train steps on the context stream (the first step
+// of a plan eagerly, later ones as the captured graph) and each step's loss
+// into the device history; with `host_losses`, each loss is also copied to
+// host_losses[it] on the stream.  Waits for nothing.
+void enqueue_train_steps(Executor* e, int iterations, double lr, float* host_losses) {
+  if (iterations < 0) throw CudaError("iterations must be >= 0");
+  e->plan(kModeTrain);
+  e->lr_f = (float)lr;
+  e->ensure_setup();
+  e->run_uploads();
+  cudaStream_t st = e->ctx->stream;
+  if (iterations > e->loss_hist_cap) {
+    // Grown outside any capture; the step loop itself allocates nothing.
+    TYSOR_CUDA(cudaStreamSynchronize(st));
+    if (e->loss_hist) TYSOR_CUDA(cudaFree(e->loss_hist));
+    e->loss_hist = nullptr;
+    e->loss_hist_cap = 0;
+    const int cap = iterations < 1024 ? 1024 : iterations;
+    TYSOR_CUDA(cudaMalloc(&e->loss_hist, sizeof(float) * cap));
+    e->loss_hist_cap = cap;
+  }
+  float* d_losses = e->loss_hist;
+  auto step = [&]() {
+    e->run_list(e->forward);
+    e->run_list(e->backward);
+    e->run_list(e->update);
+  };
+  for (int it = 0; it < iterations; ++it) {
+    const int64_t l0 = g_launches.load();
+    // The first step of a plan runs eagerly (it configures kernels); every
+    // later step, in this call or a later one, replays the captured graph.
+    if (e->capture && e->stepped) {
+      if (!e->exec) {
+        cudaGraph_t g = nullptr;
+        TYSOR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        try {
+          step();
+        } catch (...) {
+          cudaStreamEndCapture(st, &g);
+          if (g) cudaGraphDestroy(g);
+          throw;
+        }
+        TYSOR_CUDA(cudaStreamEndCapture(st, &g));
+        TYSOR_CUDA(cudaGraphInstantiate(&e->exec, g, 0));
+        cudaGraphDestroy(g);
+        e->step_launches = g_launches.load() - l0;
+      }
+      TYSOR_CUDA(cudaGraphLaunch(e->exec, st));
+    } else {
+      step();
+      e->step_launches = g_launches.load() - l0;
+      e->stepped = true;
+    }
+    // The step's loss is kept by a one-element copy kernel (no copy-engine
+    // work between the steps' kernels).
+    launch_unary(kUnaryCopy, e->loss->p, d_losses + it, 1, 0.0f, st);
+    if (host_losses)
+      TYSOR_CUDA(cudaMemcpyAsync(host_losses + it, d_losses + it, sizeof(float), cudaMemcpyDeviceToHost, st));
+    e->last_launches = e->step_launches + 1;  // kernels per step, the loss copy included
+  }
+}
+
 bool tysor_cuda_graph_train(void* graph, int iterations, double lr, float* losses) {
   return guarded_g([&] {
     Executor* e = E(graph);
-    if (iterations < 0) throw CudaError("iterations must be >= 0");
-    e->plan(kModeTrain);
-    e->lr_f = (float)lr;
-    e->ensure_setup();
-    e->run_uploads();
-    cudaStream_t st = e->ctx->stream;
-    if (iterations > e->loss_hist_cap) {
-      // Grown outside any capture; the step loop itself allocates nothing.
-      TYSOR_CUDA(cudaStreamSynchronize(st));
-      if (e->loss_hist) TYSOR_CUDA(cudaFree(e->loss_hist));
-      e->loss_hist = nullptr;
-      e->loss_hist_cap = 0;
-      const int cap = iterations < 1024 ? 1024 : iterations;
-      TYSOR_CUDA(cudaMalloc(&e->loss_hist, sizeof(float) * cap));
-      e->loss_hist_cap = cap;
-    }
-    float* d_losses = e->loss_hist;
-    auto step = [&]() {
-      e->run_list(e->forward);
-      e->run_list(e->backward);
-      e->run_list(e->update);
-    };
-    for (int it = 0; it < iterations; ++it) {
-      const int64_t l0 = g_launches.load();
-      // The first step of a plan runs eagerly (it configures kernels); every
-      // later step, in this call or a later one, replays the captured graph.
-      if (e->capture && e->stepped) {
-        if (!e->exec) {
-          cudaGraph_t g = nullptr;
-          TYSOR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-          try {
-            step();
-          } catch (...) {
-            cudaStreamEndCapture(st, &g);
-            if (g) cudaGraphDestroy(g);
-            throw;
-          }
-          TYSOR_CUDA(cudaStreamEndCapture(st, &g));
-          TYSOR_CUDA(cudaGraphInstantiate(&e->exec, g, 0));
-          cudaGraphDestroy(g);
-          e->step_launches = g_launches.load() - l0;
-        }
-        TYSOR_CUDA(cudaGraphLaunch(e->exec, st));
-      } else {
-        step();
-        e->step_launches = g_launches.load() - l0;
-        e->stepped = true;
-      }
-      // The step's loss is kept by a one-element copy kernel (no copy-engine
-      // work between the steps' kernels).
-      launch_unary(kUnaryCopy, e->loss->p, d_losses + it, 1, 0.0f, st);
-      e->last_launches = e->step_launches + 1;  // kernels per step, the loss copy included
-    }
+    enqueue_train_steps(e, iterations, lr, nullptr);
     std::vector<float> host(iterations > 0 ? iterations : 1);
     if (iterations > 0)
-      TYSOR_CUDA(cudaMemcpyAsync(host.data(), d_losses, sizeof(float) * iterations, cudaMemcpyDeviceToHost, st));
+      TYSOR_CUDA(cudaMemcpyAsync(host.data(), e->loss_hist, sizeof(float) * iterations, cudaMemcpyDeviceToHost,
+                                 e->ctx->stream));
     e->ctx->sync_and_check();
     if (losses)
       for (int i = 0; i < iterations; ++i) losses[i] = host[i];
   });
+}
+
+bool tysor_cuda_graph_train_enqueue(void* graph, int iterations, double lr, float* host_losses) {
+  return guarded_g([&] { enqueue_train_steps(E(graph), iterations, lr, host_losses); });
 }
 
 bool tysor_cuda_graph_train_traced(void* graph, double lr, float* item_ms, int capacity,

@@ -82,6 +82,7 @@ SIGNATURES = {
     "tysor_cuda_graph_run": (c_bool, [V]),
     "tysor_cuda_graph_backward": (c_bool, [V]),
     "tysor_cuda_graph_train": (c_bool, [V, c_int, c_double, FP]),
+    "tysor_cuda_graph_train_enqueue": (c_bool, [V, c_int, c_double, FP]),
     "tysor_cuda_graph_train_traced": (c_bool, [V, c_double, FP, c_int, POINTER(c_int)]),
     "tysor_cuda_graph_trace_label": (c_char_p, [V, c_int]),
     "tysor_cuda_graph_value_rank": (c_int, [V, c_int]),

@@ -222,6 +222,18 @@ class CudaGraphExecutor:
         check(self._lib.tysor_cuda_graph_train(self.handle, it, rate, fptr(losses)), "train")
         return [float(x) for x in losses[:it]]
 
+    def train_enqueue(self, iterations: int, lr: float, host_losses: Optional[np.ndarray] = None) -> None:
+        """Enqueues `iterations` train steps without waiting; step i's loss is
+        copied to host_losses[i] (a float32 array, pinned for an asynchronous
+        copy) on the stream.  The values are valid after ctx.synchronize(),
+        which also reports errors.  Keep host_losses alive until then."""
+        ptr = None
+        if host_losses is not None:
+            if host_losses.dtype != np.float32 or not host_losses.flags["C_CONTIGUOUS"] or host_losses.size < iterations:
+                raise ValueError("host_losses must be a contiguous float32 array of at least `iterations` values")
+            ptr = fptr(host_losses)
+        check(self._lib.tysor_cuda_graph_train_enqueue(self.handle, int(iterations), float(lr), ptr), "train_enqueue")
+
     def train_traced(self, lr: Optional[float] = None) -> List[Tuple[str, float]]:
         """One train step launched op by op; returns (label, device ms) for
         each planned step item, in forward, backward, update order."""
