@@ -331,11 +331,12 @@ def measured_peaks():
 
 # ---- our arm -------------------------------------------------------------------------------
 
-def roofline(ctx, lib, stream, m, n, k):
+def roofline(ctx, lib, stream, m, n, k, mode="strict"):
     """The dominant strict matmul, timed alone with events on the library's
     stream, in the layout the executor hands the kernel (A [m,k] and B
-    [n,k], both K-major); the split kernel that makes B's low part runs
-    inside each call (A's is made inside the GEMM)."""
+    [n,k], both K-major).  strict: the split kernel that makes B's low part
+    runs inside each call (A's is made inside the GEMM); strict16: the two
+    packing kernels (A and B into fp16 halves) run inside each call."""
     import torch
     from tysor_b200 import native
     from tysor_b200.runtime import DeviceBuffer
@@ -361,13 +362,25 @@ def roofline(ctx, lib, stream, m, n, k):
     e2.synchronize()
     call_ms = s2.elapsed_time(e2) / reps
     peaks, src = measured_peaks()
-    tf32_peak = peaks["bf16_tflops"] / 2.0
     achieved = 2.0 * m * n * k / (call_ms / 1000.0) / 1e12
     for buf in (A, Bw, C):
         buf.free()
+    if mode == "strict16":
+        peak = peaks["bf16_tflops"]
+        return {"bound": "tensor",
+                "kernel": "matmul strict16 (pack16 of A and B + gemm_tf32_pp_kernel<256,1,0,0,0,0,0,1>: persistent "
+                          "cluster pairs, kind::f16 over packed fp16 halves)",
+                "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "tensor_pipe_frac": round(3 * achieved / peak, 4), "traffic": None,
+                "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                "ms_per_launch": round(call_ms, 4),
+                "peak_source": f"{src}: bf16_tflops {peaks['bf16_tflops']} (the fp16 tensor rate equals bf16's)",
+                "note": "three fp16 MMAs per product: frac is capped at 0.333; tensor_pipe_frac counts all three"}
+    tf32_peak = peaks["bf16_tflops"] / 2.0
     # DRAM bytes (read + write) of one launch of this kernel on this shape,
     # from the ncu capture summarised in profiles/gemm_tf32_16384x5632x2048.md.
-    traffic = 1155622000 + 350200832 if (m, n, k) == (16384, 5632, 2048) else None
+    traffic = 1140797000 + 350372864 if (m, n, k) == (16384, 5632, 2048) else None
     return {"bound": "tensor",
             "kernel": "matmul strict 3xTF32 (split_lo of B + gemm_tf32_pp_kernel<256,1,0,0,1,0>: persistent "
                       "cluster pairs, A's low part made in shared memory)",
@@ -389,7 +402,7 @@ def run_ours(args, rank, world, local_rank, dist):
 
     wl = WORKLOADS[args.workload]
     torch.cuda.set_device(local_rank)
-    ctx = CudaContext(local_rank)
+    ctx = CudaContext(local_rank, matmul=args.matmul)
     if args.accum_chunk:
         ctx.set_matmul_accumulation(args.accum_chunk)
     lib = native.lib()
@@ -507,7 +520,7 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
-    roof = roofline(ctx, lib, stream, *wl.roof_gemm) if rank == 0 else None
+    roof = roofline(ctx, lib, stream, *wl.roof_gemm, mode=args.matmul) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -525,11 +538,13 @@ def run_ours(args, rank, world, local_rank, dist):
         cfg["last_loss"] = losses[-1] if losses else None
         if args.accum_chunk:
             cfg["accum_chunk_kblocks"] = args.accum_chunk
+        cfg["matmul"] = args.matmul
         line = {
             "metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
-            "dtype": "f32 (3xTF32 tensor-core matmul)",
+            "dtype": "f32 (3xTF32 tensor-core matmul)" if args.matmul == "strict" else
+                     "f32 (3-product split-fp16 tensor-core matmul)",
             "data": "synthetic, seeded on the host (inputs N(0,1) or U ids, weights N(0,0.02), gains N(1,0.02))",
             "config": cfg, "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(total_units / e2e_s, 1), "unit": wl.unit,
@@ -588,6 +603,8 @@ def main():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="block", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--matmul", default="strict", choices=["strict", "strict16"],
+                   help="strict: 3xTF32; strict16: the three products over fp16 halves with per-row scales")
     p.add_argument("--accum-chunk", type=int, default=0,
                    help="k-blocks per tensor-memory accumulation chunk of the matmuls (0: default 8)")
     args = p.parse_args()

@@ -42,7 +42,10 @@ void tysor_cuda_context_free(void* context);
  * error (the Metal bridge waits inside every dispatch, bridge:89-90). */
 bool tysor_cuda_synchronize(void* context);
 /* Matmul arithmetic: 0 = strict (3xTF32, the default), 1 = fast (1xTF32),
- * 2 = exact (CUDA-core fp32 in k order).  No reference counterpart. */
+ * 2 = exact (CUDA-core fp32 in k order), 3 = strict16 (the same three
+ * products over fp16 halves with a power-of-two scale per operand row, on
+ * the tensor core's fp16 rate; unbatched non-causal GEMMs with M >= 256 and
+ * N > 128, the others as strict).  No reference counterpart. */
 bool tysor_cuda_set_matmul_mode(void* context, int mode);
 /* Tensor-core matmuls (strict and fast): how many k-blocks of 16 the tensor
  * core accumulates in tensor memory before the partial sum is added into

@@ -41,7 +41,7 @@ def main() -> None:
     p.add_argument("--k", type=int, default=2048)
     p.add_argument("--ta", action="store_true")
     p.add_argument("--tb", action="store_true")
-    p.add_argument("--mode", default="strict", choices=["strict", "fast", "exact"])
+    p.add_argument("--mode", default="strict", choices=["strict", "fast", "exact", "strict16"])
     p.add_argument("--op", default="softmax", choices=["softmax", "rms_norm", "silu", "cross_entropy_labels"])
     p.add_argument("--rows", type=int, default=65536)
     p.add_argument("--width", type=int, default=4096)

@@ -118,9 +118,9 @@ float* ptr_of(void* p, size_t need, const char* what) {
 }
 
 GemmScratch gemm_scratch(Context* c, int batch, int64_t M, int64_t N, int64_t K,
-                         const GemmOperand& A, const GemmOperand& Bm) {
+                         const GemmOperand& A, const GemmOperand& Bm, int mode) {
   int64_t na = 0, nb = 0;
-  gemm_scratch_need(batch, M, N, K, A, Bm, c->matmul_mode, &na, &nb);
+  gemm_scratch_need(batch, M, N, K, A, Bm, mode, &na, &nb);
   GemmScratch s{nullptr, nullptr, 0, 0};
   if (na + nb == 0) return s;
   const int64_t na_pad = (na + 63) & ~(int64_t)63;
@@ -136,8 +136,10 @@ void run_gemm(Context* c, int batch, int64_t M, int64_t N, int64_t K, const Gemm
               const GemmOperand& Bm, const GemmOutput& out, const GemmEpilogue& ep_in) {
   GemmEpilogue ep = ep_in;
   ep.chunk_kb = c->accum_chunk_kb;
-  GemmScratch s = gemm_scratch(c, batch, M, N, K, A, Bm);
-  gemm_launch(batch, M, N, K, A, Bm, out, ep, c->matmul_mode, s, c->d_err, c->stream);
+  const int mode =
+      gemm_effective_mode(c->matmul_mode, batch, M, N, K, ep.tri, ep.smx_p != nullptr, out.ld, out.batch_stride);
+  GemmScratch s = gemm_scratch(c, batch, M, N, K, A, Bm, mode);
+  gemm_launch(batch, M, N, K, A, Bm, out, ep, mode, s, c->d_err, c->stream);
 }
 
 float* scratch_floats(Context* c, int64_t n) {
@@ -215,7 +217,8 @@ void* tysor_cuda_context_stream(void* context) {
 
 bool tysor_cuda_set_matmul_mode(void* context, int mode) {
   return guarded([&] {
-    if (mode < 0 || mode > 2) throw CudaError("matmul mode must be 0 (strict), 1 (fast) or 2 (exact)");
+    if (mode < 0 || mode > 3)
+      throw CudaError("matmul mode must be 0 (strict), 1 (fast), 2 (exact) or 3 (strict16)");
     ctx_of(context)->matmul_mode = mode;
   });
 }

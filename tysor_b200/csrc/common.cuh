@@ -102,18 +102,47 @@ struct GemmEpilogue {
   // core adds each MMA into its accumulator rounding toward zero, so shorter
   // chunks shrink that systematic error (and cost the readout more often).
   int chunk_kb = 0;
+  // Set by the launcher for the split-fp16 kernel: the per-row factors of
+  // the packed A ([M]) and B ([N]) operands (see launch_pack16).
+  const float* row_factor = nullptr;
+  const float* col_factor = nullptr;
 };
 
 enum GemmMode : int {
-  kGemmStrict = 0,  // 3xTF32 split: fp32-level accuracy
-  kGemmFast = 1,    // 1xTF32
-  kGemmExact = 2,   // CUDA-core fp32, products and sums in k order (bit-exact)
+  kGemmStrict = 0,    // 3xTF32 split: fp32-level accuracy
+  kGemmFast = 1,      // 1xTF32
+  kGemmExact = 2,     // CUDA-core fp32, products and sums in k order (bit-exact)
+  kGemmStrict16 = 3,  // 3-product split over fp16 halves with per-row scaling (kind::f16):
+                      // fp32-level accuracy at twice the tensor rate of 3xTF32; GEMMs it
+                      // does not cover run as kGemmStrict (gemm_effective_mode)
 };
+
+// The mode a GEMM of this shape runs in: kGemmStrict16 covers unbatched,
+// non-causal GEMMs with M >= 256, N > 128 and C on 16-byte strides, without
+// the fused softmax backward; the others run strict 3xTF32.  Every other
+// mode is returned unchanged.  Callers size scratch and launch with the
+// returned mode.
+int gemm_effective_mode(int mode, int batch, int64_t M, int64_t N, int64_t K, int tri, bool smx, int64_t ldc,
+                        int64_t stride_c);
+
+// Split-fp16 packing of one GEMM operand with R rows (M for A, N for B) and
+// K columns, K-major: hi [R][Kp] and lo [R][Kp] fp16 (Kp = K rounded up to
+// a multiple of 8), then factor [R] fp32, then (for an operand stored with
+// R contiguous) R words of scratch.  Per row r, x is scaled by 2^e(r), the
+// power of two that puts the row's largest magnitude in [2^14, 2^15) (e
+// clamped to [-63, 63]; 0 for a zero or non-finite maximum); hi = fp16(x
+// 2^e), lo = fp16(x 2^e - hi), factor = 2^-e.  hi + lo hold 22 significant
+// bits of x, as 3xTF32's two parts do.  `k_contiguous`: x stored [R][ld]
+// (K contiguous); else [K][ld] (R contiguous).
+int64_t gemm_pack16_elems(int64_t rows, int64_t K);
+void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, int64_t ld, float* packed,
+                   cudaStream_t st);
 
 // Scratch the strict-mode GEMM needs: one "lo" copy of each operand, laid
 // out like the operand (no a_lo when gemm_converts_a).  With `presplit` set
 // the copies already hold lo(A), lo(B) and the launcher does not recompute
-// them.
+// them.  In kGemmStrict16 mode a_lo and b_lo hold the packed operands
+// (gemm_pack16_elems floats each; packed by the launcher unless presplit).
 struct GemmScratch {
   float* a_lo;
   float* b_lo;

@@ -285,6 +285,7 @@ struct Executor {
     params.clear();
     param_order.clear();
     prep_cache.clear();
+    pack_cache.clear();
     lazy_lo.clear();
     deferred_matmul.clear();
     folded_scale.clear();
@@ -484,6 +485,9 @@ struct Executor {
   };
   using PrepKey = std::tuple<Slot*, bool, int64_t, int64_t, int64_t, int64_t, int64_t>;
   std::map<PrepKey, std::pair<Slot*, Slot*>> prep_cache;
+  // Split-fp16 packings (kGemmStrict16), keyed by operand, K contiguous or
+  // not, rows, K and row pitch.
+  std::map<std::tuple<Slot*, bool, int64_t, int64_t, int64_t>, Slot*> pack_cache;
   // Low parts that the kernel producing a value can write as it goes (the
   // fused causal softmax, forward and backward), keyed like prep_cache.  The
   // buffer is made, and the producer told to fill it, only when a GEMM's
@@ -514,14 +518,14 @@ struct Executor {
   // a step once produced, so one preparation serves every later GEMM that
   // reads the same operand the same way.
   Prepared prepare(StepList& out, Slot* x, bool is_a, bool trans, int64_t ld, int64_t bs,
-                   int batch, int64_t M, int64_t N, int64_t K, bool need_lo = true) {
+                   int batch, int64_t M, int64_t N, int64_t K, int gmode, bool need_lo = true) {
     const int64_t R = is_a ? (trans ? K : M) : (trans ? N : K);
     const int64_t C = is_a ? (trans ? M : K) : (trans ? K : N);
     const bool mn_major = is_a ? trans : !trans;
     const bool contiguous = ld == C && (batch == 1 || bs == R * C);
     const double flops = 2.0 * batch * (double)M * N * K;
     const bool transpose = mn_major && contiguous && (double)batch * R * C * 2000.0 <= flops;
-    const bool strict = plan_matmul_mode == kGemmStrict;
+    const bool strict = gmode == kGemmStrict;
     Prepared p;
     p.hi = x;
     p.trans = trans;
@@ -576,6 +580,24 @@ struct Executor {
     return p;
   }
 
+  // The split-fp16 packing of GEMM operand x with `rows` rows (M of A, N of
+  // B), once per step (launch_pack16); returns the packed buffer.
+  Slot* pack16(StepList& out, Slot* x, bool k_contiguous, int64_t rows, int64_t K, int64_t ld) {
+    auto key = std::make_tuple(x, k_contiguous, rows, K, ld);
+    if (auto it = pack_cache.find(key); it != pack_cache.end()) return it->second;
+    Slot* packed = alloc((size_t)gemm_pack16_elems(rows, K));
+    out.push_back([=](cudaStream_t st) { launch_pack16(x->p, k_contiguous, rows, K, ld, packed->p, st); });
+    pack_cache[key] = packed;
+    return packed;
+  }
+
+  // The mode this GEMM runs in (kGemmStrict16 covers only some shapes).
+  int gemm_mode_for(int batch, int64_t M, int64_t N, int64_t K, int tri, bool smx, int64_t ldc, int64_t sc) const {
+    return gemm_effective_mode(plan_matmul_mode, batch, M, N, K, tri, smx, ldc, sc);
+  }
+  // The 3xTF32 / 1xTF32 / exact mode of GEMMs the split-fp16 form does not cover.
+  int tf32_mode() const { return plan_matmul_mode == kGemmStrict16 ? kGemmStrict : plan_matmul_mode; }
+
   void gemm_step(StepList& out, int batch, int64_t M, int64_t N, int64_t K, Slot* a,
                  bool ta, int64_t lda, int64_t sa, Slot* b, bool tb, int64_t ldb, int64_t sb,
                  Slot* c, int64_t ldc, int64_t sc, Slot* bias, float alpha, bool acc, bool relu,
@@ -583,15 +605,22 @@ struct Executor {
     Prepared pa, pb;
     pa.hi = a, pa.trans = ta, pa.ld = lda, pa.bs = sa;
     pb.hi = b, pb.trans = tb, pb.ld = ldb, pb.bs = sb;
-    const bool tc = plan_matmul_mode != kGemmExact && K > 0 && tma_aligned(lda, sa, batch) &&
-                    tma_aligned(ldb, sb, batch);
-    if (tc) {
-      const bool conv_a = gemm_converts_a(batch, M, N, K, plan_matmul_mode, ldc, sc);
-      pa = prepare(out, a, true, ta, lda, sa, batch, M, N, K, !conv_a);
-      pb = prepare(out, b, false, tb, ldb, sb, batch, M, N, K);
+    const int mode_now = gemm_mode_for(batch, M, N, K, tri, smx_p != nullptr, ldc, sc);
+    if (mode_now == kGemmStrict16) {
+      // Both operands packed K-major (op(A) is [M, K], op(B) is [K, N]).
+      pa.lo = pack16(out, a, !ta, M, K, lda);
+      pb.lo = pack16(out, b, tb, N, K, ldb);
+    } else {
+      const bool tc = mode_now != kGemmExact && K > 0 && tma_aligned(lda, sa, batch) && tma_aligned(ldb, sb, batch);
+      if (tc) {
+        const bool conv_a = gemm_converts_a(batch, M, N, K, mode_now, ldc, sc);
+        pa = prepare(out, a, true, ta, lda, sa, batch, M, N, K, mode_now, !conv_a);
+        pb = prepare(out, b, false, tb, ldb, sb, batch, M, N, K, mode_now);
+      }
     }
+    const bool tc = mode_now == kGemmStrict16 ||
+                    (mode_now != kGemmExact && K > 0 && tma_aligned(lda, sa, batch) && tma_aligned(ldb, sb, batch));
     Context* cx = ctx;
-    const int mode_now = plan_matmul_mode;
     const int chunk_now = plan_accum_chunk;
     // A residual is added in the GEMM's epilogue where the kernel form has
     // it (operand layouts as prepared); otherwise by a kernel after it.
@@ -1353,7 +1382,7 @@ struct Executor {
             // only here, so the wholly masked (exact zero) groups are not
             // stored.
             std::shared_ptr<LazyLo> lo;
-            if (lhs && plan_matmul_mode == kGemmStrict && w % 4 == 0)
+            if (lhs && tf32_mode() == kGemmStrict && w % 4 == 0)
               lo = offer_lo(std::make_tuple(c, false, q, w, w, q * w, outer), (size_t)n);
             forward.push_back([=](cudaStream_t st) {
               launch_masked_softmax(src->p, c->p, outer, q, w, leak ? leak->p : nullptr, lo && lo->slot ? lo->slot->p : nullptr,
@@ -1463,7 +1492,7 @@ struct Executor {
     std::vector<int64_t> lead(l.shape.begin(), l.shape.end() - 2);
     const int batch = (int)numel(lead);
     if (!tma_aligned(n, m * n, batch) || !tma_aligned(n, k * n, batch)) return false;
-    if (!gemm_fuses_box_epilogue(batch, m, k, n, false, true, plan_matmul_mode, k, m * k)) return false;
+    if (!gemm_fuses_box_epilogue(batch, m, k, n, false, true, tf32_mode(), k, m * k)) return false;
     auto [d, acc] = contrib(mi->second);
     gemm_step(backward, batch, m, k, n, g, false, n, m * n, r.slot, true, n, k * n, d, k, m * k, nullptr, alpha, acc,
               false, 1, l.slot);
@@ -1840,7 +1869,7 @@ struct Executor {
           // matmul, its strict backward GEMMs read this gradient's low part
           // from here; a fresh zero-filled gradient skips its masked zeros.
           std::shared_ptr<LazyLo> lo;
-          if (!acc && folded_scale.count(mi->second) && plan_matmul_mode == kGemmStrict && k % 4 == 0)
+          if (!acc && folded_scale.count(mi->second) && tf32_mode() == kGemmStrict && k % 4 == 0)
             lo = offer_lo(std::make_tuple(d, false, q, k, k, q * k, outer), (size_t)n);
           const int skip = acc ? 0 : 1;
           backward.push_back([=](cudaStream_t st) {

@@ -19,10 +19,18 @@
 // transposed products of backward (dY.W^T, X^T.dY) read the stored tensors
 // directly.
 //
+// Split-fp16 strict mode (kGemmStrict16): the operands are packed K-major
+// into fp16 high and low halves with a power-of-two scale per row
+// (launch_pack16), the persistent pair kernel issues the same three products
+// with tcgen05.mma.kind::f16 (twice the tf32 rate per instruction slot: 16
+// elements of K per 32-byte slice instead of 8), and the epilogue multiplies
+// each output by its row's and column's inverse scales (exact powers of two).
+//
 // CUDA-core path: products and sums rounded separately in increasing k
 // order (bit-identical to a sequential fp32 loop).  It serves shapes whose
 // strides break TMA's 16-byte rules and the opt-in exact mode.
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 
 #include <mutex>
 
@@ -578,6 +586,23 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// The same MMA over fp16 operands (both A and B fp16; fp32 accumulator).
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+template <bool kF16>
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  if (kF16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, accumulate);
+  else umma_tf32_pair(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
 // MMA completion signalled on the barrier at this offset in both CTAs.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
   asm volatile(
@@ -813,6 +838,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsTC, 1)
 // accumulator warps add column c and c + 128 of each chunk.  A 128-wide
 // instruction costs nearly as much to issue as a 256-wide one, and the
 // N <= 128 GEMMs (attention with head dim 128) are bound by that.
+//
+// kF16 (split-fp16 strict mode, both operands K-major): the four maps
+// address the packed fp16 halves (a_hi, a_lo, b_hi, b_lo); a stage holds
+// the same 64-byte rows, now 32 elements of K, and each 32-byte slice is one
+// kind::f16 MMA of K = 16.  Chunks of tensor-memory accumulation cover half
+// as many k-blocks, i.e. the same elements of K.  The accumulator warps
+// multiply each sum by row_factor[m] * col_factor[n] (a power of two) before
+// the epilogue.
 // ---------------------------------------------------------------------------
 
 template <bool kConvA>
@@ -838,7 +871,7 @@ struct PipeCfgP {
 template <int BN>
 __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_rows, int n_tiles, int rank,
                                         int tri, int K, int* bz, int* m0, int* n0, int* kb_begin, int* kb_end,
-                                        int splits = 1, int total_tiles = 0, int* ks = nullptr) {
+                                        int splits = 1, int total_tiles = 0, int* ks = nullptr, int bk = BK) {
   constexpr int kGroupP = kGroupM / 2;
   // Split-K: tile t covers part t / total_tiles of the K range of output
   // tile t % total_tiles.
@@ -858,7 +891,7 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   *n0 = (in_group / gsize) * BN;
   *m0 = pr0 + rank * BM;
   *kb_begin = 0;
-  *kb_end = (K + BK - 1) / BK;
+  *kb_end = (K + bk - 1) / bk;
   if (tri != 0 && causal_range(tri, pr0, 2 * BM, *n0, kb_begin, kb_end)) return false;
   if (*kb_end < *kb_begin) *kb_end = *kb_begin;
   if (splits > 1) {
@@ -871,7 +904,7 @@ __device__ __forceinline__ bool pp_tile(int t, int tiles_per_batch, int pair_row
   return true;
 }
 
-template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB, int kEpi>
+template <int BN, bool kStrict, bool kAmn, bool kBmn, bool kConvA, bool kStackB, int kEpi, bool kF16 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>(), 1)
     gemm_tf32_pp_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_alo,
@@ -895,6 +928,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   constexpr int kStageBytes = Cfg::kStageBytes;
   static_assert(!kConvA || kStrict, "A's low part is only used in strict mode");
   static_assert(!kStackB || (kStrict && BN == 128), "stacked B is the strict N <= 128 form");
+  static_assert(!kF16 || (kStrict && !kConvA && !kStackB && !kAmn && !kBmn && kEpi != 1),
+                "the split-fp16 form reads four K-major packed halves");
+  constexpr int kBK = kF16 ? 2 * BK : BK;  // elements of K per stage (64-byte rows)
   static_assert(((kConvA ? 4 : 2) * kStages + 4 + 2 * kAccWarps) * 8 + 4 <= 512, "barriers exceed their reserve");
   static_assert(kA % (16 * 64) == 0, "converter warps cover the A tile in float4 rounds");
   // Both CTAs' loads on the even CTA's "full" barrier (with kConvA: B only).
@@ -905,7 +941,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
   constexpr uint32_t kTmemCols = 2 * kBufCols;
   constexpr int kHalf = BN / 2;  // columns per accumulator warp
   constexpr int kBH = BN / 2;    // rows (K-major) or columns (MN-major) of B per CTA
-  constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kAmn ? 1u : 0u) << 15) |
+  // Operand formats: tf32 = 2; f16 = 0 (kind::f16); accumulator f32.
+  constexpr uint32_t kFmt = kF16 ? 0u : 2u;
+  constexpr uint32_t kIdesc = (1u << 4) | (kFmt << 7) | (kFmt << 10) | ((kAmn ? 1u : 0u) << 15) |
                               ((kBmn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
                               ((uint32_t)(256 >> 4) << 24);
   constexpr uint32_t kIdescWide = (kIdesc & ~(0x3Fu << 17)) | ((uint32_t)((2 * BN) >> 3) << 17);
@@ -972,7 +1010,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     uint32_t it = 0;
     for (int t = cluster; t < total && ok; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks, kBK))
         continue;
       const int nb0 = n0 + rank * kBH;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
@@ -984,7 +1022,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         const uint32_t afb = smem_u32(&afull_bar[s]);
         if (kConvA) mbar_expect_tx(afb, kA);
         const uint32_t base = smem_u32(smem + s * kStageBytes);
-        const int k0 = kb * BK;
+        const int k0 = kb * kBK;
         const int nmaps = kStrict ? 2 : 1;
         for (int h = 0; h < nmaps; ++h) {
           const CUtensorMap* ma = h ? &map_alo : &map_a;
@@ -1035,11 +1073,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     }
   } else if (warp == 1 && lane == 0 && leader) {
     // MMA issuer (even CTA): stage counter and chunk counter across tiles.
-    const int ckb = chunk_kb(ep);
+    const int ckb = kF16 ? (chunk_kb(ep) + 1) / 2 : chunk_kb(ep);
     uint32_t it = 0, gch = 0;  // stages and chunks issued so far (all tiles)
     for (int t = cluster; t < total && ok; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, 0, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks, kBK))
         continue;
       const int nkb = kb1 - kb0;
       int cpos = 0;  // k-block within the chunk
@@ -1073,9 +1111,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
             umma_tf32_pair(d, da, db, kIdescWide, acc);
             umma_tf32_pair(d, operand_desc(talo, kAmn, kk), operand_desc(tb + 2 * kB, kBmn, kk), kIdesc, 1u);
           } else if (kStrict) {
-            umma_tf32_pair(d, operand_desc(talo, kAmn, kk), db, kIdesc, acc);
-            umma_tf32_pair(d, da, operand_desc(tblo, kBmn, kk), kIdesc, 1u);
-            umma_tf32_pair(d, da, db, kIdesc, 1u);
+            umma_pair<kF16>(d, operand_desc(talo, kAmn, kk), db, kIdesc, acc);
+            umma_pair<kF16>(d, da, operand_desc(tblo, kBmn, kk), kIdesc, 1u);
+            umma_pair<kF16>(d, da, db, kIdesc, 1u);
           } else {
             umma_tf32_pair(d, da, db, kIdesc, acc);
           }
@@ -1097,7 +1135,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     uint32_t it = 0;
     for (int t = cluster; t < total && ok; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks, kBK))
         continue;
       for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
         const int s = (int)(it % kStages);
@@ -1134,7 +1172,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
     bool have = true;
     for (int t = cluster; t < total && have; t += clusters) {
       int bz, m0, n0, kb0, kb1, ks;
-      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks))
+      if (!pp_tile<BN>(t, tiles_per_batch, pair_rows, n_tiles, rank, ep.tri, K, &bz, &m0, &n0, &kb0, &kb1, splits, out_tiles, &ks, kBK))
         continue;
       if (smx) {
         // The tile's first two probability boxes load while the tensor core
@@ -1151,7 +1189,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
         }
         y_pending += kBoxes < 2 ? kBoxes : 2;
       }
-      const int nch = (kb1 - kb0 + chunk_kb(ep) - 1) / chunk_kb(ep);
+      const int ckb = kF16 ? (chunk_kb(ep) + 1) / 2 : chunk_kb(ep);
+      const int nch = (kb1 - kb0 + ckb - 1) / ckb;
       float acc[kHalf];
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
@@ -1184,7 +1223,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
       if (!have) break;
       // Epilogue of this warp's 32 rows x kHalf columns.
       const int col0 = n0 + half * kHalf;
-      if (splits == 1) {
+      // kF16: the operands' row scales are undone (exact powers of two in
+      // [2^-126, 2^126]), then alpha, bias and relu applied, four columns at
+      // a time as the boxes are written, which keeps the register pressure
+      // at the accumulator's kHalf values.
+      const int frow = m0 + quad * 32 + lane;
+      const float fr = kF16 ? (frow < M ? ep.row_factor[frow] : 0.0f) : 1.0f;
+      auto value4 = [&](int i) -> float4 {
+        float4 v = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        if (kF16) {
+          const int c = col0 + i;  // a multiple of 4: col_factor is 16-byte aligned
+          float4 f;
+          if (c + 3 < N) {
+            f = __ldg((const float4*)(ep.col_factor + c));
+          } else {
+            f.x = c < N ? ep.col_factor[c] : 0.0f;
+            f.y = c + 1 < N ? ep.col_factor[c + 1] : 0.0f;
+            f.z = c + 2 < N ? ep.col_factor[c + 2] : 0.0f;
+            f.w = 0.0f;
+          }
+          v.x = v.x * (fr * f.x);
+          v.y = v.y * (fr * f.y);
+          v.z = v.z * (fr * f.z);
+          v.w = v.w * (fr * f.w);
+          if (splits == 1) {
+            float* e = &v.x;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float r = e[q] * ep.alpha;
+              if (ep.bias != nullptr && c + q < N) r = r + ep.bias[c + q];
+              if (ep.relu) r = fmaxf(r, 0.0f);
+              e[q] = r;
+            }
+          }
+        }
+        return v;
+      };
+      if (splits == 1 && !kF16) {
 #pragma unroll
         for (int i = 0; i < kHalf; ++i) {
           float r = acc[i] * ep.alpha;
@@ -1211,7 +1286,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
             const uint32_t a = box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4);
             const float4 p = ld_shared_f4(a);
             const int c = col0 + 32 * b + 4 * j;
-            const float* v = &acc[b * 32 + 4 * j];
+            const float4 v4 = value4(b * 32 + 4 * j);
+            const float* v = &v4.x;
             if (kEpi == 1)
               st_shared_f4(a, c > row ? 0.0f : (p.x * (1.0f - p.x)) * v[0],
                            c + 1 > row ? 0.0f : (p.y * (1.0f - p.y)) * v[1],
@@ -1226,9 +1302,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pp_threads<kConvA>()
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st_shared_f4(box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4), acc[b * 32 + 4 * j],
-                         acc[b * 32 + 4 * j + 1], acc[b * 32 + 4 * j + 2], acc[b * 32 + 4 * j + 3]);
+          for (int j = 0; j < 8; ++j) {
+            const float4 v4 = value4(b * 32 + 4 * j);
+            st_shared_f4(box + (uint32_t)lane * 128u + (uint32_t)((j ^ (lane & 7)) << 4), v4.x, v4.y, v4.z, v4.w);
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -1280,6 +1357,133 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
     if (ep.relu) r = fmaxf(r, 0.0f);
     float* dst = out.ptr + (int64_t)b * out.batch_stride + (int64_t)row * out.ld + col;
     *dst = ep.accumulate ? *dst + r : r;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split-fp16 packing (kGemmStrict16 operands; layout in gemm_pack16_elems's
+// declaration).
+// ---------------------------------------------------------------------------
+
+// 2^e as a float, e in [-126, 127].
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+// The row scale exponent for a row whose largest magnitude is mx: the e
+// with mx 2^e in [2^14, 2^15), from mx's exponent field, clamped to
+// [-63, 63] (so row and column factors multiply to a normal float); 0 when
+// mx is zero or infinite (the row's products are then 0, inf or NaN
+// whatever the scale).
+__device__ __forceinline__ int pack16_exponent(float mx) {
+  const int field = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
+  if (mx == 0.0f || field == 0xFF) return 0;
+  const int e = 14 - (field == 0 ? -127 : field - 127);
+  return e < -63 ? -63 : (e > 63 ? 63 : e);
+}
+
+__device__ __forceinline__ void pack16_one(float x, float up, __half* hi, __half* lo) {
+  const float xs = x * up;  // exact: a power-of-two scale
+  const __half h = __float2half_rn(xs);
+  *hi = h;
+  *lo = __float2half_rn(xs - __half2float(h));  // xs - h is exact in fp32
+}
+
+__device__ __forceinline__ float block_max256(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) v = fmaxf(v, red[w]);
+  return v;
+}
+
+// K-contiguous operand x [R][ld]: one 256-thread block per row; the row is
+// read twice (its maximum, then the halves; the second read hits cache).
+__global__ void __launch_bounds__(256) pack16_rows_kernel(const float* __restrict__ x, int64_t ld, int K, int Kp,
+                                                          __half* __restrict__ hi, __half* __restrict__ lo,
+                                                          float* __restrict__ factor) {
+  __shared__ float red[8];
+  const int r = blockIdx.x;
+  const float* row = x + (int64_t)r * ld;
+  const bool vec = ((ld & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
+  const int K4 = vec ? K >> 2 : 0;
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < K4; i += 256) {
+    const float4 v = __ldg((const float4*)row + i);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  for (int i = 4 * K4 + threadIdx.x; i < K; i += 256) mx = fmaxf(mx, fabsf(row[i]));
+  mx = block_max256(mx, red);
+  const int e = pack16_exponent(mx);
+  const float up = pow2f(e);
+  if (threadIdx.x == 0) factor[r] = pow2f(-e);
+  __half* h = hi + (int64_t)r * Kp;
+  __half* l = lo + (int64_t)r * Kp;
+  for (int i = threadIdx.x; i < K4; i += 256) {
+    const float4 v = __ldg((const float4*)row + i);
+    __align__(8) __half hv[4], lv[4];
+    pack16_one(v.x, up, &hv[0], &lv[0]);
+    pack16_one(v.y, up, &hv[1], &lv[1]);
+    pack16_one(v.z, up, &hv[2], &lv[2]);
+    pack16_one(v.w, up, &hv[3], &lv[3]);
+    *(uint2*)(h + 4 * i) = *(const uint2*)hv;  // Kp % 8 == 0: 8-byte aligned
+    *(uint2*)(l + 4 * i) = *(const uint2*)lv;
+  }
+  for (int i = 4 * K4 + threadIdx.x; i < K; i += 256) pack16_one(row[i], up, h + i, l + i);
+}
+
+// R-contiguous operand x [K][ld], pass 1: each column's largest magnitude,
+// as float bits (non-negative floats order like their bits), atomically
+// maxed into colmax[R] (zeroed before).  Block: 64 columns x 4 row lanes
+// over a slab of 64 rows.
+__global__ void __launch_bounds__(256) pack16_colmax_kernel(const float* __restrict__ x, int64_t ld, int R, int K,
+                                                            uint32_t* __restrict__ colmax) {
+  __shared__ float part[4][64];
+  const int c = blockIdx.x * 64 + (threadIdx.x & 63);
+  const int lane4 = threadIdx.x >> 6;
+  const int k0 = blockIdx.y * 64;
+  float mx = 0.0f;
+  if (c < R)
+    for (int k = k0 + lane4; k < K && k < k0 + 64; k += 4) mx = fmaxf(mx, fabsf(x[(int64_t)k * ld + c]));
+  part[lane4][threadIdx.x & 63] = mx;
+  __syncthreads();
+  if (threadIdx.x < 64 && c < R) {
+    const float m = fmaxf(fmaxf(part[0][threadIdx.x], part[1][threadIdx.x]), fmaxf(part[2][threadIdx.x], part[3][threadIdx.x]));
+    atomicMax(&colmax[c], __float_as_uint(m));
+  }
+}
+
+// Pass 2: a 64 (K) x 64 (columns) tile through shared memory, written as
+// 64 K-major output rows of 64 halves (hi and lo); blocks of the first K
+// tile also write the factors.
+__global__ void __launch_bounds__(256) pack16_cols_kernel(const float* __restrict__ x, int64_t ld, int R, int K, int Kp,
+                                                          const uint32_t* __restrict__ colmax, __half* __restrict__ hi,
+                                                          __half* __restrict__ lo, float* __restrict__ factor) {
+  __shared__ float tile[64][65];
+  const int c0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
+  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+    const int kr = i >> 6, cc = i & 63;
+    const int k = k0 + kr, c = c0 + cc;
+    tile[kr][cc] = (k < K && c < R) ? x[(int64_t)k * ld + c] : 0.0f;
+  }
+  __syncthreads();
+  const int cc = threadIdx.x & 63, j = threadIdx.x >> 6;  // output row c0 + cc, K elements 16 j .. 16 j + 15
+  const int c = c0 + cc;
+  if (c >= R) return;
+  const int e = pack16_exponent(__uint_as_float(colmax[c]));
+  const float up = pow2f(e);
+  if (blockIdx.y == 0 && j == 0) factor[c] = pow2f(-e);
+  __align__(16) __half hv[16], lv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) pack16_one(tile[16 * j + i][cc], up, &hv[i], &lv[i]);
+  __half* h = hi + (int64_t)c * Kp + k0 + 16 * j;
+  __half* l = lo + (int64_t)c * Kp + k0 + 16 * j;
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    if (k0 + 16 * j + 8 * g >= Kp) break;  // Kp % 8 == 0: whole 16-byte groups
+    *(uint4*)(h + 8 * g) = *(const uint4*)(hv + 8 * g);
+    *(uint4*)(l + 8 * g) = *(const uint4*)(lv + 8 * g);
   }
 }
 
@@ -1459,6 +1663,22 @@ CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, uint64_t
   return m;
 }
 
+// Rank-3 fp16 tensor map {inner, outer, 1} over a packed operand half
+// (rows of ld elements, ld % 8 == 0).
+CUtensorMap make_map16(const __half* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                       uint32_t box_outer) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {inner, outer, 1};
+  cuuint64_t strides[2] = {ld * 2, ld * 2 * outer};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void*)base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled (fp16) failed (" + std::to_string(r) + ")");
+  return m;
+}
+
 bool tma_ok(const GemmOperand& X, int batch) {
   if (((uintptr_t)X.ptr & 15) != 0) return false;
   if ((X.ld & 3) != 0) return false;
@@ -1514,12 +1734,12 @@ int sm_count() {
   return counts[dev];
 }
 
-template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK, int EPI = 0>
+template <int BN, bool S, bool AMN, bool BMN, bool CONV, bool STACK, int EPI = 0, bool F16 = false>
 void launch_pp(const CUtensorMap& ma, const CUtensorMap& malo, const CUtensorMap& mb, const CUtensorMap& mblo,
                const CUtensorMap& mc32, const CUtensorMap& my, const GemmEpilogue& ep, int batch, int M, int N, int K,
                int splits, int* d_err, cudaStream_t st) {
   constexpr int smem = PipeCfgP<BN, S, STACK>::kSmem;
-  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK, EPI>;
+  auto kern = gemm_tf32_pp_kernel<BN, S, AMN, BMN, CONV, STACK, EPI, F16>;
   static bool configured = false;
   if (!configured) {
     TYSOR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1655,6 +1875,49 @@ void launch_wait_timeout_probe(int* err, long long limit_cycles, cudaStream_t st
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+int64_t gemm_pack16_elems(int64_t rows, int64_t K) {
+  const int64_t kp = (K + 7) & ~(int64_t)7;
+  return rows * kp + 2 * ((rows + 3) & ~(int64_t)3);
+}
+
+void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, int64_t ld, float* packed,
+                   cudaStream_t st) {
+  if (rows <= 0 || K <= 0) return;
+  if (rows > INT32_MAX / 2 || K > INT32_MAX / 2) throw CudaError("pack16: operand too large");
+  if ((((uintptr_t)packed) & 15) != 0) throw CudaError("pack16: packed buffer not 16-byte aligned");
+  const int64_t kp = (K + 7) & ~(int64_t)7;
+  __half* hi = (__half*)packed;
+  __half* lo = hi + rows * kp;
+  float* factor = (float*)(lo + rows * kp);
+  if (k_contiguous) {
+    if (ld < K) throw CudaError("pack16: row pitch below K");
+    pack16_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(x, ld, (int)K, (int)kp, hi, lo, factor);
+    TYSOR_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return;
+  }
+  if (ld < rows) throw CudaError("pack16: row pitch below the operand's rows");
+  if (ceil_div(K, 64) > 65535) throw CudaError("pack16: K too large for the column pass");
+  uint32_t* colmax = (uint32_t*)(factor + ((rows + 3) & ~(int64_t)3));
+  TYSOR_CUDA(cudaMemsetAsync(colmax, 0, sizeof(uint32_t) * (size_t)rows, st));
+  const dim3 grid((unsigned)ceil_div(rows, 64), (unsigned)ceil_div(K, 64));
+  pack16_colmax_kernel<<<grid, 256, 0, st>>>(x, ld, (int)rows, (int)K, colmax);
+  TYSOR_CUDA(cudaGetLastError());
+  pack16_cols_kernel<<<grid, 256, 0, st>>>(x, ld, (int)rows, (int)K, (int)kp, colmax, hi, lo, factor);
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(2, std::memory_order_relaxed);
+}
+
+int gemm_effective_mode(int mode, int batch, int64_t M, int64_t N, int64_t K, int tri, bool smx, int64_t ldc,
+                        int64_t stride_c) {
+  (void)stride_c;
+  if (mode != kGemmStrict16) return mode;
+  const bool ok = batch == 1 && tri == 0 && !smx && K > 0 && M >= 256 && N > 128 && (ldc & 3) == 0 &&
+                  g_two_sm_enabled && g_persistent_enabled && M <= INT32_MAX / 2 && N <= INT32_MAX / 2 &&
+                  K <= INT32_MAX / 2 && ceil_div(K, 64) <= 65535;
+  return ok ? kGemmStrict16 : kGemmStrict;
+}
+
 void launch_split_lo(const float* x, float* lo, int64_t n, cudaStream_t st) {
   if (n <= 0) return;
   split_lo_kernel<<<elementwise_blocks(n / 4 + 1, 256), 256, 0, st>>>(x, lo, n);
@@ -1682,6 +1945,13 @@ void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOpe
                        const GemmOperand& B, int mode, int64_t* a_elems, int64_t* b_elems) {
   *a_elems = 0;
   *b_elems = 0;
+  if (mode == kGemmStrict16) {
+    if (M > 0 && N > 0 && K > 0) {
+      *a_elems = gemm_pack16_elems(M, K);
+      *b_elems = gemm_pack16_elems(N, K);
+    }
+    return;
+  }
   if (mode != kGemmStrict || !tma_ok(A, batch) || !tma_ok(B, batch) || M == 0 || N == 0 ||
       K == 0)
     return;
@@ -1691,6 +1961,11 @@ void gemm_scratch_need(int batch, int64_t M, int64_t N, int64_t K, const GemmOpe
 
 bool gemm_fuses_box_epilogue(int batch, int64_t M, int64_t N, int64_t K, bool ta, bool tb, int mode,
                              int64_t ldc, int64_t stride_c) {
+  // The split-fp16 form packs both operands K-major and adds a residual in
+  // its epilogue (it has no fused softmax backward: gemm_effective_mode
+  // sends those GEMMs to 3xTF32).
+  if (mode == kGemmStrict16)
+    return gemm_effective_mode(mode, batch, M, N, K, 0, false, ldc, stride_c) == kGemmStrict16;
   return mode == kGemmStrict && K > 0 && !ta && tb && N > 128 && g_two_sm_enabled && g_persistent_enabled &&
          g_conv_a_enabled && M >= 256 && (ldc & 3) == 0 && (batch == 1 || (stride_c & 3) == 0) &&
          M <= INT32_MAX / 2 && N <= INT32_MAX / 2 && K <= INT32_MAX / 2;
@@ -1699,6 +1974,58 @@ bool gemm_fuses_box_epilogue(int batch, int64_t M, int64_t N, int64_t K, bool ta
 int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
                      const GemmOutput& C, const GemmEpilogue& ep, int mode, const GemmScratch& scratch, int* d_err,
                      cudaStream_t st, bool* fused_smx);
+
+// The split-fp16 GEMM (one batch item; gemm_effective_mode holds): packs A
+// and B into the scratch (unless presplit), then the persistent pair kernel
+// in its kF16 form, split-K where it pays, the residual in the epilogue.
+static int launch_f16x3(int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B, const GemmOutput& C,
+                 const GemmEpilogue& ep_in, const GemmScratch& scratch, int* d_err, cudaStream_t st, bool* fused) {
+  const int64_t na = gemm_pack16_elems(M, K), nb = gemm_pack16_elems(N, K);
+  if (scratch.a_lo == nullptr || scratch.b_lo == nullptr || scratch.a_elems < na || scratch.b_elems < nb)
+    throw CudaError("split-fp16 matmul needs scratch for the packed operands (M " + std::to_string(M) + ", N " +
+                    std::to_string(N) + ", K " + std::to_string(K) + ")");
+  if ((((uintptr_t)C.ptr) & 15) != 0) throw CudaError("split-fp16 matmul needs a 16-byte aligned output");
+  if (!scratch.presplit) {
+    launch_pack16(A.ptr, !A.trans, M, K, A.ld, scratch.a_lo, st);
+    launch_pack16(B.ptr, B.trans, N, K, B.ld, scratch.b_lo, st);
+  }
+  const int64_t kp = (K + 7) & ~(int64_t)7;
+  const __half* ahi = (const __half*)scratch.a_lo;
+  const __half* bhi = (const __half*)scratch.b_lo;
+  GemmEpilogue ep = ep_in;
+  ep.row_factor = (const float*)(ahi + 2 * M * kp);
+  ep.col_factor = (const float*)(bhi + 2 * N * kp);
+  const CUtensorMap ma = make_map16(ahi, K, M, kp, 2 * BK, BM);
+  const CUtensorMap malo = make_map16(ahi + M * kp, K, M, kp, 2 * BK, BM);
+  const CUtensorMap mb = make_map16(bhi, K, N, kp, 2 * BK, 128);
+  const CUtensorMap mblo = make_map16(bhi + N * kp, K, N, kp, 2 * BK, 128);
+  int splits = 1;
+  const int64_t ldw = (N + 3) & ~(int64_t)3;
+  if (!ep.residual && scratch.ws != nullptr && (((uintptr_t)scratch.ws) & 15) == 0) {
+    splits = splitk_parts(1, M, N, K);
+    if ((int64_t)splits * M * ldw > scratch.ws_elems) splits = 1;
+  }
+  const CUtensorMap mc32 = splits > 1 ? make_map(scratch.ws, N, M, (uint64_t)splits, ldw, M * ldw, 32, 32,
+                                                 CU_TENSOR_MAP_SWIZZLE_128B)
+                                      : make_map(C.ptr, N, M, 1, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap my =
+      ep.residual ? make_map(ep.residual, N, M, 1, C.ld, C.batch_stride, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) : mc32;
+  const int im = (int)M, in = (int)N, ik = (int)K;
+  if (ep.residual) {
+    launch_pp<256, true, false, false, false, false, 2, true>(ma, malo, mb, mblo, mc32, my, ep, 1, im, in, ik, 1,
+                                                             d_err, st);
+    *fused = true;
+  } else {
+    launch_pp<256, true, false, false, false, false, 0, true>(ma, malo, mb, mblo, mc32, my, ep, 1, im, in, ik, splits,
+                                                             d_err, st);
+  }
+  if (splits > 1) {
+    splitk_reduce_kernel<<<elementwise_blocks(M * N, 256), 256, 0, st>>>(scratch.ws, splits, 1, im, in, ldw, C, ep);
+    TYSOR_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
+  return 1;
+}
 
 int gemm_causal_tile_rows(int batch, int64_t M, int64_t N, int64_t K, const GemmOperand& A, const GemmOperand& B,
                           const GemmOutput& C, int mode) {
@@ -1737,6 +2064,11 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
   if (M <= 0 || N <= 0 || batch <= 0) return 0;
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
     throw CudaError("matmul dimension too large");
+  if (mode == kGemmStrict16) {
+    if (gemm_effective_mode(mode, batch, M, N, K, ep.tri, ep.smx_p != nullptr, C.ld, C.batch_stride) != kGemmStrict16)
+      throw CudaError("split-fp16 matmul requested for a GEMM it does not cover (gemm_effective_mode)");
+    return launch_f16x3(M, N, K, A, B, C, ep, scratch, d_err, st, fused_smx);
+  }
   const bool tc = mode != kGemmExact && K > 0 && tma_ok(A, batch) && tma_ok(B, batch);
   if (!tc) {
     // (K == 0 lands here too: the loop adds nothing and the epilogue writes

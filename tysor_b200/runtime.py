@@ -29,7 +29,7 @@ from . import native
 from .graph import Graph
 from .native import check, fptr
 
-MATMUL_MODES = {"strict": 0, "fast": 1, "exact": 2}
+MATMUL_MODES = {"strict": 0, "fast": 1, "exact": 2, "strict16": 3}
 
 
 class CudaContext:
