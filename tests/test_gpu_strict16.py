@@ -116,3 +116,26 @@ def test_uncovered_shapes_run_strict(cuda_ctx, m, n, k, batch):
         finally:
             cuda_ctx.set_matmul_mode("strict")
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True)])
+def test_strict16_odd_row_pitch(cuda_ctx, ta, tb):
+    """Operands stored with a row pitch one element longer than the matrix
+    (not a multiple of 4): the packing kernels fall back to scalar loads."""
+    m, n, k = 260, 300, 200
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+
+    def padded(x):
+        out = np.zeros((x.shape[0], x.shape[1] + 1), np.float32)
+        out[:, :-1] = x
+        return out
+    a_st = padded(a.T if ta else a)
+    b_st = padded(b.T if tb else b)
+    cuda_ctx.set_matmul_mode("strict16")
+    try:
+        got = run_ex(cuda_ctx, a_st, ta, b_st, tb, m, n, k)
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    assert frob(got, oracle_mm(a, b)) < 1e-5

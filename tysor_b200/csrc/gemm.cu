@@ -1435,40 +1435,93 @@ __global__ void __launch_bounds__(256) pack16_rows_kernel(const float* __restric
 
 // R-contiguous operand x [K][ld], pass 1: each column's largest magnitude,
 // as float bits (non-negative floats order like their bits), atomically
-// maxed into colmax[R] (zeroed before).  Block: 64 columns x 4 row lanes
-// over a slab of 64 rows.
+// maxed into colmax[R] (zeroed before).  Block: 256 columns (64 threads x
+// float4) x 4 row lanes over a slab of 64 rows, 16 independent loads per
+// thread (scalar loads where ld or x breaks float4 alignment).
 __global__ void __launch_bounds__(256) pack16_colmax_kernel(const float* __restrict__ x, int64_t ld, int R, int K,
                                                             uint32_t* __restrict__ colmax) {
-  __shared__ float part[4][64];
-  const int c = blockIdx.x * 64 + (threadIdx.x & 63);
-  const int lane4 = threadIdx.x >> 6;
+  __shared__ float4 part[4][64];
+  const int c4 = threadIdx.x & 63, lane = threadIdx.x >> 6;
+  const int c = blockIdx.x * 256 + 4 * c4;
   const int k0 = blockIdx.y * 64;
-  float mx = 0.0f;
-  if (c < R)
-    for (int k = k0 + lane4; k < K && k < k0 + 64; k += 4) mx = fmaxf(mx, fabsf(x[(int64_t)k * ld + c]));
-  part[lane4][threadIdx.x & 63] = mx;
+  float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (c < R) {
+    const bool full = c + 3 < R && (ld & 3) == 0 && (((uintptr_t)x) & 15) == 0;
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int k = k0 + lane + 4 * i;
+      if (k >= K) break;
+      const float* p = x + (int64_t)k * ld + c;
+      float4 v;
+      if (full) {
+        v = __ldg((const float4*)p);
+      } else {
+        v.x = __ldg(p);
+        v.y = c + 1 < R ? __ldg(p + 1) : 0.0f;
+        v.z = c + 2 < R ? __ldg(p + 2) : 0.0f;
+        v.w = c + 3 < R ? __ldg(p + 3) : 0.0f;
+      }
+      m.x = fmaxf(m.x, fabsf(v.x));
+      m.y = fmaxf(m.y, fabsf(v.y));
+      m.z = fmaxf(m.z, fabsf(v.z));
+      m.w = fmaxf(m.w, fabsf(v.w));
+    }
+  }
+  part[lane][c4] = m;
   __syncthreads();
   if (threadIdx.x < 64 && c < R) {
-    const float m = fmaxf(fmaxf(part[0][threadIdx.x], part[1][threadIdx.x]), fmaxf(part[2][threadIdx.x], part[3][threadIdx.x]));
-    atomicMax(&colmax[c], __float_as_uint(m));
+    float4 r = part[0][c4];
+#pragma unroll
+    for (int l = 1; l < 4; ++l) {
+      const float4 q = part[l][c4];
+      r.x = fmaxf(r.x, q.x);
+      r.y = fmaxf(r.y, q.y);
+      r.z = fmaxf(r.z, q.z);
+      r.w = fmaxf(r.w, q.w);
+    }
+    atomicMax(&colmax[c], __float_as_uint(r.x));
+    if (c + 1 < R) atomicMax(&colmax[c + 1], __float_as_uint(r.y));
+    if (c + 2 < R) atomicMax(&colmax[c + 2], __float_as_uint(r.z));
+    if (c + 3 < R) atomicMax(&colmax[c + 3], __float_as_uint(r.w));
   }
 }
 
-// Pass 2: a 64 (K) x 64 (columns) tile through shared memory, written as
-// 64 K-major output rows of 64 halves (hi and lo); blocks of the first K
-// tile also write the factors.
+// Pass 2: a 64 (K) x 64 (columns) tile read with float4 loads into shared
+// memory, written as 64 K-major output rows of 64 halves: four threads per
+// output row, 16 elements of K each, so a warp writes 8 rows' 128-byte hi
+// and lo runs.  Blocks of the first K tile also write the factors.
 __global__ void __launch_bounds__(256) pack16_cols_kernel(const float* __restrict__ x, int64_t ld, int R, int K, int Kp,
                                                           const uint32_t* __restrict__ colmax, __half* __restrict__ hi,
                                                           __half* __restrict__ lo, float* __restrict__ factor) {
   __shared__ float tile[64][65];
   const int c0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
-  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
-    const int kr = i >> 6, cc = i & 63;
-    const int k = k0 + kr, c = c0 + cc;
-    tile[kr][cc] = (k < K && c < R) ? x[(int64_t)k * ld + c] : 0.0f;
+  {
+    const int c4 = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+    const int c = c0 + 4 * c4;
+    const bool aligned = (ld & 3) == 0 && (((uintptr_t)x) & 15) == 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kr = r0 + 16 * i, k = k0 + kr;
+      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (k < K && c < R) {
+        const float* p = x + (int64_t)k * ld + c;
+        if (aligned && c + 3 < R) {
+          v = __ldg((const float4*)p);
+        } else {
+          v.x = __ldg(p);
+          v.y = c + 1 < R ? __ldg(p + 1) : 0.0f;
+          v.z = c + 2 < R ? __ldg(p + 2) : 0.0f;
+          v.w = c + 3 < R ? __ldg(p + 3) : 0.0f;
+        }
+      }
+      tile[kr][4 * c4] = v.x;
+      tile[kr][4 * c4 + 1] = v.y;
+      tile[kr][4 * c4 + 2] = v.z;
+      tile[kr][4 * c4 + 3] = v.w;
+    }
   }
   __syncthreads();
-  const int cc = threadIdx.x & 63, j = threadIdx.x >> 6;  // output row c0 + cc, K elements 16 j .. 16 j + 15
+  const int cc = threadIdx.x >> 2, j = threadIdx.x & 3;  // output row c0 + cc, K elements 16 j .. 16 j + 15
   const int c = c0 + cc;
   if (c >= R) return;
   const int e = pack16_exponent(__uint_as_float(colmax[c]));
@@ -1900,10 +1953,11 @@ void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, i
   if (ceil_div(K, 64) > 65535) throw CudaError("pack16: K too large for the column pass");
   uint32_t* colmax = (uint32_t*)(factor + ((rows + 3) & ~(int64_t)3));
   TYSOR_CUDA(cudaMemsetAsync(colmax, 0, sizeof(uint32_t) * (size_t)rows, st));
-  const dim3 grid((unsigned)ceil_div(rows, 64), (unsigned)ceil_div(K, 64));
-  pack16_colmax_kernel<<<grid, 256, 0, st>>>(x, ld, (int)rows, (int)K, colmax);
+  pack16_colmax_kernel<<<dim3((unsigned)ceil_div(rows, 256), (unsigned)ceil_div(K, 64)), 256, 0, st>>>(
+      x, ld, (int)rows, (int)K, colmax);
   TYSOR_CUDA(cudaGetLastError());
-  pack16_cols_kernel<<<grid, 256, 0, st>>>(x, ld, (int)rows, (int)K, (int)kp, colmax, hi, lo, factor);
+  pack16_cols_kernel<<<dim3((unsigned)ceil_div(rows, 64), (unsigned)ceil_div(K, 64)), 256, 0, st>>>(
+      x, ld, (int)rows, (int)K, (int)kp, colmax, hi, lo, factor);
   TYSOR_CUDA(cudaGetLastError());
   g_launches.fetch_add(2, std::memory_order_relaxed);
 }
