@@ -9,7 +9,10 @@ all-reduce).
 forward + backward + SGD, tokens/s.  Per GPU: batch 8 x seq 2048 tokens,
 d_model 2048, 16 query heads / 4 KV heads (repeat_kv), head_dim 128, RoPE
 theta 1e4, causal mask, RMSNorm (gain, eps 1e-6), SwiGLU hidden 5632; fp32
-storage, strict 3xTF32 tensor-core matmuls.  Inputs x ~ N(0,1) (seeded per
+storage, strict tensor-core matmuls: by default the split-fp16 engine (the
+three products of 3xTF32 over fp16 halves with per-row power-of-two scales,
+`--matmul strict16`), with the same step timed on 3xTF32 (`--matmul strict`)
+reported beside it as `alt_matmul`.  Inputs x ~ N(0,1) (seeded per
 rank), weights ~ N(0, 0.02), gains ~ N(1, 0.02), all generated on the host
 from fixed seeds.  One step = forward, squared error against a seeded
 N(0,1) target (`d = out - target; loss = d * d`, summed as the reference
@@ -520,6 +523,38 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
+    # The same step with the other strict matmul engine (3xTF32 when the run
+    # uses strict16 and the reverse), timed the same way on the same box: the
+    # executor re-plans and re-captures its step for the new mode.
+    alt = None
+    if args.alt:
+        other = "strict" if args.matmul == "strict16" else "strict16"
+        ctx.set_matmul_mode(other)
+        ex.train(args.warmup, lr)  # re-planned: the inputs are uploaded from their host copies
+        for name, arr in pinned.items():  # device-resident again, as in the timed region above
+            native.check(lib.tysor_cuda_graph_upload_input(ex.handle, name.encode(), native.fptr(arr), arr.size))
+        ctx.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s_alt, e_alt = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(int(20e-3 * 1.9e9))
+        s_alt.record(stream)
+        ex.train(args.steps, lr)
+        e_alt.record(stream)
+        ctx.synchronize()
+        e_alt.synchronize()
+        ms_alt = s_alt.elapsed_time(e_alt)
+        if dist is not None:
+            t = torch.tensor([ms_alt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_alt = float(t.item())
+        ctx.set_matmul_mode(args.matmul)
+        alt = {"matmul": other, "value": round(total_units / (ms_alt / args.steps / 1000.0), 1), "unit": wl.unit,
+               "ms_per_step": round(ms_alt / args.steps, 3), "gpu_launches_per_step": ex.launch_count(),
+               "engine": "3xTF32 (kind::tf32)" if other == "strict" else "split-fp16 (kind::f16, per-row scales)"}
+
     roof = roofline(ctx, lib, stream, *wl.roof_gemm, mode=args.matmul) if rank == 0 else None
 
     cpu = None
@@ -546,7 +581,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "dtype": "f32 (3xTF32 tensor-core matmul)" if args.matmul == "strict" else
                      "f32 (3-product split-fp16 tensor-core matmul)",
             "data": "synthetic, seeded on the host (inputs N(0,1) or U ids, weights N(0,0.02), gains N(1,0.02))",
-            "config": cfg, "roofline": roof, "cpu_baseline": cpu,
+            "config": cfg, "roofline": roof, "cpu_baseline": cpu, "alt_matmul": alt,
             "e2e": {"value": round(total_units / e2e_s, 1), "unit": wl.unit,
                     "h2d_bytes_per_step": int(sum(a.nbytes for a in inputs.values())), "d2h_bytes_per_step": 4,
                     "h2d": "pinned host -> device on a copy stream, one step ahead (overlaps the previous step)",
@@ -603,8 +638,11 @@ def main():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="block", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--matmul", default="strict", choices=["strict", "strict16"],
-                   help="strict: 3xTF32; strict16: the three products over fp16 halves with per-row scales")
+    p.add_argument("--matmul", default="strict16", choices=["strict", "strict16"],
+                   help="strict16 (default): the three products of strict mode over fp16 halves with per-row "
+                        "power-of-two scales; strict: 3xTF32")
+    p.add_argument("--no-alt", dest="alt", action="store_false",
+                   help="skip timing the step with the other strict engine")
     p.add_argument("--accum-chunk", type=int, default=0,
                    help="k-blocks per tensor-memory accumulation chunk of the matmuls (0: default 8)")
     args = p.parse_args()

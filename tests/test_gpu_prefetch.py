@@ -112,3 +112,29 @@ def test_prefetch_queue_holds_two_values(cuda_ctx):
     ex.train(2, 0.0)  # takes one queued value (the call's first step); one stays queued
     ex.prefetch_input("x", data[0]["x"])
     ex.close()
+
+
+def test_replanning_forgets_uploaded_inputs(cuda_ctx):
+    """An input written by upload_input lives in the planned buffers; a
+    re-plan (here: a new matmul mode) makes new buffers, so the next step
+    must take the input from its host copy again, not read a buffer nothing
+    wrote."""
+    data = batches(2)
+    g, ex = make(cuda_ctx, data[0])
+    ex.train(1, 0.0)
+    for name, arr in data[1].items():
+        ex.upload_input(name, arr)
+    cuda_ctx.set_matmul_mode("exact")
+    try:
+        got = ex.train(1, 0.0)  # re-planned: the constructor's inputs (data[0])
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    ex.close()
+    cuda_ctx.set_matmul_mode("exact")
+    try:
+        _, fresh = make(cuda_ctx, data[0])
+        want = fresh.train(1, 0.0)
+        fresh.close()
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    assert got == want

@@ -304,6 +304,9 @@ struct Executor {
     scratch_floats = 0;
     setup_done = false;
     stepped = false;
+    // The input buffers are new: every input comes from its host copy again
+    // until upload_input writes it.
+    device_inputs.clear();
   }
 
   Slot* alloc(size_t n) {
