@@ -375,7 +375,10 @@ def roofline(ctx, lib, stream, m, n, k, mode="strict"):
                           "cluster pairs, kind::f16 over packed fp16 halves)",
                 "shape": [m, n, k], "achieved": round(achieved, 1), "peak": round(peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                "tensor_pipe_frac": round(3 * achieved / peak, 4), "traffic": None,
+                "tensor_pipe_frac": round(3 * achieved / peak, 4),
+                # DRAM bytes of one launch of the GEMM kernel (packing kernels apart), from the
+                # ncu capture summarised in profiles/gemm_f16x3_16384x5632x2048.md.
+                "traffic": 582994432 + 338900992 if (m, n, k) == (16384, 5632, 2048) else None,
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                 "ms_per_launch": round(call_ms, 4),
                 "peak_source": f"{src}: bf16_tflops {peaks['bf16_tflops']} (the fp16 tensor rate equals bf16's)",

@@ -207,9 +207,14 @@ def sweep(ctx, lib, stream, a) -> None:
         a.reps, a.warmup)
     flops = 2.0 * m ** 3
     tf = flops / (ms / 1e3) / 1e12
-    lines.append({"op": "matmul_relu", "shape": "x, w [2048, 2048] strict 3xTF32", "ms": round(ms, 4),
-                  "TFLOP/s": round(tf, 1), "peak": peaks["tf32_tflops"], "frac": round(tf / peaks["tf32_tflops"], 4),
-                  "pipe_frac": round(3 * tf / peaks["tf32_tflops"], 4), "peak_source": src})
+    # strict16 issues its three products at the fp16 (= bf16) tensor rate; the others at tf32's.
+    peak = 2.0 * peaks["tf32_tflops"] if a.mode == "strict16" else peaks["tf32_tflops"]
+    mmas = 1 if a.mode == "fast" else 3
+    engine = {"strict": "strict 3xTF32", "strict16": "strict16 (split-fp16, packing included)", "fast": "fast 1xTF32",
+              "exact": "exact (CUDA cores)"}[a.mode]
+    lines.append({"op": "matmul_relu", "shape": f"x, w [2048, 2048] {engine}", "ms": round(ms, 4),
+                  "TFLOP/s": round(tf, 1), "peak": peak, "frac": round(tf / peak, 4),
+                  "pipe_frac": round(mmas * tf / peak, 4), "peak_source": src})
     for buf in (xm, wm, ym):
         buf.free()
     for line in lines:
