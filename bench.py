@@ -17,9 +17,10 @@ rank), weights ~ N(0, 0.02), gains ~ N(1, 0.02), all generated on the host
 from fixed seeds.  One step = forward, squared error against a seeded
 N(0,1) target (`d = out - target; loss = d * d`, summed as the reference
 sums objectives), backward (every parameter and input gradient), gradient
-all-reduce (N > 1) and SGD (lr 1e-6: the loss is a sum over 33.6M
-elements, not a mean).  Every tensor of a step is larger than the 126 MB L2
-(x alone is 134 MB, the attention scores 2.1 GB), so no L2 flush is needed
+all-reduce (N > 1) and SGD (lr 1e-6 / N: the loss is a sum over 33.6M
+elements per GPU, not a mean, and the all-reduce sums the N gradients).
+Every tensor of a step is larger than the 126 MB L2 (x alone is 134 MB,
+the attention scores 2.1 GB), so no L2 flush is needed
 between steps.
 
 `mlp`: two-layer MLP training, x and target [8192, 1024] ~ N(0,1) sharded by
@@ -101,7 +102,11 @@ class Block:
                            n_kv_heads=KV_HEADS, hidden=FFN, lr=self.lr, mse_target=True)
 
     def step_lr(self, world):
-        return self.lr
+        # The all-reduce sums the ranks' gradients of their summed losses, so
+        # the step on the global sum is lr / world: the same parameter
+        # trajectory scale at every N (at lr 1e-6 x 4 ranks the summed
+        # objective diverges within the bench's ~35 steps).
+        return self.lr / world
 
     def units(self, world):
         return self.batch * self.seq  # tokens per rank per step

@@ -139,3 +139,37 @@ def test_strict16_odd_row_pitch(cuda_ctx, ta, tb):
     finally:
         cuda_ctx.set_matmul_mode("strict")
     assert frob(got, oracle_mm(a, b)) < 1e-5
+
+
+def test_strict16_block_step_against_the_oracle(cuda_ctx):
+    """A decoder block whose linear layers the split-fp16 engine covers (512
+    tokens, d 256): forward output, every parameter gradient and one SGD step
+    against the oracle.  The weight gradients' column packings take the
+    column maxima left by the forward packings of the same activations and
+    gradients (no maximum pass of their own)."""
+    from test_gpu_block import frob as bfrob, params_for
+    from tysor_b200.programs import llama_block
+    from tysor_b200.runtime import CudaGraphExecutor
+    cfg = dict(batch=2, seq=256, d_model=256, n_heads=4, n_kv_heads=2, hidden=384, eps=1e-6, lr=1e-4)
+    g = llama_block(**cfg)
+    t = cfg["batch"] * cfg["seq"]
+    shapes = {"x": [t, cfg["d_model"]]}
+    x = np.random.default_rng(2).standard_normal((t, cfg["d_model"])).astype(np.float32)
+    params = params_for(g)
+    oparams = {k: L.Tensor(list(v.shape), v.reshape(-1).copy()) for k, v in params.items()}
+    values, grads, _ = L.train_step_grads(g, shapes, inputs={"x": x}, parameters=oparams)
+    out_id = g.outputs[0]
+    cuda_ctx.set_matmul_mode("strict16")
+    try:
+        ex = CudaGraphExecutor(cuda_ctx, g, shapes, inputs={"x": x}, parameters=params)
+        ex.train(1, 0.0)
+        errs = {"out": bfrob(ex.value(out_id).data, values[out_id][1].data)}
+        for name, gt in grads.items():
+            errs[name] = bfrob(ex.parameter_grad(name), gt.data)
+        ex.close()
+    finally:
+        cuda_ctx.set_matmul_mode("strict")
+    print("\nstrict16 block vs oracle:", {k: f"{v:.1e}" for k, v in errs.items()})
+    assert errs.pop("out") < 1e-5
+    for name, e in errs.items():
+        assert e < 1e-4, name
