@@ -143,10 +143,9 @@ def test_strict16_odd_row_pitch(cuda_ctx, ta, tb):
 
 def test_strict16_block_step_against_the_oracle(cuda_ctx):
     """A decoder block whose linear layers the split-fp16 engine covers (512
-    tokens, d 256): forward output, every parameter gradient and one SGD step
-    against the oracle.  The weight gradients' column packings take the
-    column maxima left by the forward packings of the same activations and
-    gradients (no maximum pass of their own)."""
+    tokens, d 256): forward output and every parameter gradient against the
+    oracle, with both packings of each activation and gradient (row-wise for
+    one GEMM, column-wise for the weight gradient's)."""
     from test_gpu_block import frob as bfrob, params_for
     from tysor_b200.programs import llama_block
     from tysor_b200.runtime import CudaGraphExecutor

@@ -134,14 +134,9 @@ int gemm_effective_mode(int mode, int batch, int64_t M, int64_t N, int64_t K, in
 // 2^e), lo = fp16(x 2^e - hi), factor = 2^-e.  hi + lo hold 22 significant
 // bits of x, as 3xTF32's two parts do.  `k_contiguous`: x stored [R][ld]
 // (K contiguous); else [K][ld] (R contiguous).
-// A K-contiguous packing can also leave the maxima of x's K columns in
-// `colmax_out` (K words; where pack16_rows_can_give_colmax holds and x is
-// 16-byte aligned); an R-contiguous packing of the same x (its transpose's
-// rows) then takes them as `colmax_in` and skips its own maximum pass.
 int64_t gemm_pack16_elems(int64_t rows, int64_t K);
-bool pack16_rows_can_give_colmax(int64_t K, int64_t ld);
 void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, int64_t ld, float* packed,
-                   cudaStream_t st, uint32_t* colmax_out = nullptr, const uint32_t* colmax_in = nullptr);
+                   cudaStream_t st);
 
 // Scratch the strict-mode GEMM needs: one "lo" copy of each operand, laid
 // out like the operand (no a_lo when gemm_converts_a).  With `presplit` set

@@ -286,7 +286,6 @@ struct Executor {
     param_order.clear();
     prep_cache.clear();
     pack_cache.clear();
-    pack_links.clear();
     lazy_lo.clear();
     deferred_matmul.clear();
     folded_scale.clear();
@@ -492,13 +491,6 @@ struct Executor {
   // Split-fp16 packings (kGemmStrict16), keyed by operand, K contiguous or
   // not, rows, K and row pitch.
   std::map<std::tuple<Slot*, bool, int64_t, int64_t, int64_t>, Slot*> pack_cache;
-  // A K-contiguous packing of x (keyed by x, rows, K, pitch) whose column
-  // maxima a later packing of x's transpose takes (`colmax`, set when that
-  // packing is planned, read when the steps run).
-  struct PackLink {
-    Slot* colmax = nullptr;
-  };
-  std::map<std::tuple<Slot*, int64_t, int64_t, int64_t>, std::shared_ptr<PackLink>> pack_links;
   // Low parts that the kernel producing a value can write as it goes (the
   // fused causal softmax, forward and backward), keyed like prep_cache.  The
   // buffer is made, and the producer told to fill it, only when a GEMM's
@@ -597,31 +589,7 @@ struct Executor {
     auto key = std::make_tuple(x, k_contiguous, rows, K, ld);
     if (auto it = pack_cache.find(key); it != pack_cache.end()) return it->second;
     Slot* packed = alloc((size_t)gemm_pack16_elems(rows, K));
-    std::shared_ptr<PackLink> link;
-    if (k_contiguous) {
-      // Arena slots are 256-byte aligned; a view is 16-byte aligned when its
-      // offset is a multiple of 4 elements.
-      const bool aligned = x->base == nullptr || x->offset % 4 == 0;
-      if (aligned && pack16_rows_can_give_colmax(K, ld)) {
-        link = std::make_shared<PackLink>();
-        pack_links[std::make_tuple(x, rows, K, ld)] = link;
-      }
-      out.push_back([=](cudaStream_t st) {
-        launch_pack16(x->p, true, rows, K, ld, packed->p, st,
-                      link && link->colmax ? (uint32_t*)link->colmax->p : nullptr);
-      });
-    } else {
-      // x stored [K][ld], `rows` contiguous: the transpose of a K-contiguous
-      // packing of x with K rows of `rows` columns, if one ran earlier.
-      if (auto it = pack_links.find(std::make_tuple(x, K, rows, ld)); it != pack_links.end()) {
-        link = it->second;
-        if (!link->colmax) link->colmax = alloc((size_t)rows);
-      }
-      out.push_back([=](cudaStream_t st) {
-        launch_pack16(x->p, false, rows, K, ld, packed->p, st, nullptr,
-                      link ? (const uint32_t*)link->colmax->p : nullptr);
-      });
-    }
+    out.push_back([=](cudaStream_t st) { launch_pack16(x->p, k_contiguous, rows, K, ld, packed->p, st); });
     pack_cache[key] = packed;
     return packed;
   }

@@ -1433,65 +1433,6 @@ __global__ void __launch_bounds__(256) pack16_rows_kernel(const float* __restric
   for (int i = 4 * K4 + threadIdx.x; i < K; i += 256) pack16_one(row[i], up, h + i, l + i);
 }
 
-// The same packing, 16 rows per block, which also leaves each column's
-// largest magnitude in colmax[K] (zeroed before; float bits, atomically
-// maxed once per block): the column pass of a later packing of x's
-// transpose (the weight gradient's operand) then reads no extra pass over
-// x.  Needs ld % 4 == 0, K % 4 == 0, K <= 8192 and x 16-byte aligned.
-constexpr int kPackRowsPerBlock = 16;
-__global__ void __launch_bounds__(256) pack16_rows_colmax_kernel(const float* __restrict__ x, int64_t ld, int R, int K,
-                                                                 int Kp, __half* __restrict__ hi,
-                                                                 __half* __restrict__ lo, float* __restrict__ factor,
-                                                                 uint32_t* __restrict__ colmax) {
-  __shared__ float red[8];
-  const int K4 = K >> 2;
-  float4 cm[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) cm[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  const int r0 = blockIdx.x * kPackRowsPerBlock;
-  for (int r = r0; r < R && r < r0 + kPackRowsPerBlock; ++r) {
-    const float4* row = (const float4*)(x + (int64_t)r * ld);
-    float4 v[8];
-    float mx = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int i = threadIdx.x + 256 * j;
-      v[j] = i < K4 ? __ldg(row + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      const float4 a = make_float4(fabsf(v[j].x), fabsf(v[j].y), fabsf(v[j].z), fabsf(v[j].w));
-      mx = fmaxf(mx, fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)));
-      cm[j] = make_float4(fmaxf(cm[j].x, a.x), fmaxf(cm[j].y, a.y), fmaxf(cm[j].z, a.z), fmaxf(cm[j].w, a.w));
-    }
-    mx = block_max256(mx, red);
-    __syncthreads();  // red is reused by the next row
-    const int e = pack16_exponent(mx);
-    const float up = pow2f(e);
-    if (threadIdx.x == 0) factor[r] = pow2f(-e);
-    __half* h = hi + (int64_t)r * Kp;
-    __half* l = lo + (int64_t)r * Kp;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int i = threadIdx.x + 256 * j;
-      if (i >= K4) break;
-      __align__(8) __half hv[4], lv[4];
-      pack16_one(v[j].x, up, &hv[0], &lv[0]);
-      pack16_one(v[j].y, up, &hv[1], &lv[1]);
-      pack16_one(v[j].z, up, &hv[2], &lv[2]);
-      pack16_one(v[j].w, up, &hv[3], &lv[3]);
-      *(uint2*)(h + 4 * i) = *(const uint2*)hv;
-      *(uint2*)(l + 4 * i) = *(const uint2*)lv;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int i = threadIdx.x + 256 * j;
-    if (i >= K4) break;
-    atomicMax(&colmax[4 * i], __float_as_uint(cm[j].x));
-    atomicMax(&colmax[4 * i + 1], __float_as_uint(cm[j].y));
-    atomicMax(&colmax[4 * i + 2], __float_as_uint(cm[j].z));
-    atomicMax(&colmax[4 * i + 3], __float_as_uint(cm[j].w));
-  }
-}
-
 // R-contiguous operand x [K][ld], pass 1: each column's largest magnitude,
 // as float bits (non-negative floats order like their bits), atomically
 // maxed into colmax[R] (zeroed before).  Block: 256 columns (64 threads x
@@ -1992,10 +1933,8 @@ int64_t gemm_pack16_elems(int64_t rows, int64_t K) {
   return rows * kp + 2 * ((rows + 3) & ~(int64_t)3);
 }
 
-bool pack16_rows_can_give_colmax(int64_t K, int64_t ld) { return K % 4 == 0 && ld % 4 == 0 && K <= 8192; }
-
 void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, int64_t ld, float* packed,
-                   cudaStream_t st, uint32_t* colmax_out, const uint32_t* colmax_in) {
+                   cudaStream_t st) {
   if (rows <= 0 || K <= 0) return;
   if (rows > INT32_MAX / 2 || K > INT32_MAX / 2) throw CudaError("pack16: operand too large");
   if ((((uintptr_t)packed) & 15) != 0) throw CudaError("pack16: packed buffer not 16-byte aligned");
@@ -2005,35 +1944,22 @@ void launch_pack16(const float* x, bool k_contiguous, int64_t rows, int64_t K, i
   float* factor = (float*)(lo + rows * kp);
   if (k_contiguous) {
     if (ld < K) throw CudaError("pack16: row pitch below K");
-    if (colmax_out != nullptr) {
-      if (!pack16_rows_can_give_colmax(K, ld) || (((uintptr_t)x) & 15) != 0)
-        throw CudaError("pack16: column maxima need K % 4 == 0, K <= 8192 and 16-byte rows");
-      TYSOR_CUDA(cudaMemsetAsync(colmax_out, 0, sizeof(uint32_t) * (size_t)K, st));
-      pack16_rows_colmax_kernel<<<(unsigned)ceil_div(rows, kPackRowsPerBlock), 256, 0, st>>>(
-          x, ld, (int)rows, (int)K, (int)kp, hi, lo, factor, colmax_out);
-    } else {
-      pack16_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(x, ld, (int)K, (int)kp, hi, lo, factor);
-    }
+    pack16_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(x, ld, (int)K, (int)kp, hi, lo, factor);
     TYSOR_CUDA(cudaGetLastError());
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return;
   }
   if (ld < rows) throw CudaError("pack16: row pitch below the operand's rows");
   if (ceil_div(K, 64) > 65535) throw CudaError("pack16: K too large for the column pass");
-  const uint32_t* colmax = colmax_in;
-  if (colmax == nullptr) {
-    uint32_t* cm = (uint32_t*)(factor + ((rows + 3) & ~(int64_t)3));
-    TYSOR_CUDA(cudaMemsetAsync(cm, 0, sizeof(uint32_t) * (size_t)rows, st));
-    pack16_colmax_kernel<<<dim3((unsigned)ceil_div(rows, 256), (unsigned)ceil_div(K, 64)), 256, 0, st>>>(
-        x, ld, (int)rows, (int)K, cm);
-    TYSOR_CUDA(cudaGetLastError());
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    colmax = cm;
-  }
+  uint32_t* colmax = (uint32_t*)(factor + ((rows + 3) & ~(int64_t)3));
+  TYSOR_CUDA(cudaMemsetAsync(colmax, 0, sizeof(uint32_t) * (size_t)rows, st));
+  pack16_colmax_kernel<<<dim3((unsigned)ceil_div(rows, 256), (unsigned)ceil_div(K, 64)), 256, 0, st>>>(
+      x, ld, (int)rows, (int)K, colmax);
+  TYSOR_CUDA(cudaGetLastError());
   pack16_cols_kernel<<<dim3((unsigned)ceil_div(rows, 64), (unsigned)ceil_div(K, 64)), 256, 0, st>>>(
       x, ld, (int)rows, (int)K, (int)kp, colmax, hi, lo, factor);
   TYSOR_CUDA(cudaGetLastError());
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  g_launches.fetch_add(2, std::memory_order_relaxed);
 }
 
 int gemm_effective_mode(int mode, int batch, int64_t M, int64_t N, int64_t K, int tri, bool smx, int64_t ldc,
