@@ -97,8 +97,11 @@ layer model(x: tensor[float16]): tensor[float16]:
 
 
 @pytest.mark.parametrize("src,msg", [
-    ("layer helper(x: tensor): tensor:\n  return relu(x)\n\n"
-     "layer model(x: tensor): tensor:\n  return helper(x)\n", "not inlined"),
+    ("layer helper(x: tensor): tensor:\n  return helper(x)\n\n"
+     "layer model(x: tensor): tensor:\n  return helper(x)\n", "recursive call"),
+    ("layer model(x: tensor): tensor:\n  return x if x2 else x\n", "must be known while lowering"),
+    ("config a:\n  n : int = 1\nconfig b:\n  n : int = 2\n\n"
+     "layer model(x: tensor): tensor:\n  return scale(x, config.n)\n", "exactly one config block"),
     ("layer model(x: tensor): tensor:\n  return relu(z)\n", "unknown name"),
     ("layer model(x: tensor): tensor:\n  return reshape(x, heads: 4)\n", "keyword"),
     ("layer model(x: tensor): tensor:\n  y = x\n", "no return"),

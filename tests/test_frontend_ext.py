@@ -1,0 +1,231 @@
+"""Front-end extensions for `examples/llama.ty`-style programs
+(tysor_b200/frontend.py): user-layer inlining, `scale(x, d, h)`,
+`config.head_dim`, conditional expressions and optional inputs, tuple
+returns, integer folding of compile-time arithmetic in arguments.
+
+The end-to-end check writes the Llama decoder block with these extensions
+(user layers, a derived head_dim, the three-argument scale, an optional
+target) and runs it through the oracle next to the hand-lowered
+`programs.llama_block`: with parameters drawn in constructor order, the
+output and every gradient are bit-identical (the same operations on the
+same values)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import local as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from tysor_b200.frontend import TysorSyntaxError, lower  # noqa: E402
+from tysor_b200.programs import llama_block, random_parameters  # noqa: E402
+
+
+def structure(g):
+    """Nodes without value names: (kind, op / binop, constant, inputs)."""
+    return [(n.kind, n.binop if n.kind == "binary" else n.op, repr(n.const), list(n.inputs)) for n in g.nodes]
+
+
+def test_inlined_layer_equals_the_written_out_body():
+    inlined = """
+layer Norm(t: tensor, width: int): tensor:
+  n = RMSNorm(width, 0.00001)
+  return n(t)
+
+layer model(x: tensor): tensor:
+  proj = linear(8, 8, false)
+  return x -> Norm(8) -> proj()
+"""
+    flat = """
+layer model(x: tensor): tensor:
+  proj = linear(8, 8, false)
+  n = RMSNorm(8, 0.00001)
+  return proj(n(x))
+"""
+    a, b = lower(inlined), lower(flat)
+    # The stage order puts the projection's constructor first in both.
+    assert structure(a) == structure(b)
+    assert a.outputs == b.outputs
+
+
+def test_each_call_makes_its_own_parameters():
+    src = """
+layer Proj(t: tensor): tensor:
+  p = linear(4, 4, true)
+  return p(t)
+
+layer model(x: tensor): tensor:
+  return x -> Proj() -> relu() -> Proj()
+"""
+    g = lower(src)
+    ctors = [n for n in g.nodes if n.kind == "ctor"]
+    assert [c.op for c in ctors] == ["linear", "linear"]
+    names = set(random_parameters(g, 1))
+    assert len(names) == 4  # two weights, two biases
+
+
+def test_scale_of_a_width_over_heads():
+    src = """
+config c:
+  hidden_dim : int = 2048
+  n_heads    : int = 16
+
+layer model(x: tensor): tensor:
+  return x -> scale(c.hidden_dim, c.n_heads)
+"""
+    g = lower(src)
+    consts = [n.const for n in g.nodes if n.kind == "const"]
+    assert consts == [1.0 / (128.0 ** 0.5)]
+    assert [n.op for n in g.nodes if n.kind in ("primitive", "call")] == ["scale"]
+
+
+def test_config_head_dim_is_derived_unless_declared():
+    base = """
+config llama_config:
+  hidden_dim : int = 512
+  n_heads    : int = 8{extra}
+
+layer model(x: tensor): tensor:
+  return reshape(x, 2, config.head_dim)
+"""
+    g = lower(base.format(extra=""))
+    assert [n.const for n in g.nodes if n.kind == "const"] == [2, 64]
+    g = lower(base.format(extra="\n  head_dim   : int = 32"))
+    assert [n.const for n in g.nodes if n.kind == "const"] == [2, 32]
+    with pytest.raises(TysorSyntaxError, match="not a multiple"):
+        lower(base.replace("n_heads    : int = 8", "n_heads    : int = 7").format(extra=""))
+
+
+def test_conditionals_optional_inputs_and_tuple_returns():
+    src = """
+config c:
+  use_relu : bool = true
+  depth    : int = 3
+
+layer model(x: tensor, target=None): (tensor, tensor):
+  y = relu(x) if c.use_relu else x
+  z = scale(y, 2.0) if c.depth > 2 else y
+  loss = z - target if target else None
+  return z, loss
+"""
+    full = lower(src)
+    assert [v.name for v in full.values if v.is_parameter] == ["x", "target"]
+    assert len(full.outputs) == 2
+    assert [n.op for n in full.nodes if n.kind in ("primitive", "call")] == ["relu", "scale"]
+    bare = lower(src, inputs=["x"])
+    assert [v.name for v in bare.values if v.is_parameter] == ["x"]
+    assert len(bare.outputs) == 1 and not any(n.kind == "binary" for n in bare.nodes)
+
+
+def test_integer_arithmetic_in_arguments_folds():
+    src = """
+config c:
+  n_heads    : int = 16
+  n_kv_heads : int = 4
+
+layer model(x: tensor): tensor:
+  return repeat_kv(x, c.n_heads / c.n_kv_heads)
+"""
+    g = lower(src)
+    assert [n.const for n in g.nodes if n.kind == "const"] == [4]
+    assert not any(n.kind == "binary" for n in g.nodes)
+
+
+LLAMA_STYLE = """
+config llama_config:
+  batch        : int   = 2
+  seq          : int   = 64
+  hidden_dim   : int   = 256
+  n_heads      : int   = 4
+  n_kv_heads   : int   = 2
+  intermediate : int   = 384
+  rope_theta   : float = 10000.0
+  eps          : float = 0.000001
+
+layer Heads(t: tensor, nh: int): tensor:
+  return t -> reshape(llama_config.batch, llama_config.seq, nh, config.head_dim) -> transpose(1, 2)
+
+layer DecoderBlock(x: tensor): tensor:
+  attn_norm = RMSNorm(llama_config.hidden_dim, llama_config.eps)
+  q_proj    = linear(llama_config.hidden_dim, llama_config.hidden_dim, false)
+  k_proj    = linear(llama_config.hidden_dim, llama_config.n_kv_heads * config.head_dim, false)
+  v_proj    = linear(llama_config.hidden_dim, llama_config.n_kv_heads * config.head_dim, false)
+  o_proj    = linear(llama_config.hidden_dim, llama_config.hidden_dim, false)
+  ffn_norm  = RMSNorm(llama_config.hidden_dim, llama_config.eps)
+  gate_proj = linear(llama_config.hidden_dim, llama_config.intermediate, false)
+  up_proj   = linear(llama_config.hidden_dim, llama_config.intermediate, false)
+  down_proj = linear(llama_config.intermediate, llama_config.hidden_dim, false)
+  act       = SiLU()
+  softmax   = Softmax()
+
+  hn = attn_norm(x)
+  q = hn -> q_proj() -> Heads(llama_config.n_heads) -> rope(config.head_dim, llama_config.rope_theta)
+  k = hn -> k_proj() -> Heads(llama_config.n_kv_heads) -> rope(config.head_dim, llama_config.rope_theta)
+  v = hn -> v_proj() -> Heads(llama_config.n_kv_heads)
+  k = k -> repeat_kv(llama_config.n_heads / llama_config.n_kv_heads)
+  v = v -> repeat_kv(llama_config.n_heads / llama_config.n_kv_heads)
+
+  scores = matmul(q, transpose(k, 2, 3)) -> scale(llama_config.hidden_dim, llama_config.n_heads)
+  probs = scores -> causal_mask() -> softmax()
+  ctx = matmul(probs, v) -> transpose(1, 2) -> reshape(llama_config.batch * llama_config.seq, llama_config.hidden_dim)
+  h = x + (ctx -> o_proj())
+
+  hn2 = ffn_norm(h)
+  ff = (hn2 -> gate_proj() -> act()) * (hn2 -> up_proj())
+  return h + (ff -> down_proj())
+
+layer model(x: tensor, target=None): tensor:
+  out = DecoderBlock(x)
+  d = out - target if target else out
+  loss = d * d if target else out
+  return loss
+
+train model:
+  optimizer = "sgd"
+  lr = 0.0001
+  iteration = 1
+  objective = loss
+"""
+
+CFG = dict(batch=2, seq=64, d_model=256, n_heads=4, n_kv_heads=2, hidden=384, eps=1e-6, lr=1e-4)
+
+
+def by_ctor_order(g, params):
+    """Parameter arrays in constructor order (names carry graph ids)."""
+    order = []
+    for n in g.nodes:
+        if n.kind == "ctor":
+            order += sorted(k for k in params if k.split("_")[1] == str(n.output))
+    return [params[k] for k in order], order
+
+
+@pytest.mark.parametrize("with_target", [True, False])
+def test_llama_style_program_matches_the_hand_lowered_block(with_target):
+    t = CFG["batch"] * CFG["seq"]
+    g = lower(LLAMA_STYLE, inputs=["x", "target"] if with_target else ["x"])
+    want = llama_block(**CFG, mse_target=with_target)
+    shapes = {"x": [t, CFG["d_model"]]}
+    rng = np.random.default_rng(3)
+    ins = {"x": rng.standard_normal(t * CFG["d_model"]).astype(np.float32)}
+    if with_target:
+        shapes["target"] = [t, CFG["d_model"]]
+        ins["target"] = rng.standard_normal(t * CFG["d_model"]).astype(np.float32)
+    pg, pw = random_parameters(g, 9), random_parameters(want, 9)
+    arrays_g, names_g = by_ctor_order(g, pg)
+    arrays_w, names_w = by_ctor_order(want, pw)
+    assert [a.shape for a in arrays_g] == [a.shape for a in arrays_w]
+
+    def run(graph, params):
+        ps = {k: L.Tensor(list(v.shape), v.reshape(-1).copy()) for k, v in params.items()}
+        values, grads, _ = L.train_step_grads(graph, shapes, inputs=ins, parameters=ps)
+        return values[graph.objective_id()][1].data, grads
+
+    out_g, grads_g = run(g, pg)
+    out_w, grads_w = run(want, pw)
+    np.testing.assert_array_equal(out_g, out_w)
+    for ng, nw in zip(names_g, names_w):
+        np.testing.assert_array_equal(grads_g[ng].data, grads_w[nw].data, err_msg=nw)

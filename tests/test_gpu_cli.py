@@ -100,3 +100,20 @@ def test_train_prints_the_loss_of_every_step(tmp_path):
     got = np.array([float(v) for _, v, _ in steps])
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6)
     assert got[-1] < got[0]
+
+
+def test_llama_style_program_trains_on_the_device(tmp_path):
+    """The Llama decoder block written with user layers, a derived head_dim,
+    the three-argument scale and an optional target (the front end's
+    extensions), trained through the CLI; the optional target is an input
+    only when it gets a --shape."""
+    from test_frontend_ext import LLAMA_STYLE
+    shapes = {"x": [128, 256], "target": [128, 256]}
+    text = cli(tmp_path, LLAMA_STYLE, "--train", "--shape", "x=128x256", "--shape", "target=128x256")
+    steps = re.findall(r"step=(\d+) loss=([-0-9.e+]+) params=(\d+)", text)
+    want, params = L.train(lower(LLAMA_STYLE, inputs=list(shapes)), shapes)
+    assert len(steps) == 1 and int(steps[0][2]) == len(params) == 9
+    np.testing.assert_allclose(float(steps[0][1]), want[0], rtol=1e-4)
+    text = cli(tmp_path, LLAMA_STYLE, "--run", "--shape", "x=128x256")
+    [(_, shape, _, _)] = tensors(text)
+    assert shape == [128, 256]

@@ -84,7 +84,9 @@ def main(argv: Optional[List[str]] = None) -> int:
         print(f"error: could not read {opts['input']}: {e}", file=sys.stderr)
         return 1
     try:
-        graph = lower(src, opts["entry"])
+        # An entry parameter declared `name=None` is an input only when it is
+        # given a --shape.
+        graph = lower(src, opts["entry"], inputs=list(opts["shapes"]))
     except TysorSyntaxError as e:
         print(str(e), file=sys.stderr)
         return 1

@@ -26,9 +26,30 @@ library function (`rms_norm`, `cross_entropy`, `reshape`, `repeat_kv`,
 LibraryCall, of a local variable an Apply.  A pipeline `a -> f(x) -> g()`
 is the nested call `g()(f(x)(a))` for constructor stages (the constructor
 is created, then its input lowered, then applied) and `f(a, x)` for
-function stages.  Calls of user-defined layers are not inlined: the
-reference lowers them to LibraryCall nodes its executors reject, and so
-does this backend's executor.
+function stages.
+
+Extensions for `examples/llama.ty`-style programs (the reference lowers
+none of them to something its executors run: frontend_ir.rs:708-727 makes
+a user layer's call a LibraryCall, ir/builder.rs:174 has no conditional,
+semantic_analyzer.rs:427-442 knows only declared config fields):
+  * user-layer inlining -- a call `F(args)` or stage `x -> F(args)` of a
+    user `layer` / `fn` lowers F's body in place, its parameters bound to
+    the piped input and the arguments (graph values, or compile-time values
+    for literal and config arguments) or to their literal defaults; each
+    call makes its own constructors (parameters); recursion is an error;
+  * `scale(x, d, h)` -- x times 1 / sqrt(d / h) (attention's 1/sqrt(head
+    dim) for width d over h heads; d and h known while lowering); the
+    two-argument `scale(x, c)` is the reference's primitive;
+  * `config.field` -- a field of the program's only config block, and a
+    derived `head_dim` = hidden_dim / n_heads where a config declares those
+    two and not head_dim;
+  * `a if test else b` -- decided while lowering: a literal, config field or
+    comparison of those, or the name of an input (true when the caller
+    supplies it; an entry parameter `p=None` the caller does not supply has
+    no value); `None` leaves a name without value, and `return a, b` drops a
+    None entry;
+  * integer arithmetic on compile-time integers in call arguments folds to
+    an integer (sizes, counts).
 """
 from __future__ import annotations
 
@@ -144,10 +165,34 @@ class Pipe:
 
 
 @dataclass
+class Compare:
+    op: str
+    lhs: Any
+    rhs: Any
+
+
+@dataclass
+class Cond:
+    then: Any
+    test: Any
+    other: Any
+    line: int = 0
+
+
+@dataclass
+class TupleExpr:
+    items: List[Any]
+
+
+NO_DEFAULT = object()
+
+
+@dataclass
 class Param:
     name: str
     type_name: str = ""   # tensor / int / float / bool / "" (unannotated)
     dtype: str = ""       # tensor[dtype]
+    default: Any = NO_DEFAULT  # the expression after `=`
 
 
 @dataclass
@@ -243,9 +288,10 @@ class _Parser:
             tname, dtype = "", ""
             if self.accept("op", ":"):
                 tname, dtype = self.type_ref()
+            default = NO_DEFAULT
             if self.accept("op", "="):
-                self.expr()
-            params.append(Param(pname, tname, dtype))
+                default = self.expr()
+            params.append(Param(pname, tname, dtype, default))
             self.accept("op", ",")
         if self.accept("op", ":"):
             if not (self.peek().kind == "nl"):
@@ -260,7 +306,13 @@ class _Parser:
             tok = self.peek()
             if tok.kind == "name" and tok.text == "return":
                 self.next()
-                body.append(("return", None, self.expr(), tok.line))
+                value = self.expr()
+                if self.peek().kind == "op" and self.peek().text == ",":
+                    items = [value]
+                    while self.accept("op", ","):
+                        items.append(self.expr())
+                    value = TupleExpr(items)
+                body.append(("return", None, value, tok.line))
             elif tok.kind == "name" and self.peek(1).kind == "op" and self.peek(1).text == "=":
                 self.next()
                 self.next()
@@ -305,8 +357,18 @@ class _Parser:
             self.expect("nl")
         return name, fields
 
-    # expressions: pipeline < additive < multiplicative < unary < call < atom
+    # expressions: conditional < pipeline < additive < multiplicative < unary < call < atom
     def expr(self) -> Any:
+        line = self.peek().line
+        node = self.pipeline()
+        if self.peek().kind == "name" and self.peek().text == "if":
+            self.next()
+            test = self.comparison()
+            self.expect("name", "else")
+            return Cond(node, test, self.expr(), line)
+        return node
+
+    def pipeline(self) -> Any:
         src = self.additive()
         stages = []
         while self.accept("op", "->"):
@@ -315,6 +377,13 @@ class _Parser:
                 raise TysorSyntaxError(f"line {self.peek().line}: a pipeline stage must be a call")
             stages.append(stage)
         return Pipe(src, stages) if stages else src
+
+    def comparison(self) -> Any:
+        node = self.additive()
+        if self.peek().kind == "op" and self.peek().text in ("==", "!=", "<", ">", "<=", ">="):
+            op = self.next().text
+            node = Compare(op, node, self.additive())
+        return node
 
     def additive(self) -> Any:
         node = self.multiplicative()
@@ -385,37 +454,119 @@ def parse(src: str) -> Module:
 
 # ---- lowering ------------------------------------------------------------------
 
+@dataclass
+class Const:
+    """A compile-time value bound to a name (a literal or config argument of
+    an inlined layer, or a parameter's literal default)."""
+    value: Any
+
+
+_ABSENT = object()  # a name bound to `None`: no graph value
+
+
 class _Lowerer:
-    def __init__(self, mod: Module, fn: Function):
+    def __init__(self, mod: Module, fn: Function, provided: Optional[set] = None):
         self.mod = mod
         self.fn = fn
         self.b = GraphBuilder(fn.name)
-        self.env: Dict[str, Ref] = {}
+        self.env: Dict[str, Any] = {}
+        self.provided = provided
+        self.stack: List[str] = [fn.name]  # functions being lowered (inlining)
+        self.prefix = ""                   # named-value prefix of the inlined body
+        self.inlined = 0
+
+    # -- compile-time values ----------------------------------------------------
+    def config_field(self, node: Attr) -> Any:
+        if node.base == "config":
+            if len(self.mod.configs) != 1:
+                raise TysorSyntaxError(f"line {node.line}: `config.{node.attr}` needs exactly one config block "
+                                       f"({len(self.mod.configs)} declared)")
+            cfg = next(iter(self.mod.configs.values()))
+        else:
+            cfg = self.mod.configs[node.base]
+        if node.attr in cfg:
+            return cfg[node.attr]
+        if node.attr == "head_dim" and "hidden_dim" in cfg and "n_heads" in cfg:
+            d, h = cfg["hidden_dim"], cfg["n_heads"]
+            if not (isinstance(d, int) and isinstance(h, int) and h > 0 and d % h == 0):
+                raise TysorSyntaxError(f"line {node.line}: head_dim: hidden_dim {d} is not a multiple of n_heads {h}")
+            return d // h
+        raise TysorSyntaxError(f"line {node.line}: unknown config field {node.base}.{node.attr}")
+
+    def const_value(self, node: Any) -> Tuple[bool, Any]:
+        """(True, value) when `node` is known while lowering: a literal, a
+        config field, a name bound to one, or +, -, *, / and comparisons of
+        those (Python arithmetic on the values)."""
+        if isinstance(node, Lit):
+            return True, node.value
+        if isinstance(node, Attr) and (node.base in self.mod.configs or node.base == "config"):
+            return True, self.config_field(node)
+        if isinstance(node, Name) and isinstance(self.env.get(node.id), Const):
+            return True, self.env[node.id].value
+        if isinstance(node, (BinOp, Compare)):
+            ok1, l = self.const_value(node.lhs)
+            ok2, r = self.const_value(node.rhs)
+            if not (ok1 and ok2) or isinstance(l, str) or isinstance(r, str) or l is None or r is None:
+                return False, None
+            ops = {"+": lambda: l + r, "-": lambda: l - r, "*": lambda: l * r, "/": lambda: l / r,
+                   "==": lambda: l == r, "!=": lambda: l != r, "<": lambda: l < r, ">": lambda: l > r,
+                   "<=": lambda: l <= r, ">=": lambda: l >= r}
+            return True, ops[node.op]()
+        return False, None
 
     def literal(self, node: Any) -> Any:
-        """The Python value of a literal or config field, else None."""
-        if isinstance(node, Lit):
-            return node.value
-        if isinstance(node, Attr) and node.base in self.mod.configs:
-            cfg = self.mod.configs[node.base]
-            if node.attr not in cfg:
-                raise TysorSyntaxError(f"line {node.line}: unknown config field {node.base}.{node.attr}")
-            return cfg[node.attr]
+        """The Python value of a literal, a config field or a name bound to a
+        compile-time value, else None."""
+        if isinstance(node, (Lit, Attr)) or (isinstance(node, Name) and isinstance(self.env.get(node.id), Const)):
+            ok, v = self.const_value(node)
+            return v if ok else None
         return None
 
+    def test(self, node: Any, line: int) -> bool:
+        """The condition of `a if test else b`, decided while lowering: a
+        compile-time value, or the name of a graph input (true when the
+        caller supplies it)."""
+        if isinstance(node, Name) and node.id in self.env and not isinstance(self.env[node.id], Const):
+            return self.env[node.id] is not _ABSENT
+        ok, v = self.const_value(node)
+        if not ok:
+            raise TysorSyntaxError(f"line {line}: the condition of `if ... else` must be known while lowering "
+                                   "(a literal, a config field, a comparison of those, or an input's name)")
+        return bool(v)
+
+    # -- graph values -----------------------------------------------------------
     def arg(self, node: Any) -> Union[Ref, int, float, bool]:
         """A call argument: literals stay Python values (the builder makes
-        their Constant nodes where the call is lowered)."""
+        their Constant nodes where the call is lowered).  Integer arithmetic
+        on compile-time integers (`n_kv_heads * config.head_dim`, `n_heads /
+        n_kv_heads` when it divides) folds to an integer argument, as sizes
+        and counts need; the reference lowers it to a scalar Binary node,
+        whose Float its constructors reject."""
         v = self.literal(node)
         if v is not None and not isinstance(v, str):
             return v
+        if isinstance(node, BinOp):
+            ok, v = self.const_value(node)
+            ints = ok and all(isinstance(x, int) and not isinstance(x, bool)
+                              for x in (self.const_value(node.lhs)[1], self.const_value(node.rhs)[1]))
+            if ints and (node.op != "/" or float(v).is_integer()):
+                return int(v)
         return self.value(node)
 
-    def value(self, node: Any) -> Ref:
+    def value(self, node: Any) -> Any:
+        if isinstance(node, Cond):
+            return self.value(node.then if self.test(node.test, node.line) else node.other)
         if isinstance(node, Name):
             if node.id not in self.env:
                 raise TysorSyntaxError(f"line {node.line}: unknown name {node.id!r}")
-            return self.env[node.id]
+            v = self.env[node.id]
+            if v is _ABSENT:
+                raise TysorSyntaxError(f"line {node.line}: {node.id!r} is None here")
+            if isinstance(v, Const):
+                return self.b.const(v.value)
+            return v
+        if isinstance(node, Lit) and node.value is None:
+            return _ABSENT
         v = self.literal(node)
         if v is not None:
             if isinstance(v, str):
@@ -445,7 +596,7 @@ class _Lowerer:
             src, inner = piped
             return self.pipe(src, inner)
 
-        if f in self.env:
+        if f in self.env and not isinstance(self.env[f], Const):
             # calling a constructed layer: Apply(callee, input)
             if piped is not None:
                 if node.args:
@@ -459,28 +610,100 @@ class _Lowerer:
             if piped is not None:
                 return self.b.apply(ctor, piped_input())
             return ctor
+        if f == "scale" and len(node.args) + (piped is not None) == 3:
+            # scale(x, d, h): x * 1 / sqrt(d / h), attention's 1 / sqrt(head_dim)
+            # for a width d split over h heads (d and h known while lowering).
+            x = piped_input() if piped is not None else self.value(node.args[0])
+            dims = node.args[-2:]
+            vals = [self.const_value(d) for d in dims]
+            if not all(ok and isinstance(v, (int, float)) and not isinstance(v, bool) for ok, v in vals):
+                raise TysorSyntaxError(f"line {node.line}: scale(x, d, h) needs d and h known while lowering")
+            d, h = float(vals[0][1]), float(vals[1][1])
+            if d <= 0 or h <= 0:
+                raise TysorSyntaxError(f"line {node.line}: scale(x, d, h) needs d > 0 and h > 0")
+            return self.b.call("scale", x, 1.0 / ((d / h) ** 0.5))
         if f in PRIMITIVE_OPS or f in LIBRARY_CALLS or f == "tied_logits":
             args = ([piped_input()] if piped is not None else []) + [self.arg(a) for a in node.args]
             return self.b.call(f, *args)
         if f in self.mod.functions:
-            raise TysorSyntaxError(f"line {node.line}: calls of user-defined layers ({f}) are not inlined; "
-                                   "the executor runs only library operations")
+            return self.inline(self.mod.functions[f], node, piped_input() if piped is not None else None)
         raise TysorSyntaxError(f"line {node.line}: unknown function {f!r}")
+
+    def inline(self, fn: Function, node: Call, piped: Optional[Ref]) -> Ref:
+        """A call of a user-defined layer or fn, lowered in place: its
+        parameters are bound in order to the piped input (if any) and the
+        call's arguments -- graph values, or compile-time values for literal
+        and config arguments -- or to their literal defaults; its body's
+        constructors make new parameters at every call; its named values are
+        prefixed `Name.k.` (k counts inlined calls); its return is the call's
+        value."""
+        if fn.name in self.stack:
+            raise TysorSyntaxError(f"line {node.line}: recursive call of {fn.name!r}")
+        actual: List[Any] = ([piped] if piped is not None else [])
+        for a in node.args:
+            ok, v = self.const_value(a)
+            actual.append(Const(v) if ok and not isinstance(v, str) else self.value(a))
+        if len(actual) > len(fn.params):
+            raise TysorSyntaxError(f"line {node.line}: {fn.name} takes {len(fn.params)} arguments, "
+                                   f"{len(actual)} given")
+        local: Dict[str, Any] = {}
+        for i, p in enumerate(fn.params):
+            if i < len(actual):
+                local[p.name] = actual[i]
+            elif p.default is not NO_DEFAULT:
+                ok, v = self.const_value(p.default)
+                if not ok:
+                    raise TysorSyntaxError(f"{fn.name}: the default of {p.name} must be a literal")
+                local[p.name] = _ABSENT if v is None else Const(v)
+            else:
+                raise TysorSyntaxError(f"line {node.line}: {fn.name}: missing argument {p.name!r}")
+        saved = (self.env, self.prefix)
+        self.env = local
+        self.prefix = f"{saved[1]}{fn.name}.{self.inlined}."
+        self.inlined += 1
+        self.stack.append(fn.name)
+        try:
+            result = self.body(fn)
+        finally:
+            self.stack.pop()
+            self.env, self.prefix = saved
+        if result is None or isinstance(result, list):
+            raise TysorSyntaxError(f"line {node.line}: {fn.name} must return one value to be called")
+        return result
+
+    def body(self, fn: Function) -> Any:
+        """Lowers fn's statements into the graph; returns its return value
+        (a list for a tuple return; None without a return)."""
+        for kind, name, expr, line in fn.body:
+            if kind == "assign":
+                v = self.value(expr)
+                self.env[name] = v if v is _ABSENT else self.b.let(self.prefix + name, v)
+            else:
+                if isinstance(expr, TupleExpr):
+                    # a name without value (None) is dropped from the outputs
+                    return [_ABSENT if isinstance(e, Name) and self.env.get(e.id) is _ABSENT else self.value(e)
+                            for e in expr.items]
+                v = self.value(expr)
+                if v is _ABSENT:
+                    raise TysorSyntaxError(f"line {line}: {fn.name} returns None")
+                return v
+        return None
 
     def lower(self, train: Optional[TrainRun]) -> Graph:
         for p in self.fn.params:
             if p.type_name not in ("", "tensor"):
                 raise TysorSyntaxError(f"parameter {p.name}: only tensor parameters are supported")
-            self.env[p.name] = self.b.param(p.name, p.dtype)
-        returned = False
-        for kind, name, expr, line in self.fn.body:
-            if kind == "assign":
-                self.env[name] = self.b.let(name, self.value(expr))
+            supplied = self.provided is None or p.name in self.provided
+            if not supplied and p.default is not NO_DEFAULT and isinstance(p.default, Lit) and p.default.value is None:
+                self.env[p.name] = _ABSENT  # an optional input the caller did not supply
             else:
-                self.b.ret(self.value(expr))
-                returned = True
-        if not returned:
+                self.env[p.name] = self.b.param(p.name, p.dtype)
+        result = self.body(self.fn)
+        if result is None:
             raise TysorSyntaxError(f"{self.fn.name}: no return")
+        for r in (result if isinstance(result, list) else [result]):
+            if r is not _ABSENT:
+                self.b.ret(r)
         if train is not None:
             s = train.settings
             obj = s.get("objective")
@@ -492,11 +715,15 @@ class _Lowerer:
         return self.b.build()
 
 
-def lower(src: str, entry: str = "model") -> Graph:
+def lower(src: str, entry: str = "model", inputs: Optional[List[str]] = None) -> Graph:
     """The lowered graph of function `entry` of a `.ty` program, with the
     program's `train entry:` settings (objective, lr, iterations, optimizer)
-    when it has them."""
+    when it has them.  `inputs`: the graph inputs the caller supplies (the
+    CLI's `--shape` names); an entry parameter whose default is `None` and
+    that is not among them has no graph value (`x if targets else y` then
+    takes y).  None: every parameter is an input."""
     mod = parse(src)
     if entry not in mod.functions:
         raise TysorSyntaxError(f"Entry function '{entry}' not found in lowered module")
-    return _Lowerer(mod, mod.functions[entry]).lower(mod.trains.get(entry))
+    provided = None if inputs is None else set(inputs)
+    return _Lowerer(mod, mod.functions[entry], provided).lower(mod.trains.get(entry))
