@@ -257,6 +257,27 @@ def test_cross_entropy_sweep(dev, rows, width):
     close(G.read(), L.cross_entropy_backward(lt, T(target.shape, target)).data)
 
 
+@pytest.mark.parametrize("rows,width", [(33, 4096), (3, 40000)])
+def test_cross_entropy_backward_accumulates(dev, rows, width):
+    """The backward kernels add into an existing gradient when asked
+    (labels and dense targets, a power-of-two and a wide row)."""
+    rng = np.random.default_rng(rows + width)
+    logits = (2.0 * rng.standard_normal((rows, width))).astype(np.float32)
+    labels = rng.integers(0, width, rows).astype(np.float32)
+    target = np.abs(rng.standard_normal((rows, width))).astype(np.float32)
+    old = rng.standard_normal((rows, width)).astype(np.float32)
+    lt = T(logits.shape, logits)
+    LG, LB, TG = dev.buf(logits), dev.buf(labels), dev.buf(target)
+    G = dev.buf(old)
+    dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy_labels_backward(dev.h, LG.handle, LB.handle, G.handle, rows,
+                                                                     width, True))
+    close(G.read(), old.reshape(-1) + L.cross_entropy_backward(lt, T([rows], labels)).data)
+    G = dev.buf(old)
+    dev.ok(dev.lib.tysor_cuda_dispatch_cross_entropy_backward(dev.h, LG.handle, TG.handle, G.handle, rows, width,
+                                                              True))
+    close(G.read(), old.reshape(-1) + L.cross_entropy_backward(lt, T(target.shape, target)).data)
+
+
 def test_pipeline_wait_gives_up_and_reports(dev):
     """The tensor-core pipelines' mbarrier wait is bounded: a wait on a
     barrier that nothing arrives at gives up after its cycle limit and

@@ -866,32 +866,9 @@ __device__ __forceinline__ void ms_add4(float& m, float& s, float4 v) {
   s += expf(v.w - m);
 }
 
-// `red` holds >= 66 floats.  Every thread gets (m, d).
-__device__ void row_stats(const float* __restrict__ xr, int width, bool vec, float* red, float* m_out,
-                          float* d_out) {
-  float m = -INFINITY, s = 0.0f;
-  if (vec) {
-    const float4* x4 = (const float4*)xr;
-    const int n4 = width >> 2;
-    int j = threadIdx.x;
-    for (; j + (kCeUnroll - 1) * (int)blockDim.x < n4; j += kCeUnroll * blockDim.x) {
-      float4 v[kCeUnroll];
-#pragma unroll
-      for (int u = 0; u < kCeUnroll; ++u) v[u] = x4[j + u * blockDim.x];
-#pragma unroll
-      for (int u = 0; u < kCeUnroll; ++u) ms_add4(m, s, v[u]);
-    }
-    for (; j < n4; j += blockDim.x) ms_add4(m, s, x4[j]);
-  } else {
-    for (int j = threadIdx.x; j < width; j += blockDim.x) {
-      const float v = xr[j];
-      if (v > m) {
-        s = s * expf(m - v);
-        m = v;
-      }
-      s += expf(v - m);
-    }
-  }
+// The block's (max, sum of exp(x - max)) from each thread's pair; every
+// thread gets (m, max(d, f32::EPSILON)).  `red` holds >= 66 floats.
+__device__ void block_ms(float m, float s, float* red, float* m_out, float* d_out) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -922,6 +899,35 @@ __device__ void row_stats(const float* __restrict__ xr, int width, bool vec, flo
   __syncthreads();
   *m_out = red[64];
   *d_out = fmaxf(red[65], 1.1920928955078125e-7f);  // max(sum, f32::EPSILON)
+}
+
+// `red` holds >= 66 floats.  Every thread gets (m, d).
+__device__ void row_stats(const float* __restrict__ xr, int width, bool vec, float* red, float* m_out,
+                          float* d_out) {
+  float m = -INFINITY, s = 0.0f;
+  if (vec) {
+    const float4* x4 = (const float4*)xr;
+    const int n4 = width >> 2;
+    int j = threadIdx.x;
+    for (; j + (kCeUnroll - 1) * (int)blockDim.x < n4; j += kCeUnroll * blockDim.x) {
+      float4 v[kCeUnroll];
+#pragma unroll
+      for (int u = 0; u < kCeUnroll; ++u) v[u] = x4[j + u * blockDim.x];
+#pragma unroll
+      for (int u = 0; u < kCeUnroll; ++u) ms_add4(m, s, v[u]);
+    }
+    for (; j < n4; j += blockDim.x) ms_add4(m, s, x4[j]);
+  } else {
+    for (int j = threadIdx.x; j < width; j += blockDim.x) {
+      const float v = xr[j];
+      if (v > m) {
+        s = s * expf(m - v);
+        m = v;
+      }
+      s += expf(v - m);
+    }
+  }
+  block_ms(m, s, red, m_out, d_out);
 }
 
 // loss[r] = -sum_j t_j * ln(max(p_j, 1e-6)), p = softmax(x_r)  (layers.rs:301-324)
