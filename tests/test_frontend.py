@@ -100,6 +100,8 @@ layer model(x: tensor[float16]): tensor[float16]:
     ("layer helper(x: tensor): tensor:\n  return helper(x)\n\n"
      "layer model(x: tensor): tensor:\n  return helper(x)\n", "recursive call"),
     ("layer model(x: tensor): tensor:\n  return x if x2 else x\n", "must be known while lowering"),
+    ("layer model(x: tensor): tensor:\n  y = None\n  return x + y\n", "'y' is None here"),
+    ("layer model(x: tensor): tensor:\n  return x + None\n", "None is not a graph value"),
     ("config a:\n  n : int = 1\nconfig b:\n  n : int = 2\n\n"
      "layer model(x: tensor): tensor:\n  return scale(x, config.n)\n", "exactly one config block"),
     ("layer model(x: tensor): tensor:\n  return relu(z)\n", "unknown name"),

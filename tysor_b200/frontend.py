@@ -553,7 +553,20 @@ class _Lowerer:
                 return int(v)
         return self.value(node)
 
+    def value_or_absent(self, node: Any) -> Any:
+        """The value of the right side of an assignment or of a returned
+        expression, which may be None (`_ABSENT`): a `None` literal, a name
+        bound to None, or a conditional choosing either."""
+        if isinstance(node, Cond):
+            return self.value_or_absent(node.then if self.test(node.test, node.line) else node.other)
+        if isinstance(node, Lit) and node.value is None:
+            return _ABSENT
+        if isinstance(node, Name) and self.env.get(node.id, None) is _ABSENT:
+            return _ABSENT
+        return self.value(node)
+
     def value(self, node: Any) -> Any:
+        """A graph value (never None)."""
         if isinstance(node, Cond):
             return self.value(node.then if self.test(node.test, node.line) else node.other)
         if isinstance(node, Name):
@@ -566,7 +579,7 @@ class _Lowerer:
                 return self.b.const(v.value)
             return v
         if isinstance(node, Lit) and node.value is None:
-            return _ABSENT
+            raise TysorSyntaxError("None is not a graph value here")
         v = self.literal(node)
         if v is not None:
             if isinstance(v, str):
@@ -676,14 +689,13 @@ class _Lowerer:
         (a list for a tuple return; None without a return)."""
         for kind, name, expr, line in fn.body:
             if kind == "assign":
-                v = self.value(expr)
+                v = self.value_or_absent(expr)
                 self.env[name] = v if v is _ABSENT else self.b.let(self.prefix + name, v)
             else:
                 if isinstance(expr, TupleExpr):
-                    # a name without value (None) is dropped from the outputs
-                    return [_ABSENT if isinstance(e, Name) and self.env.get(e.id) is _ABSENT else self.value(e)
-                            for e in expr.items]
-                v = self.value(expr)
+                    # an entry without value (None) is dropped from the outputs
+                    return [self.value_or_absent(e) for e in expr.items]
+                v = self.value_or_absent(expr)
                 if v is _ABSENT:
                     raise TysorSyntaxError(f"line {line}: {fn.name} returns None")
                 return v
