@@ -171,6 +171,20 @@ def test_transpose_bit_exact(dev):
     np.testing.assert_array_equal(O.read(), L.transpose(T(shape, x), 2, 3).data)
 
 
+@pytest.mark.parametrize("shape,a,b", [((2, 3, 5, 4, 64), 1, 2), ((2, 3, 5, 4, 64), 1, 3), ((2, 3, 5, 4, 64), 0, 3),
+                                       ((8, 16, 64, 128), 1, 2), ((3, 7, 9, 40), 0, 2)])
+def test_transpose_of_whole_runs_bit_exact(dev, shape, a, b):
+    """Swaps whose trailing axes form runs of >= 32 elements move the runs
+    whole (one warp per run); every element still lands where the oracle
+    puts it."""
+    x = rnd(shape, 18)
+    X, O = dev.buf(x), dev.zeros(x.size)
+    dims = (ctypes.c_int64 * len(shape))(*shape)
+    dev.ok(dev.lib.tysor_cuda_dispatch_transpose(dev.h, X.handle, O.handle, dims, len(shape), a, b))
+    np.testing.assert_array_equal(O.read(), L.transpose(T(shape, x), a, b).data)
+    np.testing.assert_array_equal(O.read().reshape(np.swapaxes(x, a, b).shape), np.swapaxes(x, a, b))
+
+
 def test_bias_grad_and_reduce_sum(dev):
     g = rnd((3001, 77), 15)
     Gb, DB, S = dev.buf(g), dev.zeros(77), dev.zeros(1)

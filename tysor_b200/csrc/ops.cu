@@ -1412,6 +1412,37 @@ __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict_
   }
 }
 
+// The same axis swap when the axes after the later swapped one hold a run
+// of T4 float4 (16-byte aligned): x is [P][A][Mid][B][run], out is
+// [P][B][Mid][A][run].  One warp per run: the run's source is found once
+// (three divisions per run, not per element) and its lanes copy it.
+__global__ void transpose_runs_kernel(const float4* __restrict__ x, float4* __restrict__ out, int64_t A,
+                                      int64_t mid, int64_t B, int64_t runs, int t4, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < runs; r += warps) {
+    // r = ((p * B + j) * mid + m) * A + i over the output.
+    int64_t q = r;
+    const int64_t i = q % A;
+    q /= A;
+    const int64_t m = q % mid;
+    q /= mid;
+    const int64_t j = q % B;
+    const int64_t p = q / B;
+    const int64_t src = ((p * A + i) * mid + m) * B + j;
+    const float4* xs = x + src * t4;
+    float4* os = out + r * t4;
+    for (int k = lane; k < t4; k += 32) {
+      float4 v = xs[k];
+      if (accumulate) {
+        const float4 o = os[k];
+        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+      }
+      os[k] = v;
+    }
+  }
+}
+
 // partial[c][j] = sum of grad rows [c*rpc, (c+1)*rpc) in column j, rows in order.
 __global__ void colsum_partial_kernel(const float* __restrict__ g, float* __restrict__ partial,
                                       int64_t rows, int64_t width, int64_t rows_per_chunk) {
@@ -1935,11 +1966,20 @@ void launch_transpose(const float* x, float* out, const int64_t* dims, int rank,
   for (int i = 0; i < rank; ++i) od.d[i] = dims[i];
   od.d[a] = dims[b];
   od.d[b] = dims[a];
-  const int hi = a > b ? a : b;
+  const int hi = a > b ? a : b, lo = a < b ? a : b;
   int64_t inner = 1;
   for (int i = hi + 1; i < rank; ++i) inner *= dims[i];
-  transpose_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
-      x, out, od, is, rank, a, b, n, inner, accumulate);
+  if (lo != hi && inner % 4 == 0 && inner / 4 >= 8 && inner / 4 <= INT32_MAX && aligned16_host(x) &&
+      aligned16_host(out)) {
+    int64_t mid = 1;
+    for (int i = lo + 1; i < hi; ++i) mid *= dims[i];
+    const int64_t runs = n / inner;
+    transpose_runs_kernel<<<elementwise_blocks(runs * 32, kThreads), kThreads, 0, st>>>(
+        (const float4*)x, (float4*)out, dims[lo], mid, dims[hi], runs, (int)(inner / 4), accumulate);
+  } else {
+    transpose_kernel<<<elementwise_blocks((n + 3) / 4, kThreads), kThreads, 0, st>>>(
+        x, out, od, is, rank, a, b, n, inner, accumulate);
+  }
   check_launch();
 }
 
