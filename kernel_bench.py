@@ -5,6 +5,7 @@ captures summarised under profiles/).
         [--ta] [--tb] [--reps 10]
     python kernel_bench.py rowop --op softmax --rows 65536 --width 4096
     python kernel_bench.py sweep [--div 1] [--reps 20] [--warmup 3]
+    python kernel_bench.py block [--batch 1] [--reps 2] [--mode strict16]
 
 Prints one JSON line with the average time per call (CUDA events on the
 library's stream) and the achieved FLOP/s or GB/s.  `sweep` prints one line
@@ -34,7 +35,8 @@ def main() -> None:
     from tysor_b200.runtime import CudaContext, DeviceBuffer
 
     p = argparse.ArgumentParser()
-    p.add_argument("kind", choices=["matmul", "rowop", "sweep"])
+    p.add_argument("kind", choices=["matmul", "rowop", "sweep", "block"])
+    p.add_argument("--batch", type=int, default=1, help="block: sequences of 2048 tokens")
     p.add_argument("--div", type=int, default=1)
     p.add_argument("--m", type=int, default=4096)
     p.add_argument("--n", type=int, default=5632)
@@ -54,6 +56,22 @@ def main() -> None:
     stream = torch.cuda.ExternalStream(lib.tysor_cuda_context_stream(ctx.handle))
     if a.kind == "sweep":
         sweep(ctx, lib, stream, a)
+        ctx.close()
+        return
+    if a.kind == "block":
+        # `reps` train steps of bench.py's Llama block (d 2048, 16/4 heads, ffn
+        # 5632) on `batch` sequences of 2048 tokens: a small case of the
+        # benchmarked step for profiler captures (batch 1 holds ~5 GB).
+        import bench
+        from tysor_b200.programs import random_parameters
+        from tysor_b200.runtime import CudaGraphExecutor
+        wl = bench.Block()
+        tokens = a.batch * wl.seq
+        g = wl.graph(1, batch=a.batch, seq=wl.seq)
+        ex = CudaGraphExecutor(ctx, g, wl.shapes(1, tokens=tokens), inputs=wl.inputs(0, 1, tokens=tokens),
+                               parameters=random_parameters(g, 1234))
+        print(json.dumps({"kind": "block", "batch": a.batch, "mode": a.mode, "losses": ex.train(a.reps, wl.lr)}))
+        ex.close()
         ctx.close()
         return
     rng = np.random.default_rng(0)
