@@ -229,3 +229,92 @@ def test_llama_style_program_matches_the_hand_lowered_block(with_target):
     np.testing.assert_array_equal(out_g, out_w)
     for ng, nw in zip(names_g, names_w):
         np.testing.assert_array_equal(grads_g[ng].data, grads_w[nw].data, err_msg=nw)
+
+
+def test_repeated_stages_and_binary_stages():
+    """`f()[n]` applies a stage n times (a local layer instance keeps its
+    parameters, a constructor or user layer makes new ones each time), and a
+    stage that is an expression applies its calls to the piped value
+    (frontend_ir.rs:730-786)."""
+    src = """
+layer Proj(t: tensor): tensor:
+  p = linear(8, 8, false)
+  return p(t)
+
+layer shared(x: tensor): tensor:
+  p = linear(8, 8, false)
+  return x -> p()[3]
+
+layer fresh(x: tensor): tensor:
+  return x -> Proj()[3] -> relu()[2] * 2.0
+
+layer model(x: tensor): tensor:
+  return x -> relu() - 1.0
+"""
+    g = lower(src, "shared")
+    assert [n.kind for n in g.nodes].count("ctor") == 1 and [n.kind for n in g.nodes].count("apply") == 3
+    g = lower(src, "fresh")
+    kinds = [(n.kind, n.op or n.binop) for n in g.nodes]
+    assert [k for k in kinds if k[0] == "ctor"] == [("ctor", "linear")] * 3
+    assert [k for k in kinds if k[0] == "primitive"] == [("primitive", "relu")] * 2 and kinds[-1] == ("binary", "*")
+    g = lower(src)
+    assert [(n.kind, n.op or n.binop) for n in g.nodes][-1] == ("binary", "-")
+    with pytest.raises(TysorSyntaxError, match="non-negative integer"):
+        lower("layer model(x: tensor): tensor:\n  return x -> relu()[1.5]\n")
+
+
+def test_reference_repetition_fixture_lowers():
+    """The reference's own repetition fixture (tests/test_arrow_constructor_repeat.ty), each layer."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    for cand in (os.environ.get("TYSOR_REFERENCE_DIR"), os.path.join(os.path.dirname(here), "..", "reference")):
+        path = cand and os.path.join(cand, "tests", "test_arrow_constructor_repeat.ty")
+        if path and os.path.isfile(path):
+            break
+    else:
+        pytest.skip("no reference checkout here")
+    src = open(path).read()
+    kinds = lambda g: [(n.kind, n.op or n.binop) for n in g.nodes if n.kind != "const"]  # noqa: E731
+    assert kinds(lower(src, "ProjectDirect")) == [("ctor", "linear"), ("apply", "+")]
+    assert kinds(lower(src, "RepeatRelu")) == [("primitive", "relu"), ("primitive", "relu"), ("binary", "*")]
+    assert kinds(lower(src, "RepeatLocal")) == [("ctor", "linear"), ("apply", "+"), ("apply", "+")]
+
+
+LM_STYLE = LLAMA_STYLE.split("layer model(")[0].replace(
+    "  eps          : float = 0.000001\n",
+    "  eps          : float = 0.000001\n  vocab_size   : int   = 512\n  n_layers     : int   = 2\n") + """
+layer model(ids: tensor, labels: tensor): tensor:
+  embed = Embedding(llama_config.vocab_size, llama_config.hidden_dim)
+  x = ids -> embed() -> DecoderBlock()[llama_config.n_layers]
+  final_norm = RMSNorm(llama_config.hidden_dim, llama_config.eps)
+  logits = tied_logits(final_norm(x), embed)
+  return cross_entropy(logits, labels)
+"""
+
+
+def test_repeated_user_layer_lm_matches_the_hand_lowered_lm():
+    """`DecoderBlock()[n_layers]` (llama.ty's repetition) with the tied head
+    lowers to the computation of `programs.llama_lm`: loss and every
+    gradient bit-identical in the oracle."""
+    from tysor_b200.programs import llama_lm
+    g = lower(LM_STYLE)
+    want = llama_lm(layers=2, batch=2, seq=64, d_model=256, n_heads=4, n_kv_heads=2, hidden=384, vocab=512,
+                    eps=1e-6)
+    t = 128
+    seqs = np.random.default_rng(5).integers(0, 512, (2, 65))
+    ins = {"ids": seqs[:, :-1].astype(np.float32).reshape(-1), "labels": seqs[:, 1:].astype(np.float32).reshape(-1)}
+    shapes = {"ids": [t], "labels": [t]}
+    pg, pw = random_parameters(g, 4), random_parameters(want, 4)
+    arrays_g, names_g = by_ctor_order(g, pg)
+    arrays_w, names_w = by_ctor_order(want, pw)
+    assert [a.shape for a in arrays_g] == [a.shape for a in arrays_w] and len(names_g) == 20
+
+    def run(graph, params):
+        ps = {k: L.Tensor(list(v.shape), v.reshape(-1).copy()) for k, v in params.items()}
+        values, grads, _ = L.train_step_grads(graph, shapes, inputs=ins, parameters=ps)
+        return values[graph.outputs[0]][1].data, grads
+
+    out_g, grads_g = run(g, pg)
+    out_w, grads_w = run(want, pw)
+    np.testing.assert_array_equal(out_g, out_w)
+    for ng, nw in zip(names_g, names_w):
+        np.testing.assert_array_equal(grads_g[ng].data, grads_w[nw].data, err_msg=nw)

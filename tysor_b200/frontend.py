@@ -10,7 +10,10 @@ Accepted (src/compiler/parser.rs, frontend_ir.rs, ir/builder.rs):
   * statements `name = expr` and `return expr`;
   * expressions: literals (ints, floats, true / false, strings), names,
     `+ - * /` (usual precedence, left-associative), parentheses, calls
-    `f(args)`, and pipelines `expr -> f(args) -> g()`;
+    `f(args)`, and pipelines `expr -> f(args) -> g()`, whose stages may be
+    repeated (`f()[n]`: n applications, n known while lowering) or be
+    expressions over calls (`x -> relu()[2] * 2`: the calls take the piped
+    value, frontend_ir.rs:730-786);
   * `train NAME:` blocks of `key = value` lines (optimizer, lr,
     iteration, objective; other keys are kept and ignored);
   * `#` comments, blank lines, `config NAME:` blocks (`field : type =
@@ -162,6 +165,14 @@ class Call:
 class Pipe:
     src: Any
     stages: List[Call]
+
+
+@dataclass
+class Repeat:
+    """`f(args)[n]` in a pipeline: the stage applied n times."""
+    call: Call
+    count: Any
+    line: int = 0
 
 
 @dataclass
@@ -372,9 +383,10 @@ class _Parser:
         src = self.additive()
         stages = []
         while self.accept("op", "->"):
-            stage = self.postfix()
-            if not isinstance(stage, Call):
-                raise TysorSyntaxError(f"line {self.peek().line}: a pipeline stage must be a call")
+            line = self.peek().line
+            stage = self.additive()
+            if not _has_stage(stage):
+                raise TysorSyntaxError(f"line {line}: a pipeline stage must be a call")
             stages.append(stage)
         return Pipe(src, stages) if stages else src
 
@@ -420,7 +432,13 @@ class _Parser:
                 else:
                     args.append(self.expr())
                 self.accept("op", ",")
-            return Call(tok.text, args, kwargs, tok.line)
+            call = Call(tok.text, args, kwargs, tok.line)
+            if self.peek().kind == "op" and self.peek().text == "[":
+                self.next()
+                count = self.expr()
+                self.expect("op", "]")
+                return Repeat(call, count, tok.line)
+            return call
         if tok.kind == "name" and self.peek(1).kind == "op" and self.peek(1).text == ".":
             self.next()
             self.next()
@@ -446,6 +464,16 @@ class _Parser:
             self.expect("op", ")")
             return node
         raise TysorSyntaxError(f"line {tok.line}: unexpected {tok.text or tok.kind!r}")
+
+
+def _has_stage(node: Any) -> bool:
+    """Whether a pipeline stage expression applies something to the piped
+    value: a call, a repeated call, or +, -, *, / of expressions with one."""
+    if isinstance(node, (Call, Repeat)):
+        return True
+    if isinstance(node, BinOp):
+        return _has_stage(node.lhs) or _has_stage(node.rhs)
+    return False
 
 
 def parse(src: str) -> Module:
@@ -591,14 +619,59 @@ class _Lowerer:
             return self.call(node, None)
         if isinstance(node, Pipe):
             return self.pipe(node.src, node.stages)
+        if isinstance(node, Repeat):
+            raise TysorSyntaxError(f"line {node.line}: `f()[n]` repeats a pipeline stage; it needs a piped input")
         raise TysorSyntaxError(f"cannot lower {node!r}")
 
-    def pipe(self, src: Any, stages: List[Call]) -> Ref:
-        # a -> s1 -> ... -> sn is sn(...s1(a)...), lowered outermost callee first.
+    def pipe(self, src: Any, stages: List[Any]) -> Ref:
+        # a -> s1 -> ... -> sn is sn(...s1(a)...), lowered outermost callee first
+        # (as the reference's builder meets them); `f()[n]` is n stages f().
         if not stages:
             return self.value(src)
-        *inner, last = stages
-        return self.call(last, (src, inner))
+        flat: List[Any] = []
+        for st in stages:
+            if isinstance(st, Repeat):
+                flat += [st.call] * self.repeat_count(st)
+            else:
+                flat.append(st)
+        if not flat:
+            return self.value(src)
+        *inner, last = flat
+        return self.stage(last, (src, inner))
+
+    def repeat_count(self, st: Repeat) -> int:
+        ok, n = self.const_value(st.count)
+        if not ok or not isinstance(n, int) or isinstance(n, bool) or n < 0:
+            raise TysorSyntaxError(f"line {st.line}: a stage repetition count must be a non-negative integer "
+                                   "known while lowering")
+        return n
+
+    def piped_value(self, piped) -> Ref:
+        if isinstance(piped, tuple):
+            src, inner = piped
+            return self.pipe(src, inner)
+        return piped
+
+    def stage(self, st: Any, piped) -> Ref:
+        """One pipeline stage applied to the piped value (a (source, inner
+        stages) pair lowered when the stage needs it, or a lowered value):
+        a call; a repeated call; or a binary expression whose operands with
+        calls in them are stages on the same piped value (lowered once) and
+        whose others are plain values (frontend_ir.rs:730-786)."""
+        if isinstance(st, Call):
+            return self.call(st, piped)
+        if isinstance(st, Repeat):
+            n = self.repeat_count(st)
+            cur = piped
+            for _ in range(n):
+                cur = self.call(st.call, cur)
+            return self.piped_value(cur)
+        if isinstance(st, BinOp):
+            cur = self.piped_value(piped)
+            lhs = self.stage(st.lhs, cur) if _has_stage(st.lhs) else self.arg(st.lhs)
+            rhs = self.stage(st.rhs, cur) if _has_stage(st.rhs) else self.arg(st.rhs)
+            return self.b.binary(st.op, lhs, rhs)
+        raise TysorSyntaxError(f"cannot use {st!r} as a pipeline stage")
 
     def call(self, node: Call, piped) -> Ref:
         if node.kwargs:
@@ -606,8 +679,7 @@ class _Lowerer:
         f = node.func
 
         def piped_input() -> Ref:
-            src, inner = piped
-            return self.pipe(src, inner)
+            return self.piped_value(piped)
 
         if f in self.env and not isinstance(self.env[f], Const):
             # calling a constructed layer: Apply(callee, input)
