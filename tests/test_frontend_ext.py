@@ -318,3 +318,12 @@ def test_repeated_user_layer_lm_matches_the_hand_lowered_lm():
     np.testing.assert_array_equal(out_g, out_w)
     for ng, nw in zip(names_g, names_w):
         np.testing.assert_array_equal(grads_g[ng].data, grads_w[nw].data, err_msg=nw)
+
+
+def test_pipeline_continuation_lines():
+    """A line starting with `->` continues the pipeline above it (the layout
+    of examples/llama.ty's attention)."""
+    one = "layer model(x: tensor): tensor:\n  y = x -> relu() -> scale(2.0) -> relu()\n  return y\n"
+    split = ("layer model(x: tensor): tensor:\n  y = x -> relu()\n        -> scale(2.0)\n"
+             "        -> relu()\n  return y\n")
+    assert structure(lower(one)) == structure(lower(split))

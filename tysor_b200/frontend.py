@@ -16,8 +16,9 @@ Accepted (src/compiler/parser.rs, frontend_ir.rs, ir/builder.rs):
     value, frontend_ir.rs:730-786);
   * `train NAME:` blocks of `key = value` lines (optimizer, lr,
     iteration, objective; other keys are kept and ignored);
-  * `#` comments, blank lines, `config NAME:` blocks (`field : type =
-    value`), whose fields are read as `NAME.field`.
+  * `#` comments, blank lines, lines starting with `->` (they continue the
+    pipeline above), `config NAME:` blocks (`field : type = value`), whose
+    fields are read as `NAME.field`.
 
 Lowering follows the reference builder (ir/builder.rs:97-174): parameters
 first, then each statement's expression in post-order; a literal argument
@@ -92,7 +93,11 @@ def tokenize(src: str) -> List[Tok]:
         line = raw.split("#", 1)[0].rstrip()
         if not line.strip():
             continue
-        if depth == 0:
+        # A line that starts with `->` continues the previous line's pipeline.
+        cont = depth == 0 and line.lstrip(" \t").startswith("->") and bool(toks) and toks[-1].kind == "nl"
+        if cont:
+            toks.pop()
+        if depth == 0 and not cont:
             width = len(line) - len(line.lstrip(" \t"))
             if width > indents[-1]:
                 indents.append(width)
