@@ -195,6 +195,11 @@ mod owners {
         CString::new(text).map_err(|_| format!("'{text}' contains a NUL byte"))
     }
 
+    /// Selects the matmul engine of new contexts: `strict` (3xTF32, the
+    /// default), `strict16` (the same three products over scaled fp16
+    /// halves), `fast` (1xTF32) or `exact` (CUDA cores in k order).
+    pub const MATMUL_ENV: &str = "TYSOR_CUDA_MATMUL";
+
     /// A CUDA context (device, stream, error word) owned by Rust.
     pub struct Context(*mut c_void);
 
@@ -202,10 +207,24 @@ mod owners {
         pub fn new(device: i32) -> Result<Self, String> {
             let ptr = unsafe { ffi::tysor_cuda_context_new(device as c_int) };
             if ptr.is_null() {
-                Err(format!("CUDA context on device {device}: {}", last_error()))
-            } else {
-                Ok(Context(ptr))
+                return Err(format!("CUDA context on device {device}: {}", last_error()));
             }
+            let context = Context(ptr);
+            if let Ok(mode) = std::env::var(MATMUL_ENV) {
+                let code: c_int = match mode.as_str() {
+                    "strict" => 0,
+                    "fast" => 1,
+                    "exact" => 2,
+                    "strict16" => 3,
+                    other => {
+                        return Err(format!("{MATMUL_ENV}={other}: expected strict, strict16, fast or exact"))
+                    }
+                };
+                if !unsafe { ffi::tysor_cuda_set_matmul_mode(context.0, code) } {
+                    return Err(format!("{MATMUL_ENV}: {}", last_error()));
+                }
+            }
+            Ok(context)
         }
 
         pub fn raw(&self) -> *mut c_void {

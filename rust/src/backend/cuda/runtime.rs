@@ -15,7 +15,8 @@
 //! There is no fallback: without a device (or without the library, when nvcc
 //! was missing at build time) every entry point returns an error, the policy
 //! TYSOR_METAL_REQUIRE_NATIVE=1 sets for Metal (metal/runtime.rs:347-360).
-//! `TYSOR_CUDA_DEVICE` picks the device ordinal (default 0).
+//! `TYSOR_CUDA_DEVICE` picks the device ordinal (default 0), `TYSOR_CUDA_MATMUL`
+//! the matmul engine (native.rs::MATMUL_ENV).
 
 #![cfg_attr(not(tysor_cuda), allow(dead_code, unused_imports))]
 

@@ -69,3 +69,17 @@ def test_fixture_dtype_strings_follow_the_reference_rules():
         assert g.value_dtypes()[g.outputs[0]] == want.dtype, fx.name
         seen.add(want.dtype)
     assert seen == {"float16", "float32"}  # the transformer fixture starts at an Embedding
+
+
+def test_matmul_engine_names_are_checked_before_any_device_work(monkeypatch):
+    """CudaContext takes its matmul engine from the argument or from
+    TYSOR_CUDA_MATMUL; an unknown name is refused before the library is
+    asked for a device."""
+    import pytest
+
+    from tysor_b200.runtime import CudaContext
+    with pytest.raises(ValueError, match="strict16"):
+        CudaContext(0, matmul="bogus")
+    monkeypatch.setenv("TYSOR_CUDA_MATMUL", "tf32x9")
+    with pytest.raises(ValueError, match="tf32x9"):
+        CudaContext(0)

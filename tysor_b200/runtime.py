@@ -38,13 +38,18 @@ class CudaContext:
     Buffers and graph executors made on a context must be released before
     it; `close()` releases any that are still open."""
 
-    def __init__(self, device: int = 0, matmul: str = "strict"):
+    def __init__(self, device: int = 0, matmul: Optional[str] = None):
+        """`matmul`: strict (3xTF32), strict16, fast or exact; by default
+        $TYSOR_CUDA_MATMUL, else strict."""
+        mode = matmul or os.environ.get("TYSOR_CUDA_MATMUL", "strict")
+        if mode not in MATMUL_MODES:
+            raise ValueError(f"matmul mode {mode!r}: expected one of {', '.join(MATMUL_MODES)}")
         self._lib = native.lib()
         self.handle = self._lib.tysor_cuda_context_new(int(device))
         check(self.handle, "tysor_cuda_context_new")
         self.device = device
         self._children = weakref.WeakSet()
-        self.set_matmul_mode(matmul)
+        self.set_matmul_mode(mode)
 
     def _adopt(self, child) -> None:
         self._children.add(child)
