@@ -1511,25 +1511,40 @@ __global__ void __launch_bounds__(256) pack16_cols_kernel(const float* __restric
     const int c4 = threadIdx.x & 15, r0 = threadIdx.x >> 4;
     const int c = c0 + 4 * c4;
     const bool aligned = (ld & 3) == 0 && (((uintptr_t)x) & 15) == 0;
+    if (aligned && k0 + 64 <= K && c0 + 64 <= R) {
+      // A whole aligned tile: four independent, unguarded float4 loads.
+      float4 v[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int kr = r0 + 16 * i, k = k0 + kr;
-      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (k < K && c < R) {
-        const float* p = x + (int64_t)k * ld + c;
-        if (aligned && c + 3 < R) {
-          v = __ldg((const float4*)p);
-        } else {
-          v.x = __ldg(p);
-          v.y = c + 1 < R ? __ldg(p + 1) : 0.0f;
-          v.z = c + 2 < R ? __ldg(p + 2) : 0.0f;
-          v.w = c + 3 < R ? __ldg(p + 3) : 0.0f;
-        }
+      for (int i = 0; i < 4; ++i) v[i] = __ldg((const float4*)(x + (int64_t)(k0 + r0 + 16 * i) * ld + c));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kr = r0 + 16 * i;
+        tile[kr][4 * c4] = v[i].x;
+        tile[kr][4 * c4 + 1] = v[i].y;
+        tile[kr][4 * c4 + 2] = v[i].z;
+        tile[kr][4 * c4 + 3] = v[i].w;
       }
-      tile[kr][4 * c4] = v.x;
-      tile[kr][4 * c4 + 1] = v.y;
-      tile[kr][4 * c4 + 2] = v.z;
-      tile[kr][4 * c4 + 3] = v.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kr = r0 + 16 * i, k = k0 + kr;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < K && c < R) {
+          const float* p = x + (int64_t)k * ld + c;
+          if (aligned && c + 3 < R) {
+            v = __ldg((const float4*)p);
+          } else {
+            v.x = __ldg(p);
+            v.y = c + 1 < R ? __ldg(p + 1) : 0.0f;
+            v.z = c + 2 < R ? __ldg(p + 2) : 0.0f;
+            v.w = c + 3 < R ? __ldg(p + 3) : 0.0f;
+          }
+        }
+        tile[kr][4 * c4] = v.x;
+        tile[kr][4 * c4 + 1] = v.y;
+        tile[kr][4 * c4 + 2] = v.z;
+        tile[kr][4 * c4 + 3] = v.w;
+      }
     }
   }
   __syncthreads();
