@@ -1408,6 +1408,39 @@ __global__ void __launch_bounds__(256) pack16_rows_kernel(const float* __restric
   const float* row = x + (int64_t)r * ld;
   const bool vec = ((ld & 3) == 0) && ((((uintptr_t)x) & 15) == 0);
   const int K4 = vec ? K >> 2 : 0;
+  if (vec && K4 <= 256 * 8) {
+    // Rows up to 8192 wide stay in registers: one read, loads issued together.
+    float4 v[8];
+    float m = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = threadIdx.x + 256 * u;
+      v[u] = i < K4 ? __ldg((const float4*)row + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) m = fmaxf(m, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+    for (int i = 4 * K4 + threadIdx.x; i < K; i += 256) m = fmaxf(m, fabsf(row[i]));
+    m = block_max256(m, red);
+    const int e = pack16_exponent(m);
+    const float up = pow2f(e);
+    if (threadIdx.x == 0) factor[r] = pow2f(-e);
+    __half* h = hi + (int64_t)r * Kp;
+    __half* l = lo + (int64_t)r * Kp;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = threadIdx.x + 256 * u;
+      if (i >= K4) break;
+      __align__(8) __half hv[4], lv[4];
+      pack16_one(v[u].x, up, &hv[0], &lv[0]);
+      pack16_one(v[u].y, up, &hv[1], &lv[1]);
+      pack16_one(v[u].z, up, &hv[2], &lv[2]);
+      pack16_one(v[u].w, up, &hv[3], &lv[3]);
+      *(uint2*)(h + 4 * i) = *(const uint2*)hv;
+      *(uint2*)(l + 4 * i) = *(const uint2*)lv;
+    }
+    for (int i = 4 * K4 + threadIdx.x; i < K; i += 256) pack16_one(row[i], up, h + i, l + i);
+    return;
+  }
   float mx = 0.0f;
   for (int i = threadIdx.x; i < K4; i += 256) {
     const float4 v = __ldg((const float4*)row + i);
