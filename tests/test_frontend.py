@@ -6,9 +6,10 @@ handling, on the CPU.
   strings, nodes, outputs, train settings) -- when a reference checkout is
   available (TYSOR_REFERENCE_DIR or ../reference).
 * Programs written here: pipelines, binary operators and constants,
-  constructors, config fields, train blocks, and the errors for what the
-  front end does not lower (user-layer calls, unknown names, keyword
-  arguments).
+  constructors, config fields, train blocks, keyword arguments (kept in
+  their written position, as the reference's builder does), and the errors
+  for what the front end does not lower (recursion, unknown names, None
+  where a value is needed).
 * `python -m tysor_b200` rejects bad command lines with exit code 2 and the
   reference's messages, and reports a program error with exit code 1.
 """
@@ -105,7 +106,6 @@ layer model(x: tensor[float16]): tensor[float16]:
     ("config a:\n  n : int = 1\nconfig b:\n  n : int = 2\n\n"
      "layer model(x: tensor): tensor:\n  return scale(x, config.n)\n", "exactly one config block"),
     ("layer model(x: tensor): tensor:\n  return relu(z)\n", "unknown name"),
-    ("layer model(x: tensor): tensor:\n  return reshape(x, heads: 4)\n", "keyword"),
     ("layer model(x: tensor): tensor:\n  y = x\n", "no return"),
     ("layer other(x: tensor): tensor:\n  return x\n", "Entry function 'model' not found"),
     ("layer model(x: tensor): tensor:\n  return x ! 2\n", "unexpected character"),
@@ -138,3 +138,11 @@ def test_cli_reports_a_bad_program(tmp_path):
     prog.write_text("layer model(x: tensor): tensor:\n  return relu(z)\n")
     res = run_cli(str(prog), "--run", "--shape", "x=2x3")
     assert res.returncode == 1 and "unknown name" in res.stderr
+
+
+def test_keyword_arguments_keep_their_position():
+    """The reference's builder lowers a call's arguments in written order and
+    drops their names (ir/builder.rs:119-123)."""
+    named = lower("layer model(x: tensor): tensor:\n  return repeat_kv(x, times: 2)\n")
+    plain = lower("layer model(x: tensor): tensor:\n  return repeat_kv(x, 2)\n")
+    assert signature(named) == signature(plain)

@@ -327,3 +327,29 @@ def test_pipeline_continuation_lines():
     split = ("layer model(x: tensor): tensor:\n  y = x -> relu()\n        -> scale(2.0)\n"
              "        -> relu()\n  return y\n")
     assert structure(lower(one)) == structure(lower(split))
+
+
+def test_reference_llama_example_lowers():
+    """The reference's examples/llama.ty lowers: its 32 DecoderBlocks inlined
+    (`DecoderBlock()[n_layers]`), its own RMSNorm layer shadowing the library
+    constructor, `config.head_dim`, the three-argument `scale`, `reshape(heads:
+    n)` with the name dropped, and `loss` present only when `targets` is an
+    input.  (Running it is another matter: its `q * k` is an elementwise
+    product under the reference's `*`.)"""
+    import collections
+    here = os.path.dirname(os.path.abspath(__file__))
+    for cand in (os.environ.get("TYSOR_REFERENCE_DIR"), os.path.join(os.path.dirname(here), "..", "reference")):
+        path = cand and os.path.join(cand, "examples", "llama.ty")
+        if path and os.path.isfile(path):
+            break
+    else:
+        pytest.skip("no reference checkout here")
+    src = open(path).read()
+    full = lower(src, inputs=["idx", "targets"])
+    ctors = collections.Counter(n.op for n in full.nodes if n.kind == "ctor")
+    calls = collections.Counter(n.op for n in full.nodes if n.kind == "call")
+    assert ctors == {"linear": 32 * 7 + 1, "Dropout": 33, "Embedding": 1, "Softmax": 32, "SiLU": 32}
+    assert calls["rms_norm"] == 65 and calls["causal_mask"] == 32 and calls["cross_entropy"] == 1
+    assert len(full.outputs) == 2
+    logits_only = lower(src, inputs=["idx"])
+    assert len(logits_only.outputs) == 1 and "cross_entropy" not in {n.op for n in logits_only.nodes}

@@ -53,7 +53,10 @@ semantic_analyzer.rs:427-442 knows only declared config fields):
     no value); `None` leaves a name without value, and `return a, b` drops a
     None entry;
   * integer arithmetic on compile-time integers in call arguments folds to
-    an integer (sizes, counts).
+    an integer (sizes, counts);
+  * a user layer named like a library constructor or function (llama.ty's
+    own `RMSNorm`) is the one called.
+With these, the reference's examples/llama.ty lowers.
 """
 from __future__ import annotations
 
@@ -431,9 +434,13 @@ class _Parser:
             args, kwargs = [], []
             while not self.accept("op", ")"):
                 if self.peek().kind == "name" and self.peek(1).kind == "op" and self.peek(1).text == ":":
+                    # `name: value`: the reference's builder keeps the value in
+                    # its written position and drops the name (ir/builder.rs:119-123).
                     key = self.next().text
                     self.next()
-                    kwargs.append((key, self.expr()))
+                    value = self.expr()
+                    kwargs.append((key, value))
+                    args.append(value)
                 else:
                     args.append(self.expr())
                 self.accept("op", ",")
@@ -679,8 +686,6 @@ class _Lowerer:
         raise TysorSyntaxError(f"cannot use {st!r} as a pipeline stage")
 
     def call(self, node: Call, piped) -> Ref:
-        if node.kwargs:
-            raise TysorSyntaxError(f"line {node.line}: keyword arguments are not supported ({node.func})")
         f = node.func
 
         def piped_input() -> Ref:
@@ -695,6 +700,9 @@ class _Lowerer:
             if len(node.args) != 1:
                 raise TysorSyntaxError(f"line {node.line}: a layer takes one input")
             return self.b.apply(self.env[f], self.value(node.args[0]))
+        if f in self.mod.functions:
+            # A user layer shadows a library name (examples/llama.ty defines its own RMSNorm).
+            return self.inline(self.mod.functions[f], node, piped_input() if piped is not None else None)
         if f in LIBRARY_CTORS:
             ctor = self.b.ctor(f, *[self.arg(a) for a in node.args])
             if piped is not None:
@@ -715,8 +723,6 @@ class _Lowerer:
         if f in PRIMITIVE_OPS or f in LIBRARY_CALLS or f == "tied_logits":
             args = ([piped_input()] if piped is not None else []) + [self.arg(a) for a in node.args]
             return self.b.call(f, *args)
-        if f in self.mod.functions:
-            return self.inline(self.mod.functions[f], node, piped_input() if piped is not None else None)
         raise TysorSyntaxError(f"line {node.line}: unknown function {f!r}")
 
     def inline(self, fn: Function, node: Call, piped: Optional[Ref]) -> Ref:
