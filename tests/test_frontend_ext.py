@@ -3,12 +3,13 @@
 `config.head_dim`, conditional expressions and optional inputs, tuple
 returns, integer folding of compile-time arithmetic in arguments.
 
-The end-to-end check writes the Llama decoder block with these extensions
-(user layers, a derived head_dim, the three-argument scale, an optional
-target) and runs it through the oracle next to the hand-lowered
-`programs.llama_block`: with parameters drawn in constructor order, the
-output and every gradient are bit-identical (the same operations on the
-same values)."""
+The end-to-end checks take the programs in examples/ -- the Llama decoder
+block written with these extensions (user layers, a derived head_dim, the
+three-argument scale, an optional target) and a 2-layer LM with
+`DecoderBlock()[n_layers]` -- and run them through the oracle next to the
+hand-lowered `programs.llama_block` / `programs.llama_lm`: with parameters
+drawn in constructor order, the output and every gradient are bit-identical
+(the same operations on the same values)."""
 import os
 import sys
 
@@ -135,61 +136,9 @@ layer model(x: tensor): tensor:
     assert not any(n.kind == "binary" for n in g.nodes)
 
 
-LLAMA_STYLE = """
-config llama_config:
-  batch        : int   = 2
-  seq          : int   = 64
-  hidden_dim   : int   = 256
-  n_heads      : int   = 4
-  n_kv_heads   : int   = 2
-  intermediate : int   = 384
-  rope_theta   : float = 10000.0
-  eps          : float = 0.000001
-
-layer Heads(t: tensor, nh: int): tensor:
-  return t -> reshape(llama_config.batch, llama_config.seq, nh, config.head_dim) -> transpose(1, 2)
-
-layer DecoderBlock(x: tensor): tensor:
-  attn_norm = RMSNorm(llama_config.hidden_dim, llama_config.eps)
-  q_proj    = linear(llama_config.hidden_dim, llama_config.hidden_dim, false)
-  k_proj    = linear(llama_config.hidden_dim, llama_config.n_kv_heads * config.head_dim, false)
-  v_proj    = linear(llama_config.hidden_dim, llama_config.n_kv_heads * config.head_dim, false)
-  o_proj    = linear(llama_config.hidden_dim, llama_config.hidden_dim, false)
-  ffn_norm  = RMSNorm(llama_config.hidden_dim, llama_config.eps)
-  gate_proj = linear(llama_config.hidden_dim, llama_config.intermediate, false)
-  up_proj   = linear(llama_config.hidden_dim, llama_config.intermediate, false)
-  down_proj = linear(llama_config.intermediate, llama_config.hidden_dim, false)
-  act       = SiLU()
-  softmax   = Softmax()
-
-  hn = attn_norm(x)
-  q = hn -> q_proj() -> Heads(llama_config.n_heads) -> rope(config.head_dim, llama_config.rope_theta)
-  k = hn -> k_proj() -> Heads(llama_config.n_kv_heads) -> rope(config.head_dim, llama_config.rope_theta)
-  v = hn -> v_proj() -> Heads(llama_config.n_kv_heads)
-  k = k -> repeat_kv(llama_config.n_heads / llama_config.n_kv_heads)
-  v = v -> repeat_kv(llama_config.n_heads / llama_config.n_kv_heads)
-
-  scores = matmul(q, transpose(k, 2, 3)) -> scale(llama_config.hidden_dim, llama_config.n_heads)
-  probs = scores -> causal_mask() -> softmax()
-  ctx = matmul(probs, v) -> transpose(1, 2) -> reshape(llama_config.batch * llama_config.seq, llama_config.hidden_dim)
-  h = x + (ctx -> o_proj())
-
-  hn2 = ffn_norm(h)
-  ff = (hn2 -> gate_proj() -> act()) * (hn2 -> up_proj())
-  return h + (ff -> down_proj())
-
-layer model(x: tensor, target=None): tensor:
-  out = DecoderBlock(x)
-  d = out - target if target else out
-  loss = d * d if target else out
-  return loss
-
-train model:
-  optimizer = "sgd"
-  lr = 0.0001
-  iteration = 1
-  objective = loss
-"""
+EXAMPLES = os.path.join(ROOT, "examples")
+with open(os.path.join(EXAMPLES, "llama_block.ty")) as _f:
+    LLAMA_STYLE = _f.read()
 
 CFG = dict(batch=2, seq=64, d_model=256, n_heads=4, n_kv_heads=2, hidden=384, eps=1e-6, lr=1e-4)
 
@@ -279,16 +228,8 @@ def test_reference_repetition_fixture_lowers():
     assert kinds(lower(src, "RepeatLocal")) == [("ctor", "linear"), ("apply", "+"), ("apply", "+")]
 
 
-LM_STYLE = LLAMA_STYLE.split("layer model(")[0].replace(
-    "  eps          : float = 0.000001\n",
-    "  eps          : float = 0.000001\n  vocab_size   : int   = 512\n  n_layers     : int   = 2\n") + """
-layer model(ids: tensor, labels: tensor): tensor:
-  embed = Embedding(llama_config.vocab_size, llama_config.hidden_dim)
-  x = ids -> embed() -> DecoderBlock()[llama_config.n_layers]
-  final_norm = RMSNorm(llama_config.hidden_dim, llama_config.eps)
-  logits = tied_logits(final_norm(x), embed)
-  return cross_entropy(logits, labels)
-"""
+with open(os.path.join(EXAMPLES, "llama_lm.ty")) as _f:
+    LM_STYLE = _f.read()
 
 
 def test_repeated_user_layer_lm_matches_the_hand_lowered_lm():
