@@ -1600,6 +1600,60 @@ __global__ void __launch_bounds__(256) pack16_cols_kernel(const float* __restric
   }
 }
 
+// The same reduction four columns at a time: one block row of threads per
+// output row (blockIdx.y = batch item * M + row), float4 loads and stores,
+// no per-element index division; the parts are added in the same order and
+// the epilogue applied per element as above (bit-identical results).  Needs
+// N, ldw, C's pitch and batch stride multiples of 4, C and bias 16-byte
+// aligned, batch * M <= 65535.
+__global__ void splitk_reduce4_kernel(const float* __restrict__ ws, int splits, int M, int N, int64_t ldw,
+                                      GemmOutput out, GemmEpilogue ep) {
+  const int bm = blockIdx.y;  // batch item * M + row
+  const int b = bm / M, row = bm - b * M;
+  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c >= N) return;
+  const int batch = gridDim.y / M;
+  float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int p = 0; p < splits; ++p) {
+    const float4 w = __ldg((const float4*)(ws + ((int64_t)(p * batch + b) * M + row) * ldw + c));
+    v.x = v.x + w.x;
+    v.y = v.y + w.y;
+    v.z = v.z + w.z;
+    v.w = v.w + w.w;
+  }
+  float* e = &v.x;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float r = e[q] * ep.alpha;
+    if (ep.bias != nullptr) r = r + ep.bias[c + q];
+    if (ep.relu) r = fmaxf(r, 0.0f);
+    e[q] = r;
+  }
+  float4* dst = (float4*)(out.ptr + (int64_t)b * out.batch_stride + (int64_t)row * out.ld + c);
+  if (ep.accumulate) {
+    const float4 o = *dst;
+    v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+  }
+  *dst = v;
+}
+
+// Launches the split-K reduction (the float4 form where its layout rules hold).
+void launch_splitk_reduce(const float* ws, int splits, int batch, int M, int N, int64_t ldw, const GemmOutput& C,
+                          const GemmEpilogue& ep, cudaStream_t st) {
+  const bool vec = N % 4 == 0 && ldw % 4 == 0 && C.ld % 4 == 0 && (batch == 1 || C.batch_stride % 4 == 0) &&
+                   (((uintptr_t)C.ptr) & 15) == 0 && (ep.bias == nullptr || (((uintptr_t)ep.bias) & 15) == 0) &&
+                   (int64_t)batch * M <= 65535;
+  if (vec) {
+    const dim3 grid((unsigned)ceil_div(N / 4, 128), (unsigned)(batch * M));
+    splitk_reduce4_kernel<<<grid, 128, 0, st>>>(ws, splits, M, N, ldw, C, ep);
+  } else {
+    splitk_reduce_kernel<<<elementwise_blocks((int64_t)batch * M * N, 256), 256, 0, st>>>(ws, splits, batch, M, N,
+                                                                                          ldw, C, ep);
+  }
+  TYSOR_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 // lo(x) = tf32_lo(x), elementwise over a contiguous span.
 __global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n >> 2;
@@ -2134,9 +2188,7 @@ static int launch_f16x3(int64_t M, int64_t N, int64_t K, const GemmOperand& A, c
                                                              d_err, st);
   }
   if (splits > 1) {
-    splitk_reduce_kernel<<<elementwise_blocks(M * N, 256), 256, 0, st>>>(scratch.ws, splits, 1, im, in, ldw, C, ep);
-    TYSOR_CUDA(cudaGetLastError());
-    g_launches.fetch_add(1, std::memory_order_relaxed);
+    launch_splitk_reduce(scratch.ws, splits, 1, im, in, ldw, C, ep, st);
   }
   return 1;
 }
@@ -2278,10 +2330,7 @@ int gemm_launch_impl(int batch, int64_t M, int64_t N, int64_t K, const GemmOpera
       else dispatch_pp<256, false>(amn, bmn, ma, malo, mb, mblo, mc32, my, ep, batch, im, in, ik, splits, d_err, st);
     }
     if (splits > 1) {
-      splitk_reduce_kernel<<<elementwise_blocks((int64_t)batch * M * N, 256), 256, 0, st>>>(scratch.ws, splits, batch, im,
-                                                                                            in, ldw, C, ep);
-      TYSOR_CUDA(cudaGetLastError());
-      g_launches.fetch_add(1, std::memory_order_relaxed);
+      launch_splitk_reduce(scratch.ws, splits, batch, im, in, ldw, C, ep, st);
     }
     return 1;
   }
