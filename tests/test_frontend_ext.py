@@ -294,3 +294,19 @@ def test_reference_llama_example_lowers():
     assert len(full.outputs) == 2
     logits_only = lower(src, inputs=["idx"])
     assert len(logits_only.outputs) == 1 and "cross_entropy" not in {n.op for n in logits_only.nodes}
+
+
+def test_unary_minus_is_zero_minus_its_operand():
+    """`-e` lowers as the binary `0 - e` (the reference's unary minus,
+    compiler/frontend_ir.rs:606-615); a negative number stays a literal, and
+    the oracle runs the result."""
+    neg = "layer model(x: tensor, w: tensor): tensor:\n  return -(x + w) * -w\n"
+    sub = "layer model(x: tensor, w: tensor): tensor:\n  return (0 - (x + w)) * (0 - w)\n"
+    assert structure(lower(neg)) == structure(lower(sub))
+    lit = lower("layer model(x: tensor): tensor:\n  return scale(x, -0.5)\n")
+    assert [n.kind for n in lit.nodes] == ["const", "primitive"] and lit.nodes[0].const == -0.5
+    twice = lower("layer model(x: tensor): tensor:\n  return --x\n")
+    assert [n.binop for n in twice.nodes if n.kind == "binary"] == ["-", "-"]
+    out, _ = L.run_forward(lower(neg), {"x": [2, 3], "w": [2, 3]})
+    x = L.synthetic([2, 3]).data
+    np.testing.assert_array_equal(out.data, -(x + x) * -x)

@@ -424,6 +424,11 @@ class _Parser:
             self.next()
             v = self.atom()
             return Lit(-v.value)
+        if self.peek().kind == "op" and self.peek().text == "-":
+            # -e is the binary 0 - e, as the reference lowers a unary minus
+            # (compiler/frontend_ir.rs:606-615, parser.rs:402-409).
+            self.next()
+            return BinOp("-", Lit(0), self.unary())
         return self.postfix()
 
     def postfix(self) -> Any:
