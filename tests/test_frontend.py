@@ -127,7 +127,8 @@ def test_cli_rejects_bad_command_lines(tmp_path):
                       ((str(prog), "--bogus"), "unknown option: --bogus"),
                       ((str(prog), "--shape", "x=2y3"), "invalid dimension '2y3' in shape 'x=2y3'"),
                       ((str(prog), "--backend", "local"), "backend 'local' is not part of this build"),
-                      ((str(prog), "--backend", "tpu"), "unsupported backend 'tpu'")]:
+                      ((str(prog), "--backend", "tpu"), "unsupported backend 'tpu'"),
+                      ((str(prog), "--ir", "--run"), "option --ir belongs to the reference compiler")]:
         res = run_cli(*args)
         assert res.returncode == 2, (args, res.stderr)
         assert msg in res.stderr and "usage:" in res.stderr, (args, res.stderr)

@@ -24,6 +24,11 @@ from .graph import parse_shape_spec
 USAGE = ("tysor <input.ty> [--run] [--backward] [--train] [--entry <name>] [--backend <cuda>] "
          "[--shape <name>=<dim>x<dim>...]")
 REFERENCE_BACKENDS = ("local", "metal", "pytorch")
+# The reference CLI's compiler-introspection and code-emission flags
+# (src/main.rs:57-66): they print the reference compiler's stages, which
+# this build does not include.
+REFERENCE_COMPILER_FLAGS = ("--emit-metal", "--emit-pytorch", "--tokens", "--ast", "--semantics", "--ir",
+                            "--print-pipeline")
 
 
 class CliError(ValueError):
@@ -59,6 +64,8 @@ def parse_cli(argv: List[str]):
             except ValueError as e:
                 raise CliError(str(e)) from None
             opts["shapes"][name] = dims
+        elif a in REFERENCE_COMPILER_FLAGS:
+            raise CliError(f"option {a} belongs to the reference compiler, which this build does not include")
         elif a.startswith("--"):
             raise CliError(f"unknown option: {a}")
         else:
