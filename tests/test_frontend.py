@@ -108,7 +108,10 @@ layer model(x: tensor[float16]): tensor[float16]:
     ("layer model(x: tensor): tensor:\n  return relu(z)\n", "unknown name"),
     ("layer model(x: tensor): tensor:\n  y = x\n", "no return"),
     ("layer other(x: tensor): tensor:\n  return x\n", "Entry function 'model' not found"),
-    ("layer model(x: tensor): tensor:\n  return x ! 2\n", "unexpected character"),
+    ("layer model(x: tensor): tensor:\n  return x & 2\n", "unexpected character"),
+    ("layer model(x: tensor): tensor:\n  return x ! 2\n", "expected 'nl', got '!'"),
+    ("layer model(x: tensor): tensor:\n  return !x\n", "not a graph value"),
+    ("layer model(x: tensor): tensor:\n  return relu(x > 1)\n", "not a graph value"),
 ])
 def test_what_the_front_end_does_not_lower_is_an_error(src, msg):
     with pytest.raises(TysorSyntaxError, match=msg):

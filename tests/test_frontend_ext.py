@@ -310,3 +310,30 @@ def test_unary_minus_is_zero_minus_its_operand():
     out, _ = L.run_forward(lower(neg), {"x": [2, 3], "w": [2, 3]})
     x = L.synthetic([2, 3]).data
     np.testing.assert_array_equal(out.data, -(x + x) * -x)
+
+
+def test_logical_conditions():
+    """Conditions take `!`, `&&` and `||` over compile-time values and input
+    names, with the reference's precedence (`||` below `&&` below the
+    comparisons, `!` binding tightest: compiler/parser.rs:351-361, 402-409)
+    and its constant rules (frontend_ir.rs:1286-1300)."""
+    src = """
+config c:
+  use_relu : bool = true
+  depth    : int = 3
+
+layer model(x: tensor, target=None): (tensor, tensor):
+  y = relu(x) if !c.use_relu || c.depth > 2 && c.depth < 4 else x
+  z = scale(y, 2.0) if !(c.depth == 3) else y
+  loss = z - target if target && c.use_relu else None
+  flat = z if !target else relu(z)
+  return flat, loss
+"""
+    full = lower(src)
+    assert [n.op for n in full.nodes if n.kind in ("primitive", "call")] == ["relu", "relu"]
+    assert len(full.outputs) == 2 and any(n.kind == "binary" for n in full.nodes)
+    bare = lower(src, inputs=["x"])
+    assert [n.op for n in bare.nodes if n.kind in ("primitive", "call")] == ["relu"]
+    assert len(bare.outputs) == 1 and not any(n.kind == "binary" for n in bare.nodes)
+    with pytest.raises(TysorSyntaxError, match="must be known while lowering"):
+        lower("layer model(x: tensor): tensor:\n  return x if x > 1 && true else x\n")

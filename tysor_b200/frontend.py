@@ -77,7 +77,7 @@ _TOKEN = re.compile(r"""
     (?P<num>\d+\.\d*(?:[eE][-+]?\d+)?|\d+[eE][-+]?\d+|\.\d+(?:[eE][-+]?\d+)?|\d+)
   | (?P<name>[A-Za-z_][A-Za-z0-9_]*)
   | (?P<str>"[^"\\n]*")
-  | (?P<op>->|==|!=|<=|>=|[-+*/()\[\],:=.<>])
+  | (?P<op>->|==|!=|<=|>=|&&|\|\||[-+*/()\[\],:=.<>!])
 """, re.X)
 
 
@@ -188,6 +188,18 @@ class Compare:
     op: str
     lhs: Any
     rhs: Any
+
+
+@dataclass
+class Logic:
+    op: str  # "&&" or "||"
+    lhs: Any
+    rhs: Any
+
+
+@dataclass
+class Not:
+    operand: Any
 
 
 @dataclass
@@ -382,21 +394,37 @@ class _Parser:
         node = self.pipeline()
         if self.peek().kind == "name" and self.peek().text == "if":
             self.next()
-            test = self.comparison()
+            test = self.logic_or()
             self.expect("name", "else")
             return Cond(node, test, self.expr(), line)
         return node
 
     def pipeline(self) -> Any:
-        src = self.additive()
+        # The operands of `->` are conditions or arithmetic (parser.rs:333-352);
+        # a condition lowers only where one is decided (`a if test else b`).
+        src = self.logic_or()
         stages = []
         while self.accept("op", "->"):
             line = self.peek().line
-            stage = self.additive()
+            stage = self.logic_or()
             if not _has_stage(stage):
                 raise TysorSyntaxError(f"line {line}: a pipeline stage must be a call")
             stages.append(stage)
         return Pipe(src, stages) if stages else src
+
+    # A condition: `||` over `&&` over one comparison, left-associative (the
+    # reference's precedence, compiler/parser.rs:351-361).
+    def logic_or(self) -> Any:
+        node = self.logic_and()
+        while self.accept("op", "||"):
+            node = Logic("||", node, self.logic_and())
+        return node
+
+    def logic_and(self) -> Any:
+        node = self.comparison()
+        while self.accept("op", "&&"):
+            node = Logic("&&", node, self.comparison())
+        return node
 
     def comparison(self) -> Any:
         node = self.additive()
@@ -429,6 +457,8 @@ class _Parser:
             # (compiler/frontend_ir.rs:606-615, parser.rs:402-409).
             self.next()
             return BinOp("-", Lit(0), self.unary())
+        if self.accept("op", "!"):
+            return Not(self.unary())
         return self.postfix()
 
     def postfix(self) -> Any:
@@ -557,6 +587,15 @@ class _Lowerer:
                    "==": lambda: l == r, "!=": lambda: l != r, "<": lambda: l < r, ">": lambda: l > r,
                    "<=": lambda: l <= r, ">=": lambda: l >= r}
             return True, ops[node.op]()
+        if isinstance(node, Not):
+            ok, v = self.const_value(node.operand)
+            return (True, not v) if ok and not isinstance(v, str) and v is not None else (False, None)
+        if isinstance(node, Logic):
+            ok1, l = self.const_value(node.lhs)
+            ok2, r = self.const_value(node.rhs)
+            if not (ok1 and ok2) or any(isinstance(x, str) or x is None for x in (l, r)):
+                return False, None
+            return True, (bool(l) and bool(r)) if node.op == "&&" else (bool(l) or bool(r))
         return False, None
 
     def literal(self, node: Any) -> Any:
@@ -569,10 +608,16 @@ class _Lowerer:
 
     def test(self, node: Any, line: int) -> bool:
         """The condition of `a if test else b`, decided while lowering: a
-        compile-time value, or the name of a graph input (true when the
-        caller supplies it)."""
+        compile-time value, the name of a graph input (true when the caller
+        supplies it), or `!`, `&&` and `||` of those."""
         if isinstance(node, Name) and node.id in self.env and not isinstance(self.env[node.id], Const):
             return self.env[node.id] is not _ABSENT
+        if isinstance(node, Not):
+            return not self.test(node.operand, line)
+        if isinstance(node, Logic):
+            # Both sides are decided (nothing is evaluated at run time).
+            l, r = self.test(node.lhs, line), self.test(node.rhs, line)
+            return (l and r) if node.op == "&&" else (l or r)
         ok, v = self.const_value(node)
         if not ok:
             raise TysorSyntaxError(f"line {line}: the condition of `if ... else` must be known while lowering "
@@ -638,6 +683,9 @@ class _Lowerer:
             return self.pipe(node.src, node.stages)
         if isinstance(node, Repeat):
             raise TysorSyntaxError(f"line {node.line}: `f()[n]` repeats a pipeline stage; it needs a piped input")
+        if isinstance(node, (Compare, Logic, Not)):
+            raise TysorSyntaxError("a comparison or logical expression is a condition of `if ... else`, "
+                                   "not a graph value")
         raise TysorSyntaxError(f"cannot lower {node!r}")
 
     def pipe(self, src: Any, stages: List[Any]) -> Ref:
