@@ -337,3 +337,16 @@ layer model(x: tensor, target=None): (tensor, tensor):
     assert len(bare.outputs) == 1 and not any(n.kind == "binary" for n in bare.nodes)
     with pytest.raises(TysorSyntaxError, match="must be known while lowering"):
         lower("layer model(x: tensor): tensor:\n  return x if x > 1 && true else x\n")
+
+
+def test_type_annotations_with_dims_and_typed_assignments():
+    """`tensor[dtype, dims...]` keeps its dtype whatever the dims hold
+    (brackets included), and `name : type = value` assigns the value."""
+    annotated = lower("layer model(x: tensor[float16, Dims[:2]], w: tensor[float16]): tensor[float16, Dims[:2]]:\n"
+                      "  k : int32 = 2\n  y : tensor[float16, Dims[:2]] = scale(x, k)\n  return y + w\n")
+    plain = lower("layer model(x: tensor[float16], w: tensor[float16]): tensor[float16]:\n"
+                  "  k = 2\n  y = scale(x, k)\n  return y + w\n")
+    assert structure(annotated) == structure(plain)
+    assert [(v.name, v.dtype) for v in annotated.values if v.is_parameter] == [("x", "float16"), ("w", "float16")]
+    with pytest.raises(TysorSyntaxError, match="unclosed"):
+        lower("layer model(x: tensor[float16, Dims[:2]): tensor:\n  return x\n")

@@ -304,9 +304,20 @@ class _Parser:
         name = self.expect("name").text
         dtype = ""
         if self.accept("op", "["):
-            parts = []
-            while not self.accept("op", "]"):
-                parts.append(self.next().text)
+            # tensor[dtype, dims...]: the dtype is the first item; the dims
+            # (which may hold brackets, `TransformerDims[:2]`) are skipped.
+            parts, depth = [], 1
+            while True:
+                tok = self.next()
+                if tok.kind in ("eof", "nl"):
+                    raise TysorSyntaxError(f"line {tok.line}: unclosed '[' in a type")
+                if tok.kind == "op" and tok.text == "[":
+                    depth += 1
+                elif tok.kind == "op" and tok.text == "]":
+                    depth -= 1
+                    if depth == 0:
+                        break
+                parts.append(tok.text)
             dtype = parts[0] if parts and parts[0] not in (",",) else ""
         return name, dtype
 
@@ -347,6 +358,13 @@ class _Parser:
             elif tok.kind == "name" and self.peek(1).kind == "op" and self.peek(1).text == "=":
                 self.next()
                 self.next()
+                body.append(("assign", tok.text, self.expr(), tok.line))
+            elif tok.kind == "name" and self.peek(1).kind == "op" and self.peek(1).text == ":":
+                # `name : type = value`: the annotation is not checked here.
+                self.next()
+                self.next()
+                self.type_ref()
+                self.expect("op", "=")
                 body.append(("assign", tok.text, self.expr(), tok.line))
             else:
                 raise TysorSyntaxError(f"line {tok.line}: expected an assignment or return")
