@@ -350,3 +350,25 @@ def test_type_annotations_with_dims_and_typed_assignments():
     assert [(v.name, v.dtype) for v in annotated.values if v.is_parameter] == [("x", "float16"), ("w", "float16")]
     with pytest.raises(TysorSyntaxError, match="unclosed"):
         lower("layer model(x: tensor[float16, Dims[:2]): tensor:\n  return x\n")
+
+
+def test_train_block_variants_and_field_rules():
+    """Tuple-valued train fields make one run per element with scalars
+    broadcast; the executor trains the first run (training/executor.rs:132-138).
+    A bare name is its own value (`optimizer = sgd`), `learning_rate` is `lr`,
+    and the reference's declaration checks hold (semantic_analyzer.rs:808-850)."""
+    base = "layer model(x: tensor): tensor:\n  return relu(x)\n\ntrain model:\n"
+    g = lower(base + "  optimizer = (sgd, adam)\n  lr = (1e-4, 5e-4)\n  objective = x\n  iteration = 5\n")
+    assert (g.optimizer, g.lr, g.iterations, g.objective) == ("sgd", 1e-4, 5, "x")
+    g = lower(base + "  optimizer = sgd\n  learning_rate = 2\n  iteration = 3\n  objective = x\n"
+                     "  scheduler = cosine(warmup: 100)\n")
+    assert (g.optimizer, g.lr, g.iterations) == ("sgd", 2.0, 3)
+    g = lower(base + "  lr = 1e-3, 2e-3\n  iteration = 2.0\n")
+    assert (g.optimizer, g.lr, g.iterations) == ("sgd", 1e-3, 1)  # a float iteration count is not an int
+    for body, msg in [("  lr = 1e-4, 5e-4, 1e-3\n  iteration = (2, 3)\n", "must have the same length"),
+                      ("  lr = ()\n", "cannot use an empty tuple"),
+                      ("  subtrain = 1\n", "'subtrain' is no longer supported"),
+                      ("  lr = 1\n  lr = 2\n", "Duplicate field 'lr'"),
+                      ("  epochs = (1, 2)\n", "'epochs' does not support tuple variants")]:
+        with pytest.raises(TysorSyntaxError, match=msg):
+            lower(base + body)

@@ -14,8 +14,10 @@ Accepted (src/compiler/parser.rs, frontend_ir.rs, ir/builder.rs):
     repeated (`f()[n]`: n applications, n known while lowering) or be
     expressions over calls (`x -> relu()[2] * 2`: the calls take the piped
     value, frontend_ir.rs:730-786);
-  * `train NAME:` blocks of `key = value` lines (optimizer, lr,
-    iteration, objective; other keys are kept and ignored);
+  * `train NAME:` blocks of `key = value` lines (optimizer, lr or
+    learning_rate, iteration, objective; other keys are kept and ignored);
+    a tuple value makes one run per element, of which the executor trains
+    the first (frontend_ir.rs:1108-1125, training/executor.rs:132-138);
   * `#` comments, blank lines, lines starting with `->` (they continue the
     pipeline above), `config NAME:` blocks (`field : type = value`), whose
     fields are read as `NAME.field`.
@@ -240,6 +242,11 @@ class TrainRun:
     settings: Dict[str, Any]
 
 
+# Train fields that may hold a tuple of per-run values (one run per
+# element, scalars broadcast: frontend_ir.rs:1037-1068, 1108-1125).
+TRAIN_VARIANT_FIELDS = ("backend", "target", "device", "optimizer", "lr", "learning_rate", "objective", "iteration")
+
+
 @dataclass
 class Module:
     functions: Dict[str, Function]
@@ -377,13 +384,38 @@ class _Parser:
         self.expect("nl")
         self.expect("indent")
         settings: Dict[str, Any] = {}
+        arity: Optional[int] = None
         while not self.accept("dedent"):
             if self.accept("nl"):
                 continue
-            key = self.expect("name").text
+            tok = self.expect("name")
+            key = tok.text
             self.expect("op", "=")
-            settings[key] = self.expr()
+            value = self.expr()
+            if self.peek().kind == "op" and self.peek().text == ",":
+                items = [value]
+                while self.accept("op", ","):
+                    items.append(self.expr())
+                value = TupleExpr(items)
             self.expect("nl")
+            # The reference's checks of a train declaration
+            # (semantic_analyzer.rs:808-850, frontend_ir.rs:1069-1081).
+            if key in settings:
+                raise TysorSyntaxError(f"line {tok.line}: Duplicate field '{key}' in train '{model}'")
+            if key == "subtrain":
+                raise TysorSyntaxError(f"line {tok.line}: Field 'subtrain' is no longer supported; use "
+                                       "tuple-valued fields on 'train model' instead")
+            if isinstance(value, TupleExpr):
+                if key not in TRAIN_VARIANT_FIELDS:
+                    raise TysorSyntaxError(f"line {tok.line}: Train field '{key}' does not support tuple "
+                                           "variants; use a scalar value")
+                if not value.items:
+                    raise TysorSyntaxError(f"line {tok.line}: Train field '{key}' cannot use an empty tuple")
+                if arity is not None and arity != len(value.items):
+                    raise TysorSyntaxError(f"line {tok.line}: Tuple-valued train fields must have the same "
+                                           "length; use scalar values to broadcast")
+                arity = len(value.items)
+            settings[key] = value
         return TrainRun(model, settings)
 
     def config(self) -> Tuple[str, Dict[str, Any]]:
@@ -525,7 +557,18 @@ class _Parser:
                 return Lit(None)
             return Name(tok.text, tok.line)
         if tok.kind == "op" and tok.text == "(":
+            if self.accept("op", ")"):
+                return TupleExpr([])
             node = self.expr()
+            if self.peek().kind == "op" and self.peek().text == ",":
+                # (a, b, ...): a tuple, as the reference parses a bracketed
+                # expression list (parser.rs:299-311).
+                items = [node]
+                while self.accept("op", ","):
+                    if self.peek().kind == "op" and self.peek().text == ")":
+                        break
+                    items.append(self.expr())
+                node = TupleExpr(items)
             self.expect("op", ")")
             return node
         raise TysorSyntaxError(f"line {tok.line}: unexpected {tok.text or tok.kind!r}")
@@ -555,6 +598,13 @@ class Const:
 
 
 _ABSENT = object()  # a name bound to `None`: no graph value
+
+
+@dataclass
+class _TrainName:
+    """A bare name as a train field's value (`optimizer = sgd`,
+    `objective = loss`)."""
+    name: str
 
 
 class _Lowerer:
@@ -871,14 +921,36 @@ class _Lowerer:
             if r is not _ABSENT:
                 self.b.ret(r)
         if train is not None:
-            s = train.settings
-            obj = s.get("objective")
-            lr = self.literal(s["lr"]) if "lr" in s else 0.01
-            it = self.literal(s["iteration"]) if "iteration" in s else 1
-            opt = self.literal(s["optimizer"]) if "optimizer" in s else "sgd"
-            self.b.train(objective=obj.id if isinstance(obj, Name) else None, lr=float(lr),
-                         iterations=int(it), optimizer=str(opt))
+            # The executor trains the first run of the block
+            # (training/executor.rs:132-138, 774-790): each field's first
+            # tuple element; lr an int or float (else 0.01), iteration an
+            # int (else 1), optimizer a name or string (else "sgd").
+            fields: Dict[str, Any] = {}
+            for key, node in train.settings.items():
+                key = "lr" if key == "learning_rate" else key
+                if key in ("objective", "lr", "iteration", "optimizer"):  # the others are not read
+                    fields[key] = self.train_value(node.items[0] if isinstance(node, TupleExpr) else node)
+            obj, lr, it, opt = (fields.get(k) for k in ("objective", "lr", "iteration", "optimizer"))
+            if isinstance(opt, _TrainName):
+                opt = opt.name
+            is_int = lambda v: isinstance(v, int) and not isinstance(v, bool)
+            self.b.train(objective=obj.name if isinstance(obj, _TrainName) else None,
+                         lr=float(lr) if is_int(lr) or isinstance(lr, float) else 0.01,
+                         iterations=it if is_int(it) else 1,
+                         optimizer=opt if isinstance(opt, str) else "sgd")
         return self.b.build()
+
+    def train_value(self, node: Any) -> Any:
+        """A train field's value: a bare name stands for itself (the
+        reference evaluates an identifier to its name,
+        frontend_ir.rs:1170-1176), anything else must be known while
+        lowering."""
+        if isinstance(node, Name):
+            return _TrainName(node.id)
+        ok, v = self.const_value(node)
+        if not ok:
+            raise TysorSyntaxError("a train field's value must be a name or known while lowering")
+        return v
 
 
 def lower(src: str, entry: str = "model", inputs: Optional[List[str]] = None) -> Graph:
