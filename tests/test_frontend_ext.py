@@ -372,3 +372,15 @@ def test_train_block_variants_and_field_rules():
                       ("  epochs = (1, 2)\n", "'epochs' does not support tuple variants")]:
         with pytest.raises(TysorSyntaxError, match=msg):
             lower(base + body)
+
+
+def test_train_objective_must_name_a_model_symbol():
+    """The objective is a bare name among `layer model`'s parameters,
+    assigned names and mentioned names (semantic_analyzer.rs:850-893)."""
+    model = "layer model(x: tensor, t: tensor): tensor:\n  y = relu(x)\n  loss = cross_entropy(y, t)\n  return loss\n"
+    assert lower(model + "\ntrain model:\n  objective = loss\n").objective == "loss"
+    assert lower(model + "\ntrain model:\n  objective = (loss, y)\n").objective == "loss"
+    for obj, msg in [('"loss"', "must reference a named tensor root"), ("relu(x)", "must reference a named"),
+                     ("missing", "unknown model root 'missing'")]:
+        with pytest.raises(TysorSyntaxError, match=msg):
+            lower(model + f"\ntrain model:\n  objective = {obj}\n")

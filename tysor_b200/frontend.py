@@ -584,8 +584,64 @@ def _has_stage(node: Any) -> bool:
     return False
 
 
+def _identifiers(node: Any, out: set) -> None:
+    """The names an expression mentions, callees excluded (the reference's
+    collect_expr_identifiers, semantic_analyzer.rs:1090-1129)."""
+    if isinstance(node, Name):
+        out.add(node.id)
+    elif isinstance(node, Attr):
+        out.update((node.base, node.attr))
+    elif isinstance(node, Call):
+        for a in node.args:
+            _identifiers(a, out)
+    elif isinstance(node, (BinOp, Compare, Logic)):
+        _identifiers(node.lhs, out)
+        _identifiers(node.rhs, out)
+    elif isinstance(node, Not):
+        _identifiers(node.operand, out)
+    elif isinstance(node, Cond):
+        for part in (node.then, node.test, node.other):
+            _identifiers(part, out)
+    elif isinstance(node, TupleExpr):
+        for item in node.items:
+            _identifiers(item, out)
+    elif isinstance(node, Pipe):
+        for part in [node.src] + list(node.stages):
+            _identifiers(part, out)
+    elif isinstance(node, Repeat):
+        _identifiers(node.call, out)
+        _identifiers(node.count, out)
+
+
+def _check_objectives(mod: Module) -> None:
+    """A train block's objective is a bare name and, when the program has a
+    `layer model`, one of the symbols of that layer: its parameters, the
+    names it assigns and the names its expressions mention
+    (semantic_analyzer.rs:850-875, 880-893)."""
+    model = mod.functions.get("model")
+    symbols: set = set()
+    if model is not None and model.is_layer:
+        symbols.update(p.name for p in model.params)
+        for kind, name, value, _ in model.body:
+            if kind == "assign":
+                symbols.add(name)
+            _identifiers(value, symbols)
+    for tr in mod.trains.values():
+        obj = tr.settings.get("objective")
+        if obj is None:
+            continue
+        for item in (obj.items if isinstance(obj, TupleExpr) else [obj]):
+            if not isinstance(item, Name):
+                raise TysorSyntaxError("Field 'objective' must reference a named tensor root, not a string "
+                                       "literal or arbitrary expression")
+            if symbols and item.id not in symbols:
+                raise TysorSyntaxError(f"Field 'objective' references unknown model root '{item.id}'")
+
+
 def parse(src: str) -> Module:
-    return _Parser(tokenize(src)).module()
+    mod = _Parser(tokenize(src)).module()
+    _check_objectives(mod)
+    return mod
 
 
 # ---- lowering ------------------------------------------------------------------
