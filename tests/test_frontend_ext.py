@@ -384,3 +384,20 @@ def test_train_objective_must_name_a_model_symbol():
                      ("missing", "unknown model root 'missing'")]:
         with pytest.raises(TysorSyntaxError, match=msg):
             lower(model + f"\ntrain model:\n  objective = {obj}\n")
+
+
+def test_train_run_needs_layer_model_and_train_model():
+    """A train run exists only for `layer model` with a `train model:` block
+    (frontend_ir.rs:458-465); --train without one is an error
+    (training/executor.rs:132-138)."""
+    layer = "layer model(x: tensor): tensor:\n  return relu(x)\n"
+    block = "\ntrain model:\n  lr = 0.5\n  iteration = 2\n"
+    assert lower(layer + block).train_run and lower(layer + block).lr == 0.5
+    assert not lower(layer).train_run
+    other = "layer other(x: tensor): tensor:\n  return relu(x)\n\ntrain other:\n  lr = 0.5\n"
+    assert not lower(other, entry="other").train_run
+    as_fn = "fn model(x: tensor): tensor:\n  return relu(x)\n" + block
+    assert not lower(as_fn).train_run
+    for name in ("llama_block.ty", "llama_lm.ty"):  # their usage lines run --train
+        with open(os.path.join(ROOT, "examples", name)) as fh:
+            assert lower(fh.read()).train_run, name

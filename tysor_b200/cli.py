@@ -108,6 +108,9 @@ def main(argv: Optional[List[str]] = None) -> int:
             if opts["backward"]:
                 backward_cuda_module(ctx, graph, opts["shapes"])
             if opts["train"]:
+                if not graph.train_run:
+                    # training/executor.rs:132-138: --train needs the `train model` run.
+                    raise ValueError("Train executor requires a resolved 'train model' execution run")
                 train_cuda_module(ctx, graph, opts["shapes"])
     except (NativeError, ValueError) as e:
         print(str(e), file=sys.stderr)

@@ -1011,8 +1011,9 @@ class _Lowerer:
 
 def lower(src: str, entry: str = "model", inputs: Optional[List[str]] = None) -> Graph:
     """The lowered graph of function `entry` of a `.ty` program, with the
-    program's `train entry:` settings (objective, lr, iterations, optimizer)
-    when it has them.  `inputs`: the graph inputs the caller supplies (the
+    settings of the program's `train model:` block (objective, lr,
+    iterations, optimizer) when the entry is `layer model` and the block
+    exists (else Graph.train_run is false).  `inputs`: the graph inputs the caller supplies (the
     CLI's `--shape` names); an entry parameter whose default is `None` and
     that is not among them has no graph value (`x if targets else y` then
     takes y).  None: every parameter is an input."""
@@ -1020,4 +1021,9 @@ def lower(src: str, entry: str = "model", inputs: Optional[List[str]] = None) ->
     if entry not in mod.functions:
         raise TysorSyntaxError(f"Entry function '{entry}' not found in lowered module")
     provided = None if inputs is None else set(inputs)
-    return _Lowerer(mod, mod.functions[entry], provided).lower(mod.trains.get(entry))
+    fn = mod.functions[entry]
+    # The reference plans train runs only for `layer model` with `train
+    # model`, and its executor trains the run of the entry
+    # (frontend_ir.rs:458-465, training/executor.rs:132-138).
+    train = mod.trains.get("model") if entry == "model" and fn.is_layer else None
+    return _Lowerer(mod, fn, provided).lower(train)

@@ -70,6 +70,9 @@ class Graph:
     lr: float = 0.01
     iterations: int = 1
     optimizer: str = "sgd"
+    # Whether a train run was declared for this graph (set by
+    # GraphBuilder.train): the reference's --train needs one.
+    train_run: bool = False
 
     # -- queries ---------------------------------------------------------
     def parameters(self) -> List[Value]:
@@ -238,6 +241,7 @@ class GraphBuilder:
         self.g.lr = lr
         self.g.iterations = iterations
         self.g.optimizer = optimizer
+        self.g.train_run = True
 
     def build(self) -> Graph:
         return self.g
